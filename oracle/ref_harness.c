@@ -1,0 +1,80 @@
+/*
+ * Reference harness (TEST INFRASTRUCTURE ONLY).
+ *
+ * Builds the reference's own sampler, unmodified, into oracle/_ref/ so the
+ * C restatement in sampler_oracle.c (and through it the CUDA path) can be
+ * pinned against it.  The reference's src/model.c is compiled as part of this
+ * translation unit, taken from where it lies in the reference tree (the
+ * include path is set by oracle/Makefile); nothing from it is copied into this
+ * repository.  rng_float is redirected to a function that returns the uniform
+ * supplied by the caller and counts the calls, which is the only change to
+ * the reference's code path.
+ *
+ * The penalty block is inline in model_forward_step (src/model.c:1268-1305),
+ * which needs a loaded model, so bm_ref_sample_row restates those few lines
+ * (same bitset dedup, protected ids and in-place update) before calling the
+ * reference's static sample_advanced (src/model.c:135-361).
+ */
+#define rng_float bm_ref_harness_uniform
+#include "model.c"
+#undef rng_float
+
+static __thread float g_uniform;
+static __thread int g_calls;
+
+float bm_ref_harness_uniform(void)
+{
+    g_calls++;
+    return g_uniform;
+}
+
+/* Returns the sampled id; *consumed = number of rng_float() calls (0 or 1);
+ * *prob = value stored for that id in the reference's probs array (1.0 for
+ * greedy and argmax-guard rows).  `logits` is modified in place, as the
+ * reference does.  `probs` must hold V entries, `visited` (V+63)/64 words. */
+int bm_ref_sample_row(float *logits, int V, const int *history,
+                      int history_len, float penalty, float temp, float min_p,
+                      float top_p, int top_k, float u, int *consumed,
+                      float *prob, token_prob_t *probs, uint64_t *visited)
+{
+    static const int prot[4] = {TOKEN_EOS, TOKEN_NL, TOKEN_NLNL, TOKEN_PERIOD};
+    memset(visited, 0, (((size_t) V + 63) / 64) * sizeof(uint64_t));
+    for (int i = 0; i < history_len; i++) {
+        int id = history[i];
+        if (id < 0 || id >= V)
+            continue;
+        if (visited[id / 64] & (1ULL << (id % 64)))
+            continue;
+        visited[id / 64] |= (1ULL << (id % 64));
+        int is_prot = 0;
+        for (int p = 0; p < 4; p++)
+            if (prot[p] == id)
+                is_prot = 1;
+        if (!is_prot && penalty > 0.0f) {
+            if (logits[id] > 0)
+                logits[id] /= penalty;
+            else
+                logits[id] *= penalty;
+        }
+    }
+    for (int i = 0; i < V; i++)
+        probs[i].id = -1;
+    g_uniform = u;
+    g_calls = 0;
+    int t = sample_advanced(logits, V, temp, min_p, top_p, top_k, probs);
+    *consumed = g_calls;
+    *prob = 1.0f;
+    if (g_calls) {
+        for (int i = 0; i < V; i++)
+            if (probs[i].id == t) {
+                *prob = probs[i].val;
+                break;
+            }
+    }
+    return t;
+}
+
+int bm_ref_sizeof_token_prob(void)
+{
+    return (int) sizeof(token_prob_t);
+}
