@@ -1,0 +1,45 @@
+// Internal interface between the C ABI (bm_sampler.cu) and the sampling
+// kernel (bm_kernel.cu).  Not part of the public ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "bm_sampler.h"
+
+namespace bmk {
+
+constexpr int NT = 1024;      // threads per CTA (one CTA per SM)
+constexpr int NW = NT / 32;   // warps per CTA
+constexpr int HB = 128;       // reference histogram buckets (src/model.c:132)
+constexpr int NB = 2048;      // full-vocabulary path: logit buckets
+constexpr int WCAP = 1024;    // full-vocabulary path: window list capacity
+constexpr int KCAP = 2048;    // top_k path: candidate list capacity
+constexpr int NCHUNK = 8;     // bulk-copy chunks (one mbarrier each) per row
+constexpr int SCRATCH = 20480;
+
+struct Params {
+    const float *logits;
+    int64_t ld;
+    int B, V;
+    const int32_t *hist;
+    const int64_t *hist_off;
+    const bm_knobs_t *knobs;
+    int64_t knob_stride;
+    const float *uniform;
+    int32_t *out_id;
+    float *out_prob;
+    bm_row_stats_t *stats;
+    int *err;  // device error word: bit 0 = bounded wait expired
+};
+
+// Dynamic shared memory the kernel needs for vocabulary V.
+size_t smem_bytes(int V);
+// Largest V whose row buffer fits in `smem_limit` bytes of shared memory.
+int max_vocab(size_t smem_limit);
+// Launch on `grid` CTAs (one per SM is the intended shape).
+cudaError_t launch(const Params &p, int grid, cudaStream_t s);
+// One-time per-device attribute setup (dynamic shared memory opt-in).
+cudaError_t prepare(int V);
+
+}  // namespace bmk

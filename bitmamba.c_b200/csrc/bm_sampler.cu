@@ -1,0 +1,384 @@
+// C ABI of the B200 sampler: contexts, argument checks, host-buffer staging,
+// the reference RNG and the reference-convention single-row / row-sequence
+// calls.  All sampling goes through the CUDA kernel in bm_kernel.cu; there is
+// no host fallback.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "bm_kernel.cuh"
+#include "bm_sampler.h"
+
+struct bm_ctx {
+    int device;
+    int sms;
+    size_t smem_optin;
+    int max_vocab;
+    cudaStream_t stream;
+    int *d_err;
+    // staging for the host-buffer entry points (grown on demand)
+    float *d_logits;
+    size_t cap_logits;
+    int32_t *d_hist;
+    size_t cap_hist;
+    int64_t *d_off;
+    size_t cap_off;
+    bm_knobs_t *d_knobs;
+    size_t cap_knobs;
+    float *d_u;
+    int32_t *d_id;
+    float *d_prob;
+    bm_row_stats_t *d_stats;
+    size_t cap_rows;
+};
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    int code = (e == cudaErrorMemoryAllocation) ? BM_ERR_OOM : BM_ERR_CUDA;
+    return fail(code, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call)                                             \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+    } while (0)
+
+template <class T>
+int grow(T **p, size_t *cap, size_t need) {
+    if (need <= *cap) return BM_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    size_t n = need + need / 4 + 16;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), n * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+    *cap = n;
+    return BM_OK;
+}
+
+int check_batch_args(const bm_ctx_t *ctx, const void *logits, int B, int V, int64_t ld,
+                     const void *hist, const void *off, const void *knobs,
+                     int64_t knob_stride, const void *uniform, const void *out_id) {
+    if (!ctx) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    if (B < 0) return fail(BM_ERR_INVALID_ARG, "B = %d < 0", B);
+    if (B == 0) return BM_OK;
+    if (V < 1) return fail(BM_ERR_INVALID_ARG, "V = %d < 1", V);
+    if (V > ctx->max_vocab)
+        return fail(BM_ERR_UNSUPPORTED, "V = %d exceeds the row buffer limit %d", V,
+                    ctx->max_vocab);
+    if (ld < V) return fail(BM_ERR_INVALID_ARG, "ld = %lld < V = %d", (long long)ld, V);
+    if (!logits || !knobs || !out_id)
+        return fail(BM_ERR_INVALID_ARG, "logits, knobs and out_id must be non-NULL");
+    if (!uniform) return fail(BM_ERR_INVALID_ARG, "uniform must be non-NULL");
+    if ((hist == nullptr) != (off == nullptr))
+        return fail(BM_ERR_INVALID_ARG, "hist and hist_off must both be NULL or both set");
+    if (knob_stride != 0 && knob_stride != 1)
+        return fail(BM_ERR_INVALID_ARG, "knob_stride must be 0 or 1");
+    if (reinterpret_cast<uintptr_t>(logits) % 4)
+        return fail(BM_ERR_INVALID_ARG, "logits not 4-byte aligned");
+    return BM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *bm_last_error(void) { return g_err; }
+int bm_abi_version(void) { return BM_SAMPLER_ABI_VERSION; }
+
+int bm_knobs_init(bm_knobs_t *k, float temp, float penalty, float min_p, float top_p,
+                  int top_k) {
+    if (!k) return fail(BM_ERR_INVALID_ARG, "knobs is NULL");
+    k->temp = temp;
+    k->penalty = penalty;
+    k->min_p = min_p;
+    k->top_p = top_p;
+    k->top_k = top_k;
+    // IEEE division and the host libm's logf, as src/model.c:157 and :173
+    volatile float one = 1.0f;
+    k->inv_temp = one / temp;
+    k->log_min_p = (min_p > 0.0f && min_p < 1.0f) ? logf(min_p) : 0.0f;
+    k->flags = 0;
+    return BM_OK;
+}
+
+int bm_ctx_create(int device, bm_ctx_t **out) {
+    if (!out) return fail(BM_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0)
+        return fail(BM_ERR_NO_DEVICE, "no CUDA device (%s)",
+                    e == cudaSuccess ? "count 0" : cudaGetErrorString(e));
+    if (device < 0 || device >= n)
+        return fail(BM_ERR_NO_DEVICE, "device %d out of range (%d devices)", device, n);
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(BM_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    CK(cudaSetDevice(device));
+    bm_ctx_t *c = static_cast<bm_ctx_t *>(calloc(1, sizeof(bm_ctx_t)));
+    if (!c) return fail(BM_ERR_OOM, "host allocation failed");
+    c->device = device;
+    c->sms = prop.multiProcessorCount;
+    c->smem_optin = prop.sharedMemPerBlockOptin;
+    c->max_vocab = bmk::max_vocab(c->smem_optin);
+    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    if (e == cudaSuccess) e = bmk::prepare(c->max_vocab);
+    if (e != cudaSuccess) {
+        int rc = cuda_fail(e, "context setup");
+        bm_ctx_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return BM_OK;
+}
+
+void bm_ctx_destroy(bm_ctx_t *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    cudaFree(c->d_err);
+    cudaFree(c->d_logits);
+    cudaFree(c->d_hist);
+    cudaFree(c->d_off);
+    cudaFree(c->d_knobs);
+    cudaFree(c->d_u);
+    cudaFree(c->d_id);
+    cudaFree(c->d_prob);
+    cudaFree(c->d_stats);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    free(c);
+}
+
+int bm_max_vocab(const bm_ctx_t *c) { return c ? c->max_vocab : 0; }
+
+int bm_ctx_check(bm_ctx_t *c) {
+    if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    int h = 0;
+    CK(cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) {
+        CK(cudaMemset(c->d_err, 0, sizeof(int)));
+        return fail(BM_ERR_DEVICE, "device error flag 0x%x (bounded wait expired or select "
+                                   "did not converge)", h);
+    }
+    return BM_OK;
+}
+
+int bm_sample_batch(bm_ctx_t *c, const float *d_logits, int B, int V, int64_t ld,
+                    const int32_t *d_hist, const int64_t *d_hist_off,
+                    const bm_knobs_t *d_knobs, int64_t knob_stride, const float *d_uniform,
+                    int32_t *d_out_id, float *d_out_prob, bm_row_stats_t *d_stats,
+                    void *stream) {
+    int rc = check_batch_args(c, d_logits, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
+                              d_uniform, d_out_id);
+    if (rc != BM_OK || B == 0) return rc;
+    CK(cudaSetDevice(c->device));
+    bmk::Params p;
+    p.logits = d_logits;
+    p.ld = ld;
+    p.B = B;
+    p.V = V;
+    p.hist = d_hist;
+    p.hist_off = d_hist_off;
+    p.knobs = d_knobs;
+    p.knob_stride = knob_stride;
+    p.uniform = d_uniform;
+    p.out_id = d_out_id;
+    p.out_prob = d_out_prob;
+    p.stats = d_stats;
+    p.err = c->d_err;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    int grid = B < c->sms ? B : c->sms;
+    CK(bmk::launch(p, grid, s));
+    return BM_OK;
+}
+
+int bm_sample_batch_host(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t ld,
+                         const int32_t *h_hist, const int64_t *h_hist_off,
+                         const bm_knobs_t *h_knobs, int64_t knob_stride,
+                         const float *h_uniform, int32_t *h_out_id, float *h_out_prob,
+                         bm_row_stats_t *h_stats) {
+    int rc = check_batch_args(c, h_logits, B, V, ld, h_hist, h_hist_off, h_knobs, knob_stride,
+                              h_uniform, h_out_id);
+    if (rc != BM_OK || B == 0) return rc;
+    CK(cudaSetDevice(c->device));
+    cudaStream_t s = c->stream;
+    const size_t rows = (size_t)B;
+    if ((rc = grow(&c->d_logits, &c->cap_logits, rows * (size_t)ld)) != BM_OK) return rc;
+    if (rows > c->cap_rows) {
+        // the four per-row buffers share one capacity
+        cudaFree(c->d_u); cudaFree(c->d_id); cudaFree(c->d_prob); cudaFree(c->d_stats);
+        c->d_u = nullptr; c->d_id = nullptr; c->d_prob = nullptr; c->d_stats = nullptr;
+        c->cap_rows = 0;
+        size_t t0 = 0, t1 = 0, t2 = 0, t3 = 0;
+        if ((rc = grow(&c->d_u, &t0, rows)) != BM_OK) return rc;
+        if ((rc = grow(&c->d_id, &t1, rows)) != BM_OK) return rc;
+        if ((rc = grow(&c->d_prob, &t2, rows)) != BM_OK) return rc;
+        if ((rc = grow(&c->d_stats, &t3, rows)) != BM_OK) return rc;
+        c->cap_rows = t0;
+    }
+    const size_t nk = knob_stride ? rows : 1;
+    if ((rc = grow(&c->d_knobs, &c->cap_knobs, nk)) != BM_OK) return rc;
+    CK(cudaMemcpyAsync(c->d_logits, h_logits, rows * (size_t)ld * sizeof(float),
+                       cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(c->d_knobs, h_knobs, nk * sizeof(bm_knobs_t), cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(c->d_u, h_uniform, rows * sizeof(float), cudaMemcpyHostToDevice, s));
+    const int32_t *dh = nullptr;
+    const int64_t *doff = nullptr;
+    if (h_hist) {
+        const int64_t h0 = h_hist_off[0], h1 = h_hist_off[B];
+        if (h0 < 0 || h1 < h0) return fail(BM_ERR_INVALID_ARG, "hist_off not monotone");
+        if ((rc = grow(&c->d_off, &c->cap_off, rows + 1)) != BM_OK) return rc;
+        if ((rc = grow(&c->d_hist, &c->cap_hist, (size_t)(h1 > 0 ? h1 : 1))) != BM_OK) return rc;
+        if (h1 > 0)
+            CK(cudaMemcpyAsync(c->d_hist, h_hist, (size_t)h1 * sizeof(int32_t),
+                               cudaMemcpyHostToDevice, s));
+        CK(cudaMemcpyAsync(c->d_off, h_hist_off, (rows + 1) * sizeof(int64_t),
+                           cudaMemcpyHostToDevice, s));
+        dh = c->d_hist;
+        doff = c->d_off;
+    }
+    rc = bm_sample_batch(c, c->d_logits, B, V, ld, dh, doff, c->d_knobs, knob_stride, c->d_u,
+                         c->d_id, h_out_prob ? c->d_prob : nullptr,
+                         h_stats ? c->d_stats : nullptr, s);
+    if (rc != BM_OK) return rc;
+    CK(cudaMemcpyAsync(h_out_id, c->d_id, rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    if (h_out_prob)
+        CK(cudaMemcpyAsync(h_out_prob, c->d_prob, rows * sizeof(float), cudaMemcpyDeviceToHost,
+                           s));
+    if (h_stats)
+        CK(cudaMemcpyAsync(h_stats, c->d_stats, rows * sizeof(bm_row_stats_t),
+                           cudaMemcpyDeviceToHost, s));
+    return bm_ctx_check(c);
+}
+
+// ---- reference RNG (src/utils.c:117-140) ---------------------------------
+static uint64_t g_rng = 0x853c49e6748fea9bULL;
+
+void bm_rng_seed(uint64_t seed) { g_rng = seed ? seed : 0x853c49e6748fea9bULL; }
+
+uint64_t bm_rng_next(void) {
+    uint64_t x = g_rng;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    g_rng = x;
+    return x * 0x2545F4914F6CDD1DULL;
+}
+
+float bm_rng_float(void) {
+    return (float)(bm_rng_next() >> 11) * (1.0f / 9007199254740992.0f);
+}
+
+uint64_t bm_rng_get_state(void) { return g_rng; }
+void bm_rng_set_state(uint64_t s) { g_rng = s; }
+
+// ---- reference calling convention ----------------------------------------
+static std::mutex g_default_mu;
+static bm_ctx_t *g_default = nullptr;
+
+static int default_ctx(bm_ctx_t **out) {
+    std::lock_guard<std::mutex> lk(g_default_mu);
+    if (!g_default) {
+        const char *s = getenv("BM_DEVICE");
+        int dev = s ? atoi(s) : 0;
+        int rc = bm_ctx_create(dev, &g_default);
+        if (rc != BM_OK) return rc;
+    }
+    *out = g_default;
+    return BM_OK;
+}
+
+int bm_sample_rows(const float *h_logits, int B, int V, int64_t ld, const int32_t *h_hist,
+                   const int64_t *h_hist_off, const bm_knobs_t *h_knobs, int64_t knob_stride,
+                   int32_t *h_out_id) {
+    if (B < 0 || !h_knobs || !h_out_id || (B > 0 && !h_logits))
+        return fail(BM_ERR_INVALID_ARG, "bad arguments to bm_sample_rows");
+    if (B == 0) return BM_OK;
+    bm_ctx_t *c;
+    int rc = default_ctx(&c);
+    if (rc != BM_OK) return rc;
+    std::vector<float> u(B);
+    std::vector<bm_row_stats_t> st(B);
+    // draw in row order for rows that will draw; greedy rows never do
+    // (src/model.c:144-154).  A row whose candidate set turns out empty
+    // (argmax guard) does not draw either; that is only known after the
+    // kernel, so the stream is re-assigned and the later rows re-run.
+    const uint64_t state0 = g_rng;
+    std::vector<char> draws(B);
+    for (int r = 0; r < B; ++r) {
+        const bm_knobs_t &k = h_knobs[knob_stride ? r : 0];
+        draws[r] = !(k.temp < 0.05f);
+        u[r] = draws[r] ? bm_rng_float() : 0.0f;
+    }
+    rc = bm_sample_batch_host(c, h_logits, B, V, ld, h_hist, h_hist_off, h_knobs, knob_stride,
+                              u.data(), h_out_id, nullptr, st.data());
+    if (rc != BM_OK) {
+        g_rng = state0;
+        return rc;
+    }
+    int first_fix = -1;
+    for (int r = 0; r < B; ++r)
+        if (draws[r] && !st[r].consumed) {
+            draws[r] = 0;
+            if (first_fix < 0) first_fix = r;
+        }
+    if (first_fix >= 0) {
+        g_rng = state0;
+        for (int r = 0; r < B; ++r) u[r] = draws[r] ? bm_rng_float() : 0.0f;
+        // rows after the first non-drawing row see shifted uniforms
+        int start = first_fix + 1;
+        if (start < B) {
+            const int32_t *hh = h_hist;
+            std::vector<int64_t> off;
+            if (h_hist) {
+                off.assign(h_hist_off + start, h_hist_off + B + 1);
+            }
+            rc = bm_sample_batch_host(c, h_logits + (size_t)start * ld, B - start, V, ld, hh,
+                                      h_hist ? off.data() : nullptr,
+                                      knob_stride ? h_knobs + start : h_knobs, knob_stride,
+                                      u.data() + start, h_out_id + start, nullptr, nullptr);
+            if (rc != BM_OK) return rc;
+        }
+    }
+    return BM_OK;
+}
+
+int bm_sample_row(float *logits, int V, const int *history, int history_len, float penalty,
+                  float temp, float min_p, float top_p, int top_k) {
+    if (!logits || V < 1 || history_len < 0 || (history_len > 0 && !history))
+        return fail(BM_ERR_INVALID_ARG, "bad arguments to bm_sample_row");
+    bm_knobs_t k;
+    bm_knobs_init(&k, temp, penalty, min_p, top_p, top_k);
+    int64_t off[2] = {0, history_len};
+    int32_t id = -1;
+    int rc = bm_sample_rows(logits, 1, V, V, history_len > 0 ? history : nullptr,
+                            history_len > 0 ? off : nullptr, &k, 0, &id);
+    return rc != BM_OK ? rc : id;
+}
+
+}  // extern "C"

@@ -1,0 +1,198 @@
+/*
+ * bm_sampler.h - C ABI of the B200 decode-step token sampler.
+ *
+ * Drop-in replacement for the sampling tail of jserv/bitmamba.c:
+ *   repetition penalty (src/model.c:1268-1305) -> sample_advanced /
+ *   filter_and_sample (src/model.c:37-361) -> rng_float (src/utils.c:117-140).
+ * The batched entry points run hand-written sm_100a CUDA kernels, one CTA per
+ * logits row.  There is no CPU fallback: every sampling entry point fails
+ * with BM_ERR_NO_DEVICE / BM_ERR_CUDA when no usable B200 is present.
+ *
+ * Semantics kept from the reference, row by row:
+ *   - penalty applied once per distinct history id in [0, V), skipping the
+ *     protected GPT-2 ids {50256, 198, 628, 13}: l > 0 ? l / penalty
+ *     : l * penalty (src/model.c:1283-1304; ids src/bitmamba.h:21-24);
+ *   - temp < 0.05 -> argmax of the penalised logits, lowest id on ties, no
+ *     uniform consumed (src/model.c:144-154);
+ *   - otherwise logits * (1/temp), min_p threshold max + logf(min_p), the
+ *     128-bucket histogram top_k path for 1 <= top_k <= 256 (heap top-k,
+ *     survivor softmax, stable descending sort when top_p < 1), or the
+ *     full-vocabulary path for other top_k (lazy id-order walk, top-256
+ *     partial sort, full sort), then the nucleus cut and the CDF walk against
+ *     r = u * (float)new_sum (src/model.c:156-360, 72-118).
+ * Token ids equal the reference's; probabilities agree to float rounding
+ * (the device expf differs from glibc's by at most 2 ulp).
+ *
+ * Thread safety: a bm_ctx_t may be used by one host thread at a time.  The
+ * reference-convention calls (bm_sample_row, bm_sample_rows) share one
+ * process-global RNG and default context, like the reference's globals
+ * (src/utils.c:119), and are not reentrant.
+ */
+#ifndef BM_SAMPLER_H
+#define BM_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BM_SAMPLER_ABI_VERSION 1
+
+/* Status codes.  Sampling entry points return >= 0 on success (a token id
+ * for the single-row calls, BM_OK for the batched calls). */
+enum {
+    BM_OK = 0,
+    BM_ERR_INVALID_ARG = -1,  /* bad pointer, size, stride or knob layout */
+    BM_ERR_CUDA = -2,         /* a CUDA runtime call failed */
+    BM_ERR_OOM = -3,          /* device or pinned-host allocation failed */
+    BM_ERR_UNSUPPORTED = -4,  /* V larger than one row buffer (bm_max_vocab) */
+    BM_ERR_NO_DEVICE = -5,    /* no CUDA device, or not an sm_100 part */
+    BM_ERR_DEVICE = -6        /* the kernel raised its error flag (a bounded
+                                 wait timed out); the context stays usable */
+};
+
+/* Per-row sampling knobs in the reference's units (src/main.c:316-321).
+ * The derived fields are filled by bm_knobs_init on the host so that
+ * 1.0f/temp is an IEEE division and logf(min_p) comes from the host libm, as
+ * in the reference (src/model.c:157, 173).  32 bytes, device-copyable. */
+typedef struct bm_knobs {
+    float temp;
+    float penalty;
+    float min_p;
+    float top_p;
+    int32_t top_k;
+    float inv_temp;  /* derived: 1.0f / temp */
+    float log_min_p; /* derived: logf(min_p) when 0 < min_p < 1, else 0 */
+    int32_t flags;   /* reserved, 0 */
+} bm_knobs_t;
+
+/* Optional per-row diagnostics written by the batched calls. */
+typedef struct bm_row_stats {
+    int32_t path;     /* 1 greedy, 2 top_k guard, 3 top_k, 4 full guard,
+                         5 lazy id-order walk, 6 top-256 partial, 7 full */
+    int32_t n_cand;   /* candidates after min_p / histogram extraction */
+    int32_t n_final;  /* size of the set the CDF walk ran over */
+    int32_t consumed; /* 1 when the reference would have drawn a uniform */
+} bm_row_stats_t;
+
+typedef struct bm_ctx bm_ctx_t;
+
+/* ---- knobs --------------------------------------------------------------- */
+
+/* Fills *k from the reference's five knobs.  Any float is accepted (NaN and
+ * infinities keep the reference's behaviour).  Returns BM_OK or
+ * BM_ERR_INVALID_ARG for k == NULL. */
+int bm_knobs_init(bm_knobs_t *k, float temp, float penalty, float min_p,
+                  float top_p, int top_k);
+
+/* ---- contexts -------------------------------------------------------------- */
+
+/* Creates a sampling context on CUDA device `device` (its stream, staging
+ * buffers, error flag).  Fails with BM_ERR_NO_DEVICE when the device is
+ * absent or is not compute capability 10.x. */
+int bm_ctx_create(int device, bm_ctx_t **out);
+void bm_ctx_destroy(bm_ctx_t *ctx);
+
+/* Largest vocabulary one row buffer holds on this device (V * 4 bytes plus
+ * scratch must fit one CTA's shared memory). */
+int bm_max_vocab(const bm_ctx_t *ctx);
+
+/* Reads and clears the device error flag (synchronises the context stream).
+ * Returns BM_OK or BM_ERR_DEVICE. */
+int bm_ctx_check(bm_ctx_t *ctx);
+
+/* ---- batched sampling, device buffers -------------------------------------- */
+
+/*
+ * Samples one token per row of a [B x V] fp32 logits matrix in device memory
+ * (row pitch ld >= V elements).  Replaces, per row, the penalty block and
+ * sample_advanced call of model_forward_step (src/model.c:1268-1307).
+ *
+ *   d_hist, d_hist_off  CSR token histories: row r owns
+ *                       d_hist[d_hist_off[r] .. d_hist_off[r+1]).
+ *                       Both NULL = no history.  Out-of-range ids are
+ *                       skipped, duplicates penalised once.
+ *   d_knobs             per-row knobs; knob_stride = 1 for one struct per
+ *                       row, 0 to apply d_knobs[0] to every row.
+ *   d_uniform           one uniform in [0,1] per row (the value the
+ *                       reference's rng_float() would return for that row);
+ *                       ignored for rows that do not draw.
+ *   d_out_id            [B] sampled ids.
+ *   d_out_prob          optional [B]: probability of the sampled id in the
+ *                       final candidate array (1.0 for greedy/guard rows).
+ *   d_stats             optional [B] diagnostics.
+ *   stream              a cudaStream_t (NULL = the context's stream).
+ * Logits are read-only (the reference scales them in place; this does not).
+ * Asynchronous: returns after enqueueing.  Call bm_ctx_check to collect the
+ * device error flag.
+ */
+int bm_sample_batch(bm_ctx_t *ctx, const float *d_logits, int B, int V,
+                    int64_t ld, const int32_t *d_hist,
+                    const int64_t *d_hist_off, const bm_knobs_t *d_knobs,
+                    int64_t knob_stride, const float *d_uniform,
+                    int32_t *d_out_id, float *d_out_prob,
+                    bm_row_stats_t *d_stats, void *stream);
+
+/* ---- batched sampling, host buffers ---------------------------------------- */
+
+/*
+ * Same as bm_sample_batch with every buffer in host memory: copies the
+ * inputs to the context's device staging buffers, samples, copies ids (and
+ * probabilities / stats when non-NULL) back, and synchronises.  Host buffers
+ * may be pageable or pinned (pinned is faster).  h_hist_off may be NULL with
+ * h_hist NULL.
+ */
+int bm_sample_batch_host(bm_ctx_t *ctx, const float *h_logits, int B, int V,
+                         int64_t ld, const int32_t *h_hist,
+                         const int64_t *h_hist_off, const bm_knobs_t *h_knobs,
+                         int64_t knob_stride, const float *h_uniform,
+                         int32_t *h_out_id, float *h_out_prob,
+                         bm_row_stats_t *h_stats);
+
+/* ---- reference calling convention ------------------------------------------ */
+
+/* The reference RNG (src/utils.c:117-140): XorShift64*, default state
+ * 0x853c49e6748fea9b, seed 0 keeps the default; process-global. */
+void bm_rng_seed(uint64_t seed);
+uint64_t bm_rng_next(void);
+float bm_rng_float(void);
+uint64_t bm_rng_get_state(void);
+void bm_rng_set_state(uint64_t state);
+
+/*
+ * One row in the reference's argument order (the tail of model_forward_step,
+ * src/model.c:1268-1307, with sample_advanced's knobs; prototype of the
+ * caller src/bitmamba.h:285-293).  `logits` is host memory and is left
+ * unchanged.  Draws from the process-global RNG exactly when the reference
+ * would (non-greedy rows whose candidate set is not empty).  Runs on the
+ * default context (device from BM_DEVICE, else 0).  Returns the token id, or
+ * a negative BM_ERR_* code.
+ */
+int bm_sample_row(float *logits, int V, const int *history, int history_len,
+                  float penalty, float temp, float min_p, float top_p,
+                  int top_k);
+
+/*
+ * B rows in one launch, equivalent to calling bm_sample_row on rows
+ * 0..B-1 in order: rows draw from the global RNG in row order, only when they
+ * consume.  Host buffers; histories in CSR form (may be NULL).  Returns
+ * BM_OK or a BM_ERR_* code.
+ */
+int bm_sample_rows(const float *h_logits, int B, int V, int64_t ld,
+                   const int32_t *h_hist, const int64_t *h_hist_off,
+                   const bm_knobs_t *h_knobs, int64_t knob_stride,
+                   int32_t *h_out_id);
+
+/* ---- misc ------------------------------------------------------------------ */
+
+/* Human-readable text of the last error on the calling thread. */
+const char *bm_last_error(void);
+int bm_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
