@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""Sampler benchmark: sampled tokens/s at B=4096, V=50257 on 1..8 B200.
+
+Workload (the benchmark's full-vocabulary nucleus stress case): per GPU
+B=4096 rows of V=50257 fp32 logits, N(0,1) with a +15 spike in 25% of the
+rows and flat N(0, 0.1) in another 25%; knobs top_k=0, top_p=0.95, min_p=0,
+temp=1, penalty=1, no history; one uniform per row from the reference
+XorShift64* stream.  Synthetic data, generated on the device.  The 823 MB of
+logits per step exceed the 126 MB L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N --steps K --warmup W]         this library
+  python bench.py --impl reference [...]                 the reference's own
+                                                         C sampler on the host
+For N > 1 launch one rank per GPU with torch.distributed.run; each rank
+samples its own 4096 rows (weak scaling, no collective on the data path).
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "bitmamba.c_b200", "python")]
+
+METRIC = "sampled tokens/s at B=4096,V=50257"
+UNIT = "tokens/s"
+KNOBS = dict(temp=1.0, penalty=1.0, min_p=0.0, top_p=0.95, top_k=0)
+RNG_SEED = 42
+FALLBACK_HBM_GBS = 6650.0
+PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "sample_kernel_c3.md")
+
+
+def workload_config(B, V):
+    return {
+        "workload": "c3 full-vocabulary nucleus stress (B rows/GPU of N(0,1) fp32 logits, "
+                    "25% rows +15 spike, 25% rows flat N(0,0.1); top_k=0 top_p=0.95 "
+                    "min_p=0 temp=1 penalty=1; no history)",
+        "B_per_gpu": B, "V": V,
+        "uniforms": f"reference XorShift64* rng_float stream, seed {RNG_SEED}",
+        "l2": "inputs (B*V*4 bytes per GPU) larger than the 126 MB L2; no flush",
+    }
+
+
+def make_logits(torch, B, V, seed, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    z = torch.randn(B, V, generator=g, device=device, dtype=torch.float32)
+    kind = torch.arange(B, device=device) % 4
+    z[kind == 1] *= 0.1
+    spike_rows = torch.nonzero(kind == 0).squeeze(1)
+    spike_ids = torch.randint(0, V, (spike_rows.numel(),), generator=g, device=device)
+    z[spike_rows, spike_ids] += 15.0
+    return z.contiguous()
+
+
+def ref_uniforms(B, seed=RNG_SEED):
+    """rng_float() stream of the reference (src/utils.c:117-140)."""
+    s = seed if seed else 0x853C49E6748FEA9B
+    m = (1 << 64) - 1
+    out = np.empty(B, np.float32)
+    for i in range(B):
+        s ^= s >> 12
+        s ^= (s << 25) & m
+        s ^= s >> 27
+        v = (s * 0x2545F4914F6CDD1D) & m
+        out[i] = np.float32(float(v >> 11)) * np.float32(1.0 / 9007199254740992.0)
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.t = None
+        self.window = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.t:
+            self.t.join(timeout=5)
+
+    def summary(self):
+        rows = self.rows
+        if self.window and rows:
+            a, b = self.window
+            inside = [r for r in rows if a - 0.15 <= r[0] <= b + 0.15]
+            rows = inside or [min(rows, key=lambda r: abs(r[0] - (a + b) / 2))]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1][1]) for r in rows if num(r[1][1]) is not None]
+        mx = [num(r[1][2]) for r in rows if num(r[1][2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if len(r[1]) > 5 + i and r[1][5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def read_traffic():
+    """dram bytes per launch of the sampling kernel from the committed ncu summary."""
+    try:
+        for line in open(PROFILE_TRAFFIC):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def peak_hbm():
+    try:
+        d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured copy, burst)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback 6650 GB/s (pool measurement)"
+
+
+def cpu_leg(logits_host, u, threads, kind_pref="reference"):
+    """Time the reference's C sampler (oracle/_ref, else the oracle port) on
+    host rows.  Returns (ids, seconds, kind)."""
+    sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests", "golden")]
+    import oracle
+    import synth
+    B, V = logits_host.shape
+    b = synth.Batch(logits_host, np.zeros(0, np.int32), np.zeros(B + 1, np.int64),
+                    np.full(B, KNOBS["temp"], np.float32), np.full(B, KNOBS["penalty"], np.float32),
+                    np.full(B, KNOBS["min_p"], np.float32), np.full(B, KNOBS["top_p"], np.float32),
+                    np.full(B, KNOBS["top_k"], np.int32))
+    if kind_pref == "reference" and oracle.has_ref():
+        t = time.perf_counter()
+        ids = oracle.ref_sample_batch_mt(b, u, threads)
+        return ids, time.perf_counter() - t, "reference"
+    oracle.lib()
+    t = time.perf_counter()
+    ids, _, _ = oracle.sample_batch(b, u, threads=threads, with_results=False)
+    return ids, time.perf_counter() - t, "port"
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    """The reference arm: the reference's own sampler on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    import torch
+    B, V = args.B, args.V
+    threads = host_threads()
+    # a bounded sample of the workload, sized so warmup + steps stay within
+    # about two minutes on this host
+    pool_rows = 512
+    logits = make_logits(torch, pool_rows, V, 1234, "cpu").numpy()
+    u = ref_uniforms(pool_rows)
+    per_row_s = 0.006  # measured scale of the full-sort rows on one core
+    budget = 120.0
+    rows_per_step = int(max(threads, min(pool_rows, budget / (args.steps + args.warmup)
+                                         * threads / per_row_s)))
+    rows_per_step = max(1, min(pool_rows, rows_per_step))
+    kind = None
+    for w in range(args.warmup):
+        s = (w * rows_per_step) % pool_rows
+        sel = np.arange(s, s + rows_per_step) % pool_rows
+        _, _, kind = cpu_leg(np.ascontiguousarray(logits[sel]), u[sel], threads)
+    total = 0.0
+    for k in range(args.steps):
+        s = (k * rows_per_step) % pool_rows
+        sel = np.arange(s, s + rows_per_step) % pool_rows
+        _, dt, kind = cpu_leg(np.ascontiguousarray(logits[sel]), u[sel], threads)
+        total += dt
+    value = rows_per_step * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(B, V), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{rows_per_step} rows of the workload per step "
+                                   f"(pool of {pool_rows} rows), row-parallel pthreads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import bmsampler as bm
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (no CPU fallback)")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    B, V = args.B, args.V
+    dev = torch.device("cuda", local)
+    ctx = bm.Context(local)
+    logits = make_logits(torch, B, V, 1234 + rank, dev)
+    knobs = bm.knobs_array(KNOBS["temp"], KNOBS["penalty"], KNOBS["min_p"], KNOBS["top_p"],
+                           KNOBS["top_k"])
+    knobs_d = torch.from_numpy(knobs.view(np.uint8).copy()).to(dev)
+    u_host = ref_uniforms(B)
+    u_d = torch.from_numpy(u_host).to(dev)
+    out_d = torch.empty(B, dtype=torch.int32, device=dev)
+    # a dedicated stream: torch's legacy default stream has handle 0, which the
+    # library reads as "use the context stream"
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)
+
+    def launch():
+        ctx.sample_device(logits.data_ptr(), B, V, V, 0, 0, knobs_d.data_ptr(), 0,
+                          u_d.data_ptr(), out_d.data_ptr(), None, None, stream.cuda_stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- device-resident throughput -------------------------------------
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize(dev)
+    ctx.check()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_a = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_b = time.time()
+    barrier()
+    clocks.window = (t_a, t_b)
+    time.sleep(0.25)
+    clocks.stop()
+    ctx.check()
+    ms = e0.elapsed_time(e1)
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * B * args.steps / (ms_max / 1e3)
+    kernel_ms = ms / args.steps
+    alg_bytes = B * (4 * V + 4 + 4) + 32  # logits, uniform, id, knobs (no history)
+    achieved = alg_bytes / (kernel_ms / 1e3) / 1e9
+    peak, peak_src = peak_hbm()
+    ids_dev = out_d.cpu().numpy()
+
+    # ---- end to end through the host-buffer API -----------------------------
+    e2e = None
+    if not args.no_e2e:
+        h_logits = logits.cpu().pin_memory()
+        h_u = torch.from_numpy(u_host).pin_memory()
+        h_ids = torch.empty(B, dtype=torch.int32).pin_memory()
+        h_knobs = torch.from_numpy(knobs.view(np.uint8).copy()).pin_memory()
+        L = bm.lib()
+        c = bm.ctypes.c_void_p
+
+        def call():
+            bm.check(L.bm_sample_batch_host(ctx.handle, c(h_logits.data_ptr()), B, V, V, None,
+                                            None, c(h_knobs.data_ptr()), 0,
+                                            c(h_u.data_ptr()), c(h_ids.data_ptr()), None,
+                                            None))
+        n_e2e = max(3, min(args.steps, 20))
+        for _ in range(min(3, args.warmup)):
+            call()
+        cs = torch.cuda.ExternalStream(ctx.stream(), device=dev)
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        f0.record(cs)
+        for _ in range(n_e2e):
+            call()
+        f1.record(cs)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e_ms = f0.elapsed_time(f1)
+        if dist is not None:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        if not np.array_equal(h_ids.numpy(), ids_dev):
+            raise SystemExit("e2e ids differ from the device-resident run")
+        e2e = {"value": world * B * n_e2e / (e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": B * V * 4 + B * 4 + 32, "d2h_bytes_per_step": B * 4,
+               "steps": n_e2e, "ms_per_step": e_ms / n_e2e}
+
+    # ---- CPU baseline on a bounded sample (rank 0, N=1 only) ----------------
+    cpu = None
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n = min(B, args.cpu_rows)
+        threads = host_threads()
+        h = logits[:n].cpu().numpy()
+        ids_cpu, dt, kind = cpu_leg(h, u_host[:n], threads)
+        cpu = {"value": n / dt, "unit": UNIT, "cores": threads, "kind": kind,
+               "sample": f"first {n} rows of the workload (all four row kinds), "
+                         f"row-parallel pthreads"}
+        same = int((ids_cpu == ids_dev[:n]).sum())
+        parity = {"rows": n, "identical_ids": same}
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    traffic = read_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(B, V),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": alg_bytes, "peak_source": peak_src,
+                     "kernel": "sample_kernel", "kernel_ms": kernel_ms},
+        "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+        "gpu_launches": args.steps, "parity_sample": parity,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--B", type=int, default=4096)
+    ap.add_argument("--V", type=int, default=50257)
+    ap.add_argument("--cpu-rows", type=int, default=2048)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -174,6 +174,8 @@ void bm_ctx_destroy(bm_ctx_t *c) {
 
 int bm_max_vocab(const bm_ctx_t *c) { return c ? c->max_vocab : 0; }
 
+void *bm_ctx_stream(bm_ctx_t *c) { return c ? static_cast<void *>(c->stream) : nullptr; }
+
 int bm_ctx_check(bm_ctx_t *c) {
     if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
     CK(cudaSetDevice(c->device));

@@ -58,6 +58,8 @@ def lib():
         L.bm_ctx_destroy.restype = None
         L.bm_max_vocab.argtypes = [_P]
         L.bm_ctx_check.argtypes = [_P]
+        L.bm_ctx_stream.argtypes = [_P]
+        L.bm_ctx_stream.restype = _P
         L.bm_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
                                       _P, _P, _P, ctypes.c_int64, _P, _P, _P, _P, _P]
         L.bm_sample_batch_host.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int,
@@ -133,6 +135,9 @@ class Context:
 
     def check(self):
         check(lib().bm_ctx_check(self._c))
+
+    def stream(self) -> int:
+        return lib().bm_ctx_stream(self._c) or 0
 
     def sample_device(self, logits_ptr, B, V, ld, hist_ptr, off_ptr, knobs_ptr, knob_stride,
                       u_ptr, out_id_ptr, out_prob_ptr=None, stats_ptr=None, stream=None):

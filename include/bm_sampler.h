@@ -103,6 +103,12 @@ int bm_max_vocab(const bm_ctx_t *ctx);
  * Returns BM_OK or BM_ERR_DEVICE. */
 int bm_ctx_check(bm_ctx_t *ctx);
 
+/* The context's CUDA stream (a cudaStream_t), on which bm_sample_batch_host
+ * and bm_sample_batch with stream == NULL run; lets callers order their own
+ * work (events, copies) against the sampler.  No reference counterpart: the
+ * reference sampler is synchronous on the calling thread. */
+void *bm_ctx_stream(bm_ctx_t *ctx);
+
 /* ---- batched sampling, device buffers -------------------------------------- */
 
 /*

@@ -130,3 +130,25 @@ def ref_sample_batch(b, uniforms):
         probs[r] = p.value
         cons[r] = c.value
     return ids, probs, cons
+
+
+def ref_sample_batch_mt(b, uniforms, threads: int):
+    """The reference's own sampler over a batch with `threads` pthreads
+    (oracle/_ref).  Returns ids."""
+    L = ref_lib()
+    f = L.bm_ref_sample_batch
+    f.restype = ctypes.c_int
+    B, V = b.logits.shape
+    u = np.ascontiguousarray(uniforms, np.float32)
+    out = np.empty(B, np.int32)
+    hist = b.hist if b.hist.size else None
+    rc = f(_p(b.logits, ctypes.c_float), B, V, ctypes.c_longlong(V),
+           _p(hist, ctypes.c_int32) if hist is not None else None,
+           _p(b.hist_off, ctypes.c_int64) if hist is not None else None,
+           _p(b.temp, ctypes.c_float), _p(b.penalty, ctypes.c_float),
+           _p(b.min_p, ctypes.c_float), _p(b.top_p, ctypes.c_float),
+           _p(b.top_k, ctypes.c_int32), _p(u, ctypes.c_float),
+           _p(out, ctypes.c_int32), threads)
+    if rc != 0:
+        raise MemoryError("reference batch failed")
+    return out

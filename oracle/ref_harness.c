@@ -78,3 +78,67 @@ int bm_ref_sizeof_token_prob(void)
 {
     return (int) sizeof(token_prob_t);
 }
+
+/* Row-parallel driver over the reference sampler for the CPU baseline: rows
+ * [B x ld], per-row knobs, CSR histories (may be NULL), one uniform per row.
+ * Each thread owns a logits copy, a probs buffer and a bitset, so the
+ * reference's shared model buffers are not needed.  Returns 0 or -1. */
+#include <pthread.h>
+typedef struct {
+    const float *logits; int B, V; long long ld;
+    const int *hist; const long long *off;
+    const float *temp, *penalty, *min_p, *top_p; const int *top_k;
+    const float *u; int *out; int nt, tid, failed;
+} ref_job_t;
+
+static void *ref_worker(void *arg)
+{
+    ref_job_t *j = (ref_job_t *) arg;
+    float *row = malloc((size_t) j->V * sizeof(float));
+    token_prob_t *probs = malloc((size_t) j->V * sizeof(token_prob_t));
+    uint64_t *vis = malloc(((size_t) j->V + 63) / 64 * 8);
+    if (!row || !probs || !vis) {
+        j->failed = 1;
+        free(row); free(probs); free(vis);
+        return NULL;
+    }
+    for (int r = j->tid; r < j->B; r += j->nt) {
+        memcpy(row, j->logits + (long long) r * j->ld, (size_t) j->V * sizeof(float));
+        const int *h = j->hist ? j->hist + j->off[r] : NULL;
+        int hl = j->hist ? (int) (j->off[r + 1] - j->off[r]) : 0;
+        int c; float p;
+        j->out[r] = bm_ref_sample_row(row, j->V, h, hl, j->penalty[r], j->temp[r],
+                                      j->min_p[r], j->top_p[r], j->top_k[r], j->u[r],
+                                      &c, &p, probs, vis);
+    }
+    free(row); free(probs); free(vis);
+    return NULL;
+}
+
+int bm_ref_sample_batch(const float *logits, int B, int V, long long ld,
+                        const int *hist, const long long *off, const float *temp,
+                        const float *penalty, const float *min_p, const float *top_p,
+                        const int *top_k, const float *u, int *out, int n_threads)
+{
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > B) n_threads = B > 0 ? B : 1;
+    ref_job_t *jobs = calloc((size_t) n_threads, sizeof(ref_job_t));
+    pthread_t *th = calloc((size_t) n_threads, sizeof(pthread_t));
+    if (!jobs || !th) { free(jobs); free(th); return -1; }
+    int rc = 0;
+    for (int t = 0; t < n_threads; t++) {
+        ref_job_t jb = {logits, B, V, ld, hist, off, temp, penalty, min_p, top_p, top_k,
+                        u, out, n_threads, t, 0};
+        jobs[t] = jb;
+        if (pthread_create(&th[t], NULL, ref_worker, &jobs[t]) != 0) {
+            ref_worker(&jobs[t]);
+            th[t] = 0;
+        }
+    }
+    for (int t = 0; t < n_threads; t++) {
+        if (th[t]) pthread_join(th[t], NULL);
+        rc |= jobs[t].failed;
+    }
+    free(jobs); free(th);
+    return rc ? -1 : 0;
+}
