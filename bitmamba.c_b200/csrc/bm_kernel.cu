@@ -3,26 +3,32 @@
 //
 // Per row (reference: jserv/bitmamba.c src/model.c:1268-1307, 37-361):
 //   load      bulk async copy of the row's 16-byte-aligned interior into shared
-//             memory in NCHUNK pieces (one mbarrier each), ragged head/tail by
-//             plain loads, next row of this CTA prefetched into L2.  The
-//             repetition penalty is applied while the row is consumed, from a
-//             bitset of the row's distinct history ids (src/model.c:1277-1304),
-//             and the pass computes max / min of the scaled logits
+//             memory in NCHUNK pieces (one mbarrier each; the copy for the
+//             next row is issued as soon as this row's buffer is free, and the
+//             row after that is prefetched into L2), ragged head/tail by plain
+//             loads with NaN in the junk lanes so every later pass runs over
+//             whole 16-byte slots.  The repetition penalty is applied from a
+//             bitset of the row's distinct history ids (src/model.c:1277-1304);
+//             the pass reduces max / min of the scaled logits
 //             (src/model.c:156-163) or the greedy argmax (src/model.c:144-154).
 //   top_k     1 <= top_k <= 256: the reference's 128-bucket histogram cut
-//             (src/model.c:181-214), extraction, exact emulation of its
-//             min-heap (heap layout decides the CDF walk order), survivor
+//             (src/model.c:181-214) with the candidates above the min_p
+//             threshold collected in the same pass, exact emulation of its
+//             min-heap (the heap layout decides the CDF walk order), survivor
 //             softmax, stable descending sort, nucleus cut and draw.
-//   full      other top_k: expf against the global max into shared memory with
-//             a logit-bucket count histogram, then either the id-order walk
-//             (src/model.c:319-320) or a select in (prob desc, id asc) order
-//             (the order the reference's stable qsort produces) through
-//             estimated windows verified by exact passes.  Rows where the
-//             reference's top-256 heap path applies and ties make its layout
-//             visible are replayed exactly (src/model.c:327-356).
+//   full      other top_k: exp(l - max) into shared memory with a bucket-count
+//             histogram over max - l, then either the id-order walk
+//             (src/model.c:319-320) or one exact pass that resolves the
+//             nucleus cut, the top_k position and the draw in
+//             (probability desc, id asc) order -- the order the reference's
+//             stable qsort produces -- through windows estimated from the
+//             histogram.  Rows where the reference's top-256 heap path applies
+//             and ties make its layout visible are replayed exactly
+//             (src/model.c:327-356).
 //
-// Arithmetic that decides ids is done with the reference's fp32 operations
-// (no contraction: explicit __fmul_rn/__fadd_rn/__fdiv_rn), sums in fp64.
+// Arithmetic that decides ids uses the reference's fp32 operations (no
+// contraction: explicit __fmul_rn/__fadd_rn/__fdiv_rn; the library is built
+// with --fmad=false), sums in fp64.
 #include "bm_kernel.cuh"
 
 #include <cfloat>
@@ -32,9 +38,15 @@ namespace bmk {
 namespace {
 
 constexpr unsigned FULL = 0xffffffffu;
-constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded mbarrier waits: 2 s
-constexpr float DCAP = 40.0f;                // bucket range cap (e^-40 ~ 4e-18)
-constexpr float MAGIC = 12582912.0f;         // 1.5 * 2^23: round-to-int trick
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
+constexpr float DCAP = 40.0f;                          // bucket range cap
+constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
+constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
+constexpr int LCAP = 512;                              // per-window list cap
+constexpr int BPT = NB / NT;                            // estimate buckets per thread
+constexpr int SLOW_CAP = 512;                          // rare-path list cap
+constexpr float PINF = __builtin_huge_valf();
+constexpr size_t RED_BYTES = 2048;
 
 // GPT-2 ids the reference never penalises (src/bitmamba.h:21-24).
 __device__ __forceinline__ bool protected_id(int id) {
@@ -44,15 +56,18 @@ __device__ __forceinline__ bool protected_id(int id) {
 struct __align__(16) Vars {
     float mx, thr, xmin, inv_temp;
     float temp, penalty, min_p, top_p;
-    float log_min_p, u, inv_sum, dmax;
+    float log_min_p, u, inv_sum, w;
     int top_k, greedy, pen, k;
     int sh, nslots, s_int0, s_int1;
-    int res_id, n_cand, n_final, path;
-    int consumed, kcut, kcnt, list_n;
-    int bhat, cnt_above, last_cand, fail;
-    int sel_j, sel_found, sel_tie, own;
-    float res_p, w, inv_w, pad0;
-    double S, above, cs, aux;
+    int h0, h1, released, fail;
+    int kcut, kcnt, n_cand, own;
+    int bh0, bh1, bh2, pad0;
+    int ln0, ln1, ln2, ln3;
+    int sel_found, sel_j, res_id, n_final;
+    float res_p, pad1, pad2, pad3;
+    double S, cs, aux0, aux1;
+    double wab[3];
+    int wca[3], pad4;
 };
 
 struct Layout {
@@ -68,7 +83,7 @@ __host__ __device__ inline Layout layout(int V) {
     L.mbar = o;
     o += NCHUNK * 8;
     L.red = o;
-    o += 1024;
+    o += RED_BYTES;
     L.vars = o;
     o += r16(sizeof(Vars));
     L.nbw = (V + 3 + 31) / 32 + 1;
@@ -136,6 +151,11 @@ __device__ __forceinline__ void fence_proxy_async() {
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // --------------------------------------------------------- small helpers --
 // (int)t as x86 cvttss2si computes it (NaN / out of range -> INT_MIN), the
@@ -147,6 +167,21 @@ __device__ __forceinline__ int x86_cvtt(float t) {
 __device__ __forceinline__ float penalize(float l, float pen) {
     return (l > 0.0f) ? __fdiv_rn(l, pen) : __fmul_rn(l, pen);
 }
+// exp(x) for x <= 0 as 2^y * 2^c with y = fl(x*L1) and c the exact residual
+// of x*L1 plus x*L2 (L1 + L2 = log2 e); 2^c = 1 + c ln2 to fp32 accuracy
+// since |c| < 2^-16.  Error: that of ex2.approx plus one rounding.
+__device__ __forceinline__ float2 exp_pair(float2 x) {
+    const float2 L1 = make_float2(1.4426950216293335f, 1.4426950216293335f);
+    const float2 L2 = make_float2(1.925963033500011e-08f, 1.925963033500011e-08f);
+    const float2 LN2 = make_float2(0.6931471824645996f, 0.6931471824645996f);
+    const float2 y = __fmul2_rn(x, L1);
+    float2 c = __ffma2_rn(x, L1, make_float2(-y.x, -y.y));
+    c = __ffma2_rn(x, L2, c);
+    const float2 e = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+    const float2 t = __fmul2_rn(e, c);
+    return __ffma2_rn(t, LN2, e);
+}
+__device__ __forceinline__ float exp_one(float x) { return exp_pair(make_float2(x, x)).x; }
 __device__ __forceinline__ unsigned long long canon_key(float p, int id) {
     // ascending key order == probability descending, id ascending (p >= 0)
     return ((unsigned long long)(~__float_as_uint(p)) << 32) | (unsigned)id;
@@ -182,7 +217,6 @@ __device__ __forceinline__ int warp_imin(int v) {
     for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(FULL, v, o));
     return v;
 }
-// inclusive warp scan
 template <class T>
 __device__ __forceinline__ T warp_iscan(T v, int lane) {
 #pragma unroll
@@ -192,8 +226,7 @@ __device__ __forceinline__ T warp_iscan(T v, int lane) {
     }
     return v;
 }
-// (value, index) with "larger value, then smaller index" preference; idx
-// INT_MAX means none.
+// (value, index): larger value, then smaller index; idx INT_MAX = none.
 __device__ __forceinline__ void argmax_combine(float &v, int &i, float v2, int i2) {
     bool take = (i == INT_MAX) ? (i2 != INT_MAX)
                                : (i2 != INT_MAX && (v2 > v || (v2 == v && i2 < i)));
@@ -208,21 +241,19 @@ __device__ __forceinline__ void warp_argmax(float &v, int &i) {
     }
 }
 
-// Block-level reductions.  `rd` holds NW doubles, `ri` NW ints (two arrays
-// laid side by side in the red area).  Every thread gets the result.
+// Block reductions over NT threads; every thread gets the result.  The red
+// area holds 2*NW doubles, 4*NW ints and 2*NW floats side by side.
 struct Red {
     double *d;
     int *i;
     float *f;
 };
-
 __device__ __forceinline__ double block_sum_d(double v, Red r) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     v = warp_sum(v);
     if (lane == 0) r.d[warp] = v;
     __syncthreads();
-    double t = r.d[lane];
-    t = warp_sum(t);
+    double t = warp_sum(lane < NW ? r.d[lane] : 0.0);
     __syncthreads();
     return t;
 }
@@ -231,8 +262,7 @@ __device__ __forceinline__ int block_sum_i(int v, Red r) {
     v = warp_sum(v);
     if (lane == 0) r.i[warp] = v;
     __syncthreads();
-    int t = r.i[lane];
-    t = warp_sum(t);
+    int t = warp_sum(lane < NW ? r.i[lane] : 0);
     __syncthreads();
     return t;
 }
@@ -241,7 +271,7 @@ __device__ __forceinline__ int block_max_i(int v, Red r) {
     v = warp_imax(v);
     if (lane == 0) r.i[warp] = v;
     __syncthreads();
-    int t = warp_imax(r.i[lane]);
+    int t = warp_imax(lane < NW ? r.i[lane] : INT_MIN);
     __syncthreads();
     return t;
 }
@@ -250,7 +280,7 @@ __device__ __forceinline__ int block_min_i(int v, Red r) {
     v = warp_imin(v);
     if (lane == 0) r.i[warp] = v;
     __syncthreads();
-    int t = warp_imin(r.i[lane]);
+    int t = warp_imin(lane < NW ? r.i[lane] : INT_MAX);
     __syncthreads();
     return t;
 }
@@ -260,8 +290,8 @@ __device__ __forceinline__ void block_maxmin_f(float &mx, float &mn, Red r) {
     mn = warp_min(mn);
     if (lane == 0) { r.f[warp] = mx; r.f[NW + warp] = mn; }
     __syncthreads();
-    mx = warp_max(r.f[lane]);
-    mn = warp_min(r.f[NW + lane]);
+    mx = warp_max(lane < NW ? r.f[lane] : -PINF);
+    mn = warp_min(lane < NW ? r.f[NW + lane] : PINF);
     __syncthreads();
 }
 __device__ __forceinline__ void block_argmax(float &v, int &i, Red r) {
@@ -269,18 +299,38 @@ __device__ __forceinline__ void block_argmax(float &v, int &i, Red r) {
     warp_argmax(v, i);
     if (lane == 0) { r.f[warp] = v; r.i[warp] = i; }
     __syncthreads();
-    v = r.f[lane];
-    i = r.i[lane];
+    v = lane < NW ? r.f[lane] : 0.f;
+    i = lane < NW ? r.i[lane] : INT_MAX;
     warp_argmax(v, i);
     __syncthreads();
 }
-// exclusive block scan of doubles; returns exclusive prefix, sets total
+// several sums at once: doubles a, b and ints c, d
+__device__ __forceinline__ void block_sum4(double &a, double &b, int &c, int &d, Red r) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    a = warp_sum(a);
+    b = warp_sum(b);
+    c = warp_sum(c);
+    d = warp_sum(d);
+    if (lane == 0) {
+        r.d[warp] = a;
+        r.d[NW + warp] = b;
+        r.i[2 * NW + warp] = c;
+        r.i[3 * NW + warp] = d;
+    }
+    __syncthreads();
+    a = warp_sum(lane < NW ? r.d[lane] : 0.0);
+    b = warp_sum(lane < NW ? r.d[NW + lane] : 0.0);
+    c = warp_sum(lane < NW ? r.i[2 * NW + lane] : 0);
+    d = warp_sum(lane < NW ? r.i[3 * NW + lane] : 0);
+    __syncthreads();
+}
+// exclusive block scans; return the exclusive prefix, set the total
 __device__ __forceinline__ double block_xscan_d(double v, double &total, Red r) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     double inc = warp_iscan(v, lane);
     if (lane == 31) r.d[warp] = inc;
     __syncthreads();
-    double w = r.d[lane];
+    double w = lane < NW ? r.d[lane] : 0.0;
     double winc = warp_iscan(w, lane);
     double woff = __shfl_sync(FULL, winc - w, warp);
     total = __shfl_sync(FULL, winc, 31);
@@ -292,7 +342,7 @@ __device__ __forceinline__ int block_xscan_i(int v, int &total, Red r) {
     int inc = warp_iscan(v, lane);
     if (lane == 31) r.i[warp] = inc;
     __syncthreads();
-    int w = r.i[lane];
+    int w = lane < NW ? r.i[lane] : 0;
     int winc = warp_iscan(w, lane);
     int woff = __shfl_sync(FULL, winc - w, warp);
     total = __shfl_sync(FULL, winc, 31);
@@ -300,9 +350,9 @@ __device__ __forceinline__ int block_xscan_i(int v, int &total, Red r) {
     return woff + inc - v;
 }
 
-// In-place ascending bitonic sort of n <= cap 64-bit keys in shared memory,
-// padded to a power of two with ~0.  All threads call it.
-__device__ void block_sort_u64(unsigned long long *a, int n, int cap) {
+// In-place ascending bitonic sort of n <= cap 64-bit keys, padded to a power
+// of two with ~0 (cap a power of two).  All threads call it.
+__device__ void bitonic_u64(unsigned long long *a, int n, int cap) {
     int P = 1;
     while (P < n) P <<= 1;
     if (P > cap) P = cap;
@@ -311,15 +361,56 @@ __device__ void block_sort_u64(unsigned long long *a, int n, int cap) {
     for (int k = 2; k <= P; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
             for (int t = threadIdx.x; t < (P >> 1); t += NT) {
-                int i = ((t / j) * (j << 1)) + (t % j);
-                int l = i + j;
-                bool up = ((i & k) == 0);
-                unsigned long long x = a[i], y = a[l];
+                const int i = ((t / j) * (j << 1)) + (t % j);
+                const int l = i + j;
+                const bool up = ((i & k) == 0);
+                const unsigned long long x = a[i], y = a[l];
                 if ((x > y) == up) { a[i] = y; a[l] = x; }
             }
             __syncthreads();
         }
     }
+}
+
+// Ascending sort of n unique 64-bit keys in shared memory.  n <= 32: one warp
+// by register ranks; n <= NT: ranks summed from slices of the comparisons
+// with integer shared atomics into `rank` (n ints), then a scatter; larger n:
+// bitonic with capacity `cap`.  All threads call it.
+__device__ void sort_keys(unsigned long long *a, int n, int *rank, int cap) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (n <= 1) return;
+    if (n <= 32) {
+        if (warp == 0) {
+            const unsigned long long k = (lane < n) ? a[lane] : ~0ull;
+            int r = 0;
+            for (int j = 0; j < n; ++j) r += (__shfl_sync(FULL, k, j) < k);
+            __syncwarp();
+            if (lane < n) a[r] = k;
+        }
+        __syncthreads();
+        return;
+    }
+    if (n > NT) {
+        bitonic_u64(a, n, cap);
+        return;
+    }
+    for (int i = threadIdx.x; i < n; i += NT) rank[i] = 0;
+    __syncthreads();
+    const int G = NT / n;
+    const int per = (n + G - 1) / G;
+    if ((int)threadIdx.x < n * G) {
+        const int i = threadIdx.x % n, g = threadIdx.x / n;
+        const unsigned long long ki = a[i];
+        const int j0 = g * per, j1 = min(n, j0 + per);
+        int r = 0;
+        for (int j = j0; j < j1; ++j) r += (a[j] < ki);
+        if (r) atomicAdd(&rank[i], r);
+    }
+    __syncthreads();
+    const unsigned long long mine = ((int)threadIdx.x < n) ? a[threadIdx.x] : 0ull;
+    __syncthreads();
+    if ((int)threadIdx.x < n) a[rank[threadIdx.x]] = mine;
+    __syncthreads();
 }
 
 // Min-heap sift-down on parallel arrays, exactly src/model.c:50-66
@@ -336,8 +427,8 @@ __device__ void heap_down(float *hv, int *hi, int n, int i) {
     }
 }
 // Floyd heapify (src/model.c:242-243, 330-331) by one warp, level by level:
-// nodes of one level root disjoint subtrees, and every deeper node has a
-// larger index, so this is the reference's sequential order.
+// nodes of one level root disjoint subtrees and every deeper node has a
+// larger index, so this equals the reference's sequential order.
 __device__ void warp_heapify(float *hv, int *hi, int k, int lane) {
     int last = k / 2 - 1;
     if (last < 0) return;
@@ -349,10 +440,12 @@ __device__ void warp_heapify(float *hv, int *hi, int k, int lane) {
     }
 }
 
-// ------------------------------------------------------------ the kernel --
+// ---------------------------------------------------------- row context --
 struct Ctx {
-    Params P;
-    Layout L;
+    const float *logits;
+    int64_t ld;
+    int B, V;
+    int *err;
     uint64_t *mbar;
     Red red;
     Vars *v;
@@ -360,482 +453,98 @@ struct Ctx {
     unsigned char *scr;
     float *row;  // 16-byte aligned; element e lives at row[e + sh]
     const float *g;
+    int32_t *out_id;
+    float *out_prob;
+    bm_row_stats_t *stats;
     int rowid;
     uint32_t parity;
+    // Point the shared-memory fields at the dynamic shared array.  Called at
+    // the top of every non-inlined function: pointers that arrive as
+    // arguments lose their address space and every access through them would
+    // become a generic load, store or atomic.
+    __device__ __forceinline__ void attach() {
+        extern __shared__ __align__(128) unsigned char smem_dyn[];
+        const Layout L = layout(V);
+        mbar = reinterpret_cast<uint64_t *>(smem_dyn + L.mbar);
+        red.d = reinterpret_cast<double *>(smem_dyn + L.red);
+        red.i = reinterpret_cast<int *>(smem_dyn + L.red + 2 * NW * 8);
+        red.f = reinterpret_cast<float *>(smem_dyn + L.red + 2 * NW * 8 + 4 * NW * 4);
+        v = reinterpret_cast<Vars *>(smem_dyn + L.vars);
+        bits = reinterpret_cast<uint32_t *>(smem_dyn + L.bits);
+        scr = smem_dyn + L.scr;
+        row = reinterpret_cast<float *>(smem_dyn + L.row);
+    }
 };
 
-// Walk a list (in shared memory, n entries, key form) from a starting mass:
-// finds the first j with start + cum(j) >= T (mode 0), > T (mode 1).  Runs on
-// one warp; results go to vars (sel_found/sel_j, cs).
-__device__ void warp_walk(const unsigned long long *keys, int n, double start, int mode,
-                          double T, Vars *v, int lane) {
-    const int per = (n + 31) / 32;
-    const int b = lane * per, e = min(n, b + per);
-    double s = 0.0;
-    for (int j = b; j < e; ++j) s += (double)key_p(keys[j]);
-    double inc = warp_iscan(s, lane);
-    double pre = start + (inc - s);
-    int hit = INT_MAX;
-    double hit_cs = 0.0;
-    if (b < e) {
-        double cs = pre;
-        for (int j = b; j < e; ++j) {
-            cs += (double)key_p(keys[j]);
-            bool ok = (mode == 0) ? (cs >= T) : (cs > T);
-            if (ok) { hit = j; hit_cs = cs; break; }
-        }
+// Issue the bulk copies of one row into the row buffer (one thread).
+__device__ __forceinline__ void issue_row(const float *g, int V, uint64_t *mbar, float *rowbuf) {
+    const int sh = (int)(((uintptr_t)g & 15u) >> 2);
+    int i0 = sh ? 4 - sh : 0;
+    if (i0 > V) i0 = V;
+    int n4 = ((V - i0) >> 2) << 2;
+    if (n4 < 4 * NCHUNK * 4) n4 = 0;  // tiny rows: plain loads only
+    const int s_int0 = (i0 + sh) >> 2;
+    const int nint = n4 >> 2;
+    for (int ch = 0; ch < NCHUNK; ++ch) {
+        const int a = (ch * nint) / NCHUNK, b = ((ch + 1) * nint) / NCHUNK;
+        const uint32_t bytes = (uint32_t)(b - a) * 16u;
+        mbar_expect_tx(&mbar[ch], bytes);
+        if (bytes) bulk_load(rowbuf + 4 * (s_int0 + a), g + i0 + 4 * a, bytes, &mbar[ch]);
     }
-    int best = warp_imin(hit);
-    if (best != INT_MAX) {
-        int owner = (best / per);
-        double cs = __shfl_sync(FULL, hit_cs, owner);
-        if (lane == 0) { v->sel_found = 1; v->sel_j = best; v->cs = cs; }
-    } else if (lane == 0) {
-        v->sel_found = 0;
-        v->sel_j = n;
-        v->cs = start + __shfl_sync(FULL, inc, 31);
-    }
-    if (best == INT_MAX) (void)__shfl_sync(FULL, inc, 31);
 }
 
-// ---- full-vocabulary select ------------------------------------------------
-// Candidates hold e = expf(l - max) >= 0 in the row buffer (non-candidates
-// -1).  p = e * inv_sum.  Canonical order: p descending, id ascending (the
-// order the reference's stable qsort leaves the id-ordered candidates in).
-struct Sel {
-    int found;  // 1 = crossing found; 0 = beyond the last candidate
-    int pos;    // position in canonical order (0-based)
-    int id;
-    float p;
-    double cs;  // cumulative mass through `pos`
-    int tie;    // another candidate has the same p
-};
-
-struct PassOut {
-    double above, in_mass;
-    int cnt_above, in_cnt;
-};
-
-// One exact pass over the candidates for the probability window [plo, phi]:
-// mass / count strictly above phi, mass / count inside, and the inside
-// elements collected into `list` as canonical keys (only the first WCAP).
-__device__ PassOut exact_pass(Ctx &c, float plo, float phi, unsigned long long *list) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    Vars *v = c.v;
-    const float inv_sum = v->inv_sum;
-    const int sh = v->sh, nslots = v->nslots;
-    if (threadIdx.x == 0) v->list_n = 0;
+// The row buffer is no longer read for this row: let the next row's copy in.
+__device__ __forceinline__ void release_row(Ctx &c) {
+    fence_proxy_async();
     __syncthreads();
-    double acc_up = 0.0, acc_in = 0.0;
-    int cnt_up = 0;
-    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    for (int base = warp * 32; base < nslots; base += NT) {
-        int s = base + lane;
-        float4 e4 = make_float4(-1.f, -1.f, -1.f, -1.f);
-        if (s < nslots) e4 = r4[s];
-        float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-        float gu0 = 0.f, gu1 = 0.f, gi0 = 0.f, gi1 = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float e = ev[q];
-            bool cand = (e >= 0.0f);
-            float p = __fmul_rn(cand ? e : 0.0f, inv_sum);
-            bool up = cand && (p > phi);
-            bool in = cand && !up && (p >= plo);
-            if (q < 2) { gu0 = __fadd_rn(gu0, up ? p : 0.f); gi0 = __fadd_rn(gi0, in ? p : 0.f); }
-            else { gu1 = __fadd_rn(gu1, up ? p : 0.f); gi1 = __fadd_rn(gi1, in ? p : 0.f); }
-            cnt_up += up;
-            unsigned m = __ballot_sync(FULL, in);
-            if (m) {
-                int leader = __ffs(m) - 1;
-                int bpos = 0;
-                if (lane == leader) bpos = atomicAdd(&v->list_n, __popc(m));
-                bpos = __shfl_sync(FULL, bpos, leader);
-                if (in) {
-                    int pos = bpos + __popc(m & ((1u << lane) - 1));
-                    if (pos < WCAP) list[pos] = canon_key(p, 4 * s + q - sh);
-                }
-            }
-        }
-        acc_up += (double)__fadd_rn(gu0, gu1);
-        acc_in += (double)__fadd_rn(gi0, gi1);
+    if (threadIdx.x == 0) {
+        c.v->released = 1;
+        const int next_row = c.rowid + gridDim.x;
+        if (next_row < c.B) issue_row(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row);
     }
-    PassOut o;
-    o.above = block_sum_d(acc_up, c.red);
-    o.in_mass = block_sum_d(acc_in, c.red);
-    o.cnt_above = block_sum_i(cnt_up, c.red);
-    o.in_cnt = v->list_n;
-    __syncthreads();
-    return o;
 }
 
-// Ordered select inside one probability value: the j-th (0-based, id order)
-// candidate whose p equals `pv`.  Contiguous slot segments per thread.
-__device__ int ordered_pick(Ctx &c, float pv, int j) {
-    Vars *v = c.v;
-    const float inv_sum = v->inv_sum;
-    const int sh = v->sh, nslots = v->nslots;
-    const int Q = (nslots + NT - 1) / NT;
-    const int s0 = threadIdx.x * Q, s1 = min(nslots, s0 + Q);
-    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    int cnt = 0;
-    for (int s = s0; s < s1; ++s) {
-        float4 e4 = r4[s];
-        float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            cnt += (ev[q] >= 0.0f) && (__fmul_rn(ev[q], inv_sum) == pv);
-    }
-    int tot;
-    int ex = block_xscan_i(cnt, tot, c.red);
-    if (threadIdx.x == 0) v->own = -1;
-    __syncthreads();
-    if (j >= ex && j < ex + cnt) {
-        int k = ex;
-        for (int s = s0; s < s1; ++s) {
-            float4 e4 = r4[s];
-            float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-            for (int q = 0; q < 4; ++q) {
-                if ((ev[q] >= 0.0f) && (__fmul_rn(ev[q], inv_sum) == pv)) {
-                    if (k == j) v->own = 4 * s + q - sh;
-                    ++k;
-                }
-            }
+__device__ __forceinline__ void write_result(const Ctx &c, int id, float p, int path, int n_cand,
+                                             int n_final, int consumed) {
+    if (threadIdx.x == 0) {
+        c.out_id[c.rowid] = id;
+        if (c.out_prob) c.out_prob[c.rowid] = p;
+        if (c.stats) {
+            bm_row_stats_t st;
+            st.path = path; st.n_cand = n_cand; st.n_final = n_final; st.consumed = consumed;
+            c.stats[c.rowid] = st;
         }
     }
-    __syncthreads();
-    int id = v->own;
-    __syncthreads();
-    return id;
 }
 
-// where the target lies relative to a window
-enum { W_INSIDE = 0, W_HIGH = 1, W_LOW = 2 };
-__device__ __forceinline__ int classify(const PassOut &o, int mode, double T, int m) {
-    if (mode == 2) {
-        if (m < o.cnt_above) return W_HIGH;
-        if (m >= o.cnt_above + o.in_cnt) return W_LOW;
-        return W_INSIDE;
-    }
-    bool hi = (mode == 0) ? (o.above >= T) : (o.above > T);
-    if (hi && o.cnt_above > 0) return W_HIGH;
-    double tot = o.above + o.in_mass;
-    bool reach = (mode == 0) ? (tot >= T) : (tot > T);
-    return reach ? W_INSIDE : W_LOW;
+// The penalised (and optionally temperature-scaled) logit of element e read
+// from global memory; used by the rare paths once the buffer is released.
+__device__ __forceinline__ float logit_g(const Ctx &c, int e, bool scale) {
+    float x = __ldg(c.g + e);
+    const int b = e + c.v->sh;
+    if (c.v->pen && ((c.bits[b >> 5] >> (b & 31)) & 1u)) x = penalize(x, c.v->penalty);
+    return scale ? __fmul_rn(x, c.v->inv_temp) : x;
 }
 
-// Sort the collected window and find the crossing inside it.  Returns 1 and
-// fills `out` on success; 0 when the walk disagrees with the pass sums.
-__device__ int finish_window(Ctx &c, unsigned long long *list, const PassOut &o, int mode,
-                             double T, int m, Sel &out) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    Vars *v = c.v;
-    const int n = o.in_cnt;
-    block_sort_u64(list, n, WCAP);
-    if (warp == 0) {
-        if (mode == 2) {
-            int j = m - o.cnt_above;
-            const int per = (j + 1 + 31) / 32;
-            const int bb = lane * per, ee = min(j + 1, bb + per);
-            double s = 0.0;
-            for (int q = bb; q < ee; ++q) s += (double)key_p(list[q]);
-            s = warp_sum(s);
-            if (lane == 0) { v->sel_found = 1; v->sel_j = j; v->cs = o.above + s; }
-        } else {
-            warp_walk(list, n, o.above, mode, T, v, lane);
-        }
-    }
-    __syncthreads();
-    int f = v->sel_found, j = v->sel_j;
-    double cs = v->cs;
-    __syncthreads();
-    if (!f) return 0;
-    unsigned long long kk = list[j];
-    out.found = 1;
-    out.pos = o.cnt_above + j;
-    out.id = key_id(kk);
-    out.p = key_p(kk);
-    out.cs = cs;
-    out.tie = (j > 0 && key_p(list[j - 1]) == out.p) || (j + 1 < n && key_p(list[j + 1]) == out.p);
-    __syncthreads();
-    return 1;
-}
-
-// The last candidate in canonical order (smallest p, then largest id) and
-// whether its probability is shared.
-__device__ Sel last_canon(Ctx &c) {
-    Vars *v = c.v;
-    const float inv_sum = v->inv_sum;
-    const int sh = v->sh, nslots = v->nslots;
-    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    float pmin = __int_as_float(0x7f800000);
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        float4 e4 = r4[s];
-        float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (ev[q] >= 0.0f) pmin = fminf(pmin, __fmul_rn(ev[q], inv_sum));
-    }
-    float dummy = 0.f;
-    block_maxmin_f(dummy, pmin, c.red);
-    int idmax = -1, cnt = 0;
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        float4 e4 = r4[s];
-        float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (ev[q] >= 0.0f && __fmul_rn(ev[q], inv_sum) == pmin) {
-                idmax = max(idmax, 4 * s + q - sh);
-                ++cnt;
-            }
-    }
-    idmax = block_max_i(idmax, c.red);
-    cnt = block_sum_i(cnt, c.red);
-    Sel out;
-    out.found = 0;
-    out.pos = v->n_cand - 1;
-    out.id = idmax;
-    out.p = pmin;
-    out.cs = 0.0;
-    out.tie = cnt > 1;
-    return out;
-}
-
-// mode 0: first position with cs >= T; mode 1: cs > T; mode 2: position m.
-// Window estimate from the count histogram, verified by exact passes,
-// widened on a miss, bisected in probability when too dense.
-__device__ Sel select_canon(Ctx &c, int mode, double T, int m) {
-    Vars *v = c.v;
-    const uint32_t *hcnt = reinterpret_cast<const uint32_t *>(c.scr);
-    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
-    const float inv_sum = v->inv_sum, w = v->w;
-    const int n_cand = v->n_cand;
-    const float PINF = __int_as_float(0x7f800000);
-    Sel out;
-    out.found = 0; out.pos = n_cand - 1; out.id = -1; out.p = 0.f; out.cs = 0.0; out.tie = 0;
-
-    // 1. estimate the crossing bucket from counts x bucket-centre probability
-    const int b0 = 2 * threadIdx.x, b1 = b0 + 1;
-    const int c0 = (int)hcnt[b0], c1 = (int)hcnt[b1];
-    const double m0 = (double)c0 * (double)__fmul_rn(expf(-(float)b0 * w), inv_sum);
-    const double m1 = (double)c1 * (double)__fmul_rn(expf(-(float)b1 * w), inv_sum);
-    double mt;
-    const double mex = block_xscan_d(m0 + m1, mt, c.red);
-    int ct;
-    const int cex = block_xscan_i(c0 + c1, ct, c.red);
-    if (threadIdx.x == 0) v->bhat = NB - 1;
-    __syncthreads();
-    int hitb = INT_MAX;
-    if (mode == 2) {
-        if (m >= cex && m < cex + c0) hitb = b0;
-        else if (m >= cex + c0 && m < cex + c0 + c1) hitb = b1;
-    } else {
-        bool h0 = (mode == 0) ? (mex + m0 >= T) : (mex + m0 > T);
-        bool h1 = (mode == 0) ? (mex + m0 + m1 >= T) : (mex + m0 + m1 > T);
-        if (h0) hitb = b0;
-        else if (h1) hitb = b1;
-    }
-    if (hitb != INT_MAX) atomicMin(&v->bhat, hitb);
-    __syncthreads();
-    const int bh = v->bhat;
-    __syncthreads();
-
-    // 2. windows around the estimate, widening on a miss; [lo, hi] is the
-    //    probability interval the crossing is known to lie in
-    float lo = -1.0f, hi = PINF;
-    const int deltas[3] = {0, 2, 16};
-    PassOut o;
-    bool dense = false;
-    for (int a = 0; a < 3; ++a) {
-        const int blo = max(0, bh - deltas[a]), bhi = min(NB - 1, bh + deltas[a]);
-        float phi = (blo == 0) ? PINF : __fmul_rn(expf(-((float)blo - 0.5f) * w), inv_sum);
-        float plo = (bhi == NB - 1) ? -1.0f : __fmul_rn(expf(-((float)bhi + 0.5f) * w), inv_sum);
-        phi = fminf(phi, hi);
-        plo = fmaxf(plo, lo);
-        o = exact_pass(c, plo, phi, list);
-        int cl = classify(o, mode, T, m);
-        if (cl == W_INSIDE) {
-            lo = plo; hi = phi;
-            if (o.in_cnt <= WCAP) {
-                if (finish_window(c, list, o, mode, T, m, out)) return out;
-            } else {
-                dense = true;
-                break;
-            }
-        } else if (cl == W_HIGH) {
-            lo = __uint_as_float(__float_as_uint(phi) + 1u);  // p > phi
-        } else {
-            if (plo <= 0.0f) {
-                // nothing below the window: the target lies beyond the last
-                // candidate (total mass under the target)
-                out = last_canon(c);
-                out.found = 0;
-                out.cs = o.above + o.in_mass;
-                return out;
-            }
-            hi = __uint_as_float(__float_as_uint(plo) - 1u);  // p < plo
-            if (hi < 0.0f) hi = 0.0f;
-        }
-    }
-    // 3. bisection on the probability bits of [lo, hi]
-    (void)dense;
-    for (int it = 0; it < 64; ++it) {
-        unsigned ub = (hi == PINF) ? 0x3f800001u : __float_as_uint(hi);
-        unsigned lb = (lo < 0.0f) ? 0u : __float_as_uint(lo);
-        if (ub > 0x3f800001u) ub = 0x3f800001u;
-        if (lb > ub) lb = ub;
-        o = exact_pass(c, (lo < 0.0f) ? -1.0f : __uint_as_float(lb), __uint_as_float(ub), list);
-        int cl = classify(o, mode, T, m);
-        if (cl == W_INSIDE && o.in_cnt <= WCAP) {
-            if (finish_window(c, list, o, mode, T, m, out)) return out;
-        }
-        if (cl == W_LOW && lb == 0u) {
-            out = last_canon(c);
-            out.found = 0;
-            out.cs = o.above + o.in_mass;
-            return out;
-        }
-        if (cl != W_INSIDE) {
-            // the estimate drifted outside [lo, hi]; reopen the interval
-            if (cl == W_HIGH) { lo = __uint_as_float(ub + 1u); hi = PINF; }
-            else { hi = (lb == 0u) ? 0.0f : __uint_as_float(lb - 1u); lo = -1.0f; }
-            continue;
-        }
-        if (lb == ub) {
-            // more than WCAP candidates share one probability value: the
-            // position inside the tie group is arithmetic, then the j-th id
-            const float pv = __uint_as_float(ub);
-            const int n = o.in_cnt;
-            int j;
-            if (mode == 2) {
-                j = m - o.cnt_above;
-            } else {
-                j = 0;
-                while (j < n - 1 && !((mode == 0) ? (o.above + (double)(j + 1) * pv >= T)
-                                                  : (o.above + (double)(j + 1) * pv > T))) {
-                    double need = (T - o.above) / (double)pv;
-                    int jj = (int)need - 1;
-                    j = (jj > j) ? jj : j + 1;
-                    if (j > n - 1) j = n - 1;
-                }
-            }
-            out.found = 1;
-            out.pos = o.cnt_above + j;
-            out.p = pv;
-            out.cs = o.above + (double)(j + 1) * pv;
-            out.tie = (n > 1);
-            out.id = ordered_pick(c, pv, j);
-            return out;
-        }
-        const unsigned mid = lb + (ub - lb) / 2;
-        // upper half (mid, ub]
-        PassOut u = exact_pass(c, __uint_as_float(mid + 1u), __uint_as_float(ub), list);
-        int cu = classify(u, mode, T, m);
-        if (cu == W_INSIDE) {
-            lo = __uint_as_float(mid + 1u);
-            hi = __uint_as_float(ub);
-            if (u.in_cnt <= WCAP && finish_window(c, list, u, mode, T, m, out)) return out;
-        } else {
-            lo = (lb == 0u && lo < 0.0f) ? -1.0f : __uint_as_float(lb);
-            hi = __uint_as_float(mid);
-        }
-    }
-    if (threadIdx.x == 0) atomicOr(c.P.err, 2);
-    return out;
-}
-
-// Exact replay of the reference's top-256 heap (src/model.c:327-356) over the
-// candidates in id order, by one warp: heapify the first 256, then replace
-// the root by every later candidate that is strictly greater.  The result is
-// left in `outk` sorted as the stable qsort leaves it: probability
-// descending, ties in heap-array order (low word = heap slot).
-__device__ __noinline__ void replay_top256(Ctx &c, unsigned long long *outk, float *hv,
-                                           int *hi) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    Vars *v = c.v;
-    const float inv_sum = v->inv_sum;
-    const int sh = v->sh, V = c.P.V;
-    if (warp == 0) {
-        int filled = 0;
-        for (int base = 0; base < V; base += 32) {
-            const int id = base + lane;
-            const float e = (id < V) ? c.row[id + sh] : -1.0f;
-            const bool cand = e >= 0.0f;
-            const float p = __fmul_rn(cand ? e : 0.0f, inv_sum);
-            const unsigned mk = __ballot_sync(FULL, cand);
-            bool rest = cand;
-            if (filled < 256) {
-                const int rank = __popc(mk & ((1u << lane) - 1));
-                const int take = min(__popc(mk), 256 - filled);
-                if (cand && rank < take) { hv[filled + rank] = p; hi[filled + rank] = id; }
-                rest = cand && rank >= take;
-                filled += take;
-                __syncwarp();
-                if (filled < 256) continue;
-                if (filled - take < 256 && take > 0) warp_heapify(hv, hi, 256, lane);
-            }
-            const float root = hv[0];
-            unsigned mr = __ballot_sync(FULL, rest && p > root);
-            while (mr) {
-                const int src = __ffs(mr) - 1;
-                const float pb = __shfl_sync(FULL, p, src);
-                const int ib = __shfl_sync(FULL, id, src);
-                if (lane == 0 && pb > hv[0]) { hv[0] = pb; hi[0] = ib; heap_down(hv, hi, 256, 0); }
-                __syncwarp();
-                mr &= mr - 1;
-            }
-        }
-        __syncwarp();
-        for (int q = lane; q < 256; q += 32) outk[q] = canon_key(hv[q], q);
-    }
-    __syncthreads();
-    block_sort_u64(outk, 256, 256);
-}
-
-// ------------------------------------------------------------ row passes --
-// Pass 1: consume the freshly loaded row (waiting chunk by chunk), apply the
-// penalty bitset, and reduce.  greedy: argmax of raw penalised logits.
-__device__ void load_pass(Ctx &c, bool greedy, float &mx, float &xmin, float &gv, int &gi) {
+// ------------------------------------------------------------ load pass --
+// Consume the freshly loaded row chunk by chunk: apply the penalty, fill the
+// junk lanes of the ragged first / last slots with NaN, and reduce.
+template <bool GREEDY, bool PEN, bool SCALE>
+__device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float &gv, int &gi) {
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots, s0 = v->s_int0, s1 = v->s_int1;
-    const int V = c.P.V;
-    const bool pen = v->pen != 0;
+    const int V = c.V;
     const float penalty = v->penalty, inv_temp = v->inv_temp;
-    const bool scale = (inv_temp != 1.0f);
-    const int nint = s1 - s0;
-    unsigned waited = 0;
     float4 *r4 = reinterpret_cast<float4 *>(c.row);
+    const float QNAN = __int_as_float(0x7fc00000);
     mx = -1e30f;
-    xmin = __int_as_float(0x7f800000);
+    xmin = PINF;
     gv = -1e9f;
     gi = INT_MAX;
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        float4 x;
-        if (s >= s0 && s < s1) {
-            int j = s - s0;
-            int ch = (j * NCHUNK) / nint;
-            if (((ch + 1) * nint) / NCHUNK <= j) ++ch;
-            if (!((waited >> ch) & 1u)) {
-                if (!mbar_wait(&c.mbar[ch], c.parity)) {
-                    atomicOr(c.P.err, 1);
-                    v->fail = 1;
-                }
-                waited |= 1u << ch;
-            }
-            x = r4[s];
-        } else {
-            float t[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                int e = 4 * s + q - sh;
-                t[q] = (e >= 0 && e < V) ? __ldg(c.g + e) : 0.0f;
-            }
-            x = make_float4(t[0], t[1], t[2], t[3]);
-            r4[s] = x;
-        }
+    auto consume = [&](int s, float4 x) {
         float t[4] = {x.x, x.y, x.z, x.w};
-        if (pen) {
-            unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
+        if (PEN) {
+            const unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
             if (nib) {
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
@@ -845,93 +554,136 @@ __device__ void load_pass(Ctx &c, bool greedy, float &mx, float &xmin, float &gv
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            int e = 4 * s + q - sh;
-            if (e < 0 || e >= V) continue;
-            if (greedy) {
-                if (t[q] > gv) { gv = t[q]; gi = e; }
+            if (GREEDY) {
+                if (t[q] > gv) { gv = t[q]; gi = 4 * s + q - sh; }
             } else {
-                float l = scale ? __fmul_rn(t[q], inv_temp) : t[q];
+                const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
                 mx = fmaxf(mx, l);
                 xmin = fminf(xmin, l);
             }
         }
+    };
+    auto plain = [&](int s) {
+        float t[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int e = 4 * s + q - sh;
+            t[q] = (e >= 0 && e < V) ? __ldg(c.g + e) : QNAN;
+        }
+        const float4 x = make_float4(t[0], t[1], t[2], t[3]);
+        r4[s] = x;
+        consume(s, x);
+    };
+    // plain head slot(s): junk lanes NaN (all slots when the row is tiny)
+    for (int s = threadIdx.x; s < s0; s += NT) plain(s);
+    // interior, chunk by chunk
+    const int nint = s1 - s0;
+    if (nint > 0) {
+        for (int ch = 0; ch < NCHUNK; ++ch) {
+            const int a = s0 + (ch * nint) / NCHUNK, b = s0 + ((ch + 1) * nint) / NCHUNK;
+            int s = a + ((int)threadIdx.x - a % NT + NT) % NT;
+            if (s >= b) continue;
+            if (!mbar_wait(&c.mbar[ch], c.parity)) {
+                atomicOr(c.err, 1);
+                v->fail = 1;
+                return;
+            }
+            for (; s < b; s += NT) consume(s, r4[s]);
+        }
     }
+    for (int s = max(s1, s0) + (int)threadIdx.x; s < nslots; s += NT) plain(s);
 }
 
-// Argmax over the scaled (penalised) logits with the guard semantics of
-// src/model.c:227-237 and 296-303: start from element 0, strict '>'.
-// Reloads from global memory (the row buffer may hold probabilities).
-__device__ int guard_argmax(Ctx &c) {
-    Vars *v = c.v;
-    const int V = c.P.V;
-    const bool pen = v->pen != 0;
-    const float penalty = v->penalty, inv_temp = v->inv_temp;
-    const bool scale = (inv_temp != 1.0f);
-    const int sh = v->sh;
+// Argmax over the scaled penalised logits with the guard semantics of
+// src/model.c:227-237 and 296-303 (start from element 0, strict '>'),
+// read from global memory.
+__device__ __noinline__ int guard_argmax(Ctx c) {
+    c.attach();
+    const int V = c.V;
+    const bool scale = (c.v->inv_temp != 1.0f);
     float bv = 0.f;
     int bi = INT_MAX;
     for (int e = threadIdx.x; e < V; e += NT) {
-        float x = __ldg(c.g + e);
-        int s = (e + sh) >> 2, q = (e + sh) & 3;
-        if (pen && ((c.bits[s >> 3] >> ((s & 7) * 4 + q)) & 1u)) x = penalize(x, penalty);
-        float l = scale ? __fmul_rn(x, inv_temp) : x;
+        const float l = logit_g(c, e, scale);
         if (l == l) argmax_combine(bv, bi, l, e);
     }
     block_argmax(bv, bi, c.red);
-    float l0 = __ldg(c.g);
-    {
-        int s = sh >> 2, q = sh & 3;
-        if (pen && ((c.bits[s >> 3] >> ((s & 7) * 4 + q)) & 1u)) l0 = penalize(l0, penalty);
-    }
-    l0 = scale ? __fmul_rn(l0, inv_temp) : l0;
+    const float l0 = logit_g(c, 0, scale);
     if (l0 != l0 || bi == INT_MAX) return 0;
     return bi;
 }
 
-__device__ void write_result(Ctx &c, int id, float p, int path, int n_cand, int n_final,
-                             int consumed) {
-    if (threadIdx.x == 0) {
-        c.P.out_id[c.rowid] = id;
-        if (c.P.out_prob) c.P.out_prob[c.rowid] = p;
-        if (c.P.stats) {
-            bm_row_stats_t st;
-            st.path = path; st.n_cand = n_cand; st.n_final = n_final; st.consumed = consumed;
-            c.P.stats[c.rowid] = st;
-        }
-    }
-}
-
 // ---------------------------------------------------------------- top_k --
-__device__ void topk_path(Ctx &c) {
+template <bool SCALE>
+__device__ __forceinline__ void topk_path(Ctx &c) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     Vars *v = c.v;
-    const int sh = v->sh, nslots = v->nslots, V = c.P.V, k = v->k;
+    const int sh = v->sh, nslots = v->nslots, V = c.V, k = v->k;
     const float mx = v->mx, thr = v->thr, inv_temp = v->inv_temp;
-    const bool scale = (inv_temp != 1.0f);
     const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    uint32_t *kh = reinterpret_cast<uint32_t *>(c.scr);                       // 8 x 128
+    uint32_t *kh = reinterpret_cast<uint32_t *>(c.scr);                            // 8 x 128
     unsigned long long *kc = reinterpret_cast<unsigned long long *>(c.scr + 4096);  // KCAP
     const float bscale = __fdiv_rn(127.0f, 20.0f);  // src/model.c:184
+    // collect the candidates above the min_p threshold while counting, when
+    // that threshold is a real one (otherwise every logit passes it)
+    const bool collect = v->min_p > 0.0f;
 
     for (int i = threadIdx.x; i < 8 * HB; i += NT) kh[i] = 0;
     if (threadIdx.x == 0) v->kcnt = 0;
     __syncthreads();
+    uint32_t *myh = kh + (warp & 7) * HB;
+    unsigned long long lo8 = 0, hi8 = 0;  // per-thread counts of buckets 0..15
+    bool full = false;  // this warp stopped collecting: the list overflowed
     // histogram of (max - l) over l >= thr (src/model.c:185-195); the last
     // bucket never decides the cut, so it is not counted
-    uint32_t *myh = kh + (warp & 7) * HB;
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        float4 x = r4[s];
-        float t[4] = {x.x, x.y, x.z, x.w};
+    for (int base = warp * 32; base < nslots; base += NT) {
+        const int s = base + lane;
+        if (collect && !full) full = *(volatile int *)&v->kcnt > KCAP;
+        float4 x = make_float4(-PINF, -PINF, -PINF, -PINF);
+        if (s < nslots) x = r4[s];
+        const float t[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            int e = 4 * s + q - sh;
-            if (e < 0 || e >= V) continue;
-            float l = scale ? __fmul_rn(t[q], inv_temp) : t[q];
-            if (l >= thr) {
+            const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
+            const bool ok = (l >= thr);
+            if (ok) {
                 int b = x86_cvtt(__fmul_rn(__fsub_rn(mx, l), bscale));
                 b = min(max(b, 0), HB - 1);
-                if (b < HB - 1) atomicAdd(&myh[b], 1u);
+                // buckets 0..15 (where the cut of a top_k <= 256 nearly always
+                // lies, and where flat rows pile up) in 8-bit register fields
+                if (b < 8) lo8 += 1ull << (8 * b);
+                else if (b < 16) hi8 += 1ull << (8 * (b - 8));
+                else if (b < HB - 1) atomicAdd(&myh[b], 1u);
             }
+            if (collect) {
+                const unsigned m = __ballot_sync(FULL, ok && !full);
+                if (m) {
+                    const int leader = __ffs(m) - 1;
+                    int bpos = 0;
+                    if (lane == leader) bpos = atomicAdd(&v->kcnt, __popc(m));
+                    bpos = __shfl_sync(FULL, bpos, leader);
+                    if (ok) {
+                        const int pos = bpos + __popc(m & ((1u << lane) - 1));
+                        if (pos < KCAP)
+                            kc[pos] = ((unsigned long long)(unsigned)(4 * s + q - sh) << 32) |
+                                      __float_as_uint(l);
+                    }
+                }
+            }
+        }
+    }
+    {
+        // widen the 8-bit fields to 16 bits (a warp holds at most 32 * 100
+        // per bucket), sum over the warp, add 16 counts to the histogram
+        const unsigned long long M = 0x00ff00ff00ff00ffull;
+        unsigned long long f[4] = {lo8 & M, (lo8 >> 8) & M, hi8 & M, (hi8 >> 8) & M};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = warp_sum(f[j]);
+        if (lane < 16) {
+            const int j = lane >> 3, q = lane & 7;  // bucket = 8j + q
+            const unsigned long long fw = f[2 * j + (q & 1)];
+            const unsigned cnt = (unsigned)((fw >> (16 * (q >> 1))) & 0xffffu);
+            if (cnt) atomicAdd(&kh[lane], cnt);
         }
     }
     __syncthreads();
@@ -946,7 +698,7 @@ __device__ void topk_path(Ctx &c) {
             cq[q] = s;
             ls += s;
         }
-        uint32_t inc = warp_iscan(ls, lane);
+        const uint32_t inc = warp_iscan(ls, lane);
         uint32_t run = inc - ls;
         int hit = INT_MAX;
 #pragma unroll
@@ -961,50 +713,68 @@ __device__ void topk_path(Ctx &c) {
     const int cut = v->kcut;
     const float bthr = __fsub_rn(mx, __fdiv_rn((float)(cut + 1), bscale));  // src/model.c:210-211
     const float ethr = bthr > thr ? bthr : thr;                          // src/model.c:213-214
-    // extraction (src/model.c:217-224), unordered here, ordered by id below
-    for (int base = warp * 32; base < nslots; base += NT) {
-        int s = base + lane;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (s < nslots) x = r4[s];
-        float t[4] = {x.x, x.y, x.z, x.w};
+    const int collected = v->kcnt;
+    __syncthreads();
+    if (collect && collected <= KCAP) {
+        // the extraction set is the collected set filtered by ethr >= thr
+        unsigned long long mine[(KCAP + NT - 1) / NT];
+        int nm = 0;
+        for (int i = threadIdx.x; i < collected; i += NT) {
+            const unsigned long long kk = kc[i];
+            if (__uint_as_float((unsigned)(kk & 0xffffffffu)) >= ethr) mine[nm++] = kk;
+        }
+        if (threadIdx.x == 0) v->kcnt = 0;
+        __syncthreads();
+        for (int i = 0; i < nm; ++i) kc[atomicAdd(&v->kcnt, 1)] = mine[i];
+        __syncthreads();
+    } else {
+        // extraction pass (src/model.c:217-224), unordered here
+        if (threadIdx.x == 0) v->kcnt = 0;
+        __syncthreads();
+        for (int base = warp * 32; base < nslots; base += NT) {
+            const int s = base + lane;
+            float4 x = make_float4(-PINF, -PINF, -PINF, -PINF);
+            if (s < nslots) x = r4[s];
+            const float t[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            int e = 4 * s + q - sh;
-            bool ok = false;
-            float l = 0.f;
-            if (s < nslots && e >= 0 && e < V) {
-                l = scale ? __fmul_rn(t[q], inv_temp) : t[q];
-                ok = (l >= ethr);
-            }
-            unsigned m = __ballot_sync(FULL, ok);
-            if (m) {
-                int leader = __ffs(m) - 1, bpos = 0;
-                if (lane == leader) bpos = atomicAdd(&v->kcnt, __popc(m));
-                bpos = __shfl_sync(FULL, bpos, leader);
-                if (ok) {
-                    int pos = bpos + __popc(m & ((1u << lane) - 1));
-                    if (pos < KCAP)
-                        kc[pos] = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
+            for (int q = 0; q < 4; ++q) {
+                const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
+                const bool ok = (l >= ethr);
+                const unsigned m = __ballot_sync(FULL, ok);
+                if (m) {
+                    const int leader = __ffs(m) - 1;
+                    int bpos = 0;
+                    if (lane == leader) bpos = atomicAdd(&v->kcnt, __popc(m));
+                    bpos = __shfl_sync(FULL, bpos, leader);
+                    if (ok) {
+                        const int pos = bpos + __popc(m & ((1u << lane) - 1));
+                        if (pos < KCAP)
+                            kc[pos] = ((unsigned long long)(unsigned)(4 * s + q - sh) << 32) |
+                                      __float_as_uint(l);
+                    }
                 }
             }
         }
+        __syncthreads();
     }
-    __syncthreads();
     const int n = v->kcnt;
+    // the buffer is no longer needed: the rest works on the candidate list
+    // (or re-reads global memory on the rare overflow / guard paths)
+    release_row(c);
     if (n == 0) {  // argmax guard (src/model.c:227-237)
-        int id = guard_argmax(c);
+        const int id = guard_argmax(c);
         write_result(c, id, 1.0f, 2, 0, 0, 0);
         return;
     }
-    float *hv = reinterpret_cast<float *>(c.scr);            // 256 (reuses histogram)
-    int *hi = reinterpret_cast<int *>(c.scr + 1024);         // 256
-    float *pv = reinterpret_cast<float *>(c.scr + 2048);     // 256: probabilities
-    int *rk = reinterpret_cast<int *>(c.scr + 3072);         // 256: ranks
-    int ns;  // survivors
+    float *hv = reinterpret_cast<float *>(c.scr);         // 256 (reuses the histogram)
+    int *hi = reinterpret_cast<int *>(c.scr + 1024);      // 256
+    float *pv = reinterpret_cast<float *>(c.scr + 2048);  // 256 probabilities
+    int *rk = reinterpret_cast<int *>(c.scr + 3072);      // 256 ranks
     if (n <= KCAP) {
-        block_sort_u64(kc, n, KCAP);  // by id (ids are unique)
+        // by id (ids are unique); ranks up to NT in the histogram area
+        sort_keys(kc, n, reinterpret_cast<int *>(c.scr), KCAP);
         if (warp == 0) {
-            int first = min(n, k);
+            const int first = min(n, k);
             for (int q = lane; q < first; q += 32) {
                 hv[q] = __uint_as_float((unsigned)(kc[q] & 0xffffffffu));
                 hi[q] = (int)(kc[q] >> 32);
@@ -1013,16 +783,19 @@ __device__ void topk_path(Ctx &c) {
             if (n > k) {  // heap top-k (src/model.c:240-254)
                 warp_heapify(hv, hi, k, lane);
                 for (int base = k; base < n; base += 32) {
-                    int j = base + lane;
+                    const int j = base + lane;
                     float val = 0.f;
                     int id = 0;
-                    if (j < n) { val = __uint_as_float((unsigned)(kc[j] & 0xffffffffu)); id = (int)(kc[j] >> 32); }
-                    float root = hv[0];
+                    if (j < n) {
+                        val = __uint_as_float((unsigned)(kc[j] & 0xffffffffu));
+                        id = (int)(kc[j] >> 32);
+                    }
+                    const float root = hv[0];
                     unsigned mr = __ballot_sync(FULL, j < n && val > root);
                     while (mr) {
-                        int src = __ffs(mr) - 1;
-                        float vb = __shfl_sync(FULL, val, src);
-                        int ib = __shfl_sync(FULL, id, src);
+                        const int src = __ffs(mr) - 1;
+                        const float vb = __shfl_sync(FULL, val, src);
+                        const int ib = __shfl_sync(FULL, id, src);
                         if (lane == 0 && vb > hv[0]) { hv[0] = vb; hi[0] = ib; heap_down(hv, hi, k, 0); }
                         __syncwarp();
                         mr &= mr - 1;
@@ -1031,8 +804,8 @@ __device__ void topk_path(Ctx &c) {
             }
         }
     } else {
-        // more candidates than the list holds: stream them in id order
-        // straight from the row buffer through the same heap rules
+        // more candidates than the list holds: stream them in id order from
+        // global memory through the same heap rules
         if (warp == 0) {
             int filled = 0;
             for (int base = 0; base < V; base += 32) {
@@ -1040,8 +813,7 @@ __device__ void topk_path(Ctx &c) {
                 float l = 0.f;
                 bool ok = false;
                 if (e < V) {
-                    const float x = c.row[e + sh];
-                    l = scale ? __fmul_rn(x, inv_temp) : x;
+                    l = logit_g(c, e, SCALE);
                     ok = (l >= ethr);
                 }
                 const unsigned mk = __ballot_sync(FULL, ok);
@@ -1069,7 +841,7 @@ __device__ void topk_path(Ctx &c) {
             }
         }
     }
-    ns = min(n, k);
+    const int ns = min(n, k);
     __syncthreads();
     // survivor softmax (src/model.c:257-269), warp 0, <= 8 per lane in order
     if (warp == 0) {
@@ -1077,17 +849,17 @@ __device__ void topk_path(Ctx &c) {
         float lm = -1e30f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            int j = lane * 8 + q;
+            const int j = lane * 8 + q;
             val[q] = (j < ns) ? hv[j] : -1e30f;
             if (j < ns) lm = fmaxf(lm, val[q]);
         }
         lm = warp_max(lm);
         float ev[8];
         double s = 0.0;
-        float emin = __int_as_float(0x7f800000);
+        float emin = PINF;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            int j = lane * 8 + q;
+            const int j = lane * 8 + q;
             ev[q] = (j < ns) ? expf(__fsub_rn(val[q], lm)) : 0.0f;
             s += (double)ev[q];
             if (j < ns && ev[q] > 0.0f) emin = fminf(emin, ev[q]);
@@ -1101,10 +873,10 @@ __device__ void topk_path(Ctx &c) {
             for (int j = 0; j < ns; ++j) q0 += (double)__shfl_sync(FULL, ev[j & 7], j >> 3);
             S = q0;
         }
-        float inv = __fdiv_rn(1.0f, __double2float_rn(S));
+        const float inv = __fdiv_rn(1.0f, __double2float_rn(S));
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            int j = lane * 8 + q;
+            const int j = lane * 8 + q;
             if (j < ns) pv[j] = __fmul_rn(ev[q], inv);
         }
         if (lane == 0) v->S = S;
@@ -1117,19 +889,19 @@ __device__ void topk_path(Ctx &c) {
         return;
     }
     // stable descending sort when top_p < 1 (src/model.c:275-276)
-    unsigned long long *srt = kc;  // reuse
+    unsigned long long *srt = kc;
     if (top_p < 1.0f) {
         for (int j = threadIdx.x; j < ns; j += NT) rk[j] = 0;
         __syncthreads();
-        int G = NT / ns;  // >= 4
-        if (threadIdx.x < G * ns) {
-            int j = threadIdx.x % ns, g = threadIdx.x / ns;
-            int per = (ns + G - 1) / G;
-            int a = g * per, b = min(ns, a + per);
-            float pj = pv[j];
+        const int G = NT / ns;
+        if ((int)threadIdx.x < G * ns) {
+            const int j = threadIdx.x % ns, g = threadIdx.x / ns;
+            const int per = (ns + G - 1) / G;
+            const int a = g * per, b = min(ns, a + per);
+            const float pj = pv[j];
             int r = 0;
             for (int i = a; i < b; ++i) {
-                float pi = pv[i];
+                const float pi = pv[i];
                 r += (pi > pj) || (pi == pj && i < j);
             }
             if (r) atomicAdd(&rk[j], r);
@@ -1146,30 +918,28 @@ __device__ void topk_path(Ctx &c) {
     if (warp == 0) {
         const int per = (ns + 31) / 32;
         const int b = lane * per, e = min(ns, b + per);
-        float pmin = __int_as_float(0x7f800000);
+        float pmin = PINF;
         double ls = 0.0;
         for (int j = b; j < e; ++j) {
-            float p = __uint_as_float((unsigned)(srt[j] & 0xffffffffu));
+            const float p = __uint_as_float((unsigned)(srt[j] & 0xffffffffu));
             ls += (double)p;
             if (p > 0.0f) pmin = fminf(pmin, p);
         }
         pmin = warp_min(pmin);
-        double inc = warp_iscan(ls, lane);
-        double pre = inc - ls;
-        bool exact = (pmin >= 0x1p-29f);
-        // nucleus cut: first j with cs_j >= top_p
+        const double inc = warp_iscan(ls, lane);
+        const double pre = inc - ls;
+        const bool exact = (pmin >= 0x1p-29f);
         int nf = ns;
         double cs_cut = __shfl_sync(FULL, inc, 31);
         if (top_p < 1.0f) {
-            int hit = INT_MAX;
-            double hcs = 0.0;
             if (exact) {
-                double cs = pre;
+                int hit = INT_MAX;
+                double hcs = 0.0, cs = pre;
                 for (int j = b; j < e; ++j) {
                     cs += (double)__uint_as_float((unsigned)(srt[j] & 0xffffffffu));
                     if (cs >= (double)top_p) { hit = j; hcs = cs; break; }
                 }
-                int best = warp_imin(hit);
+                const int best = warp_imin(hit);
                 if (best != INT_MAX) {
                     hcs = __shfl_sync(FULL, hcs, best / per);
                     nf = best + 1;
@@ -1184,9 +954,7 @@ __device__ void topk_path(Ctx &c) {
                 cs_cut = cs;
             }
         }
-        // renormalise and draw: r = u * (float)new_sum, first j with r < cdf_j
-        const double new_sum = cs_cut;
-        const float r = __fmul_rn(v->u, __double2float_rn(new_sum));
+        const float r = __fmul_rn(v->u, __double2float_rn(cs_cut));
         int pos = nf - 1;
         if (exact) {
             int hit = INT_MAX;
@@ -1195,7 +963,7 @@ __device__ void topk_path(Ctx &c) {
                 cs += (double)__uint_as_float((unsigned)(srt[j] & 0xffffffffu));
                 if ((double)r < cs) { hit = j; break; }
             }
-            int best = warp_imin(hit);
+            const int best = warp_imin(hit);
             if (best != INT_MAX) pos = best;
         } else {
             double cs = 0.0;
@@ -1205,7 +973,7 @@ __device__ void topk_path(Ctx &c) {
             }
         }
         if (lane == 0) {
-            unsigned long long kk = srt[pos];
+            const unsigned long long kk = srt[pos];
             v->res_id = (int)(kk >> 32);
             v->res_p = __uint_as_float((unsigned)(kk & 0xffffffffu));
             v->n_final = nf;
@@ -1216,15 +984,510 @@ __device__ void topk_path(Ctx &c) {
 }
 
 // ------------------------------------------------------ full vocabulary --
-__device__ void full_path(Ctx &c) {
+// Selection targets in canonical order (p desc, id asc).
+enum { T_MASS_GE = 0, T_MASS_GT = 1, T_POS = 2 };
+
+struct Sel {
+    int found;  // 1 = crossing found; 0 = beyond the last candidate
+    int pos;    // position in canonical order (0-based)
+    int id;
+    float p;
+    double cs;  // cumulative mass through `pos`
+    int tie;    // another candidate has the same p
+};
+
+struct PassOut {
+    double above, in_mass;
+    int cnt_above, in_cnt;
+};
+
+// e of element `e` recomputed from global memory (bit-identical to the exp
+// pass): -0 for non-candidates.
+__device__ __forceinline__ float e_global(const Ctx &c, int e, bool scale) {
+    const float l = logit_g(c, e, scale);
+    if (!(l >= c.v->thr)) return -0.0f;
+    return exp_one(__fsub_rn(l, c.v->mx));
+}
+
+// One exact pass over global memory (rare paths): mass / count above phi,
+// mass / count inside [plo, phi], inside elements appended to `list`.
+__device__ __forceinline__ PassOut exact_pass_g(Ctx &c, bool scale, float plo, float phi,
+                                                unsigned long long *list, int cap) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     Vars *v = c.v;
-    const int sh = v->sh, nslots = v->nslots, V = c.P.V;
+    const float inv_sum = v->inv_sum;
+    const int V = c.V;
+    if (threadIdx.x == 0) v->ln3 = 0;
+    __syncthreads();
+    double au = 0.0, ai = 0.0;
+    int cu = 0, ci = 0;
+    for (int base = warp * 32; base < V; base += NT) {
+        const int e = base + lane;
+        float p = -0.0f;
+        if (e < V) p = __fmul_rn(e_global(c, e, scale), inv_sum);
+        const int pb = __float_as_int(p);
+        const bool up = pb > __float_as_int(phi);
+        const bool in = !up && pb >= __float_as_int(plo);
+        au += up ? (double)p : 0.0;
+        ai += in ? (double)p : 0.0;
+        cu += up;
+        ci += in;
+        const unsigned m = __ballot_sync(FULL, in);
+        if (m) {
+            const int leader = __ffs(m) - 1;
+            int bpos = 0;
+            if (lane == leader) bpos = atomicAdd(&v->ln3, __popc(m));
+            bpos = __shfl_sync(FULL, bpos, leader);
+            if (in) {
+                const int pos = bpos + __popc(m & ((1u << lane) - 1));
+                if (pos < cap) list[pos] = canon_key(p, e);
+            }
+        }
+    }
+    PassOut o;
+    o.above = au;
+    o.in_mass = ai;
+    o.cnt_above = cu;
+    o.in_cnt = ci;
+    block_sum4(o.above, o.in_mass, o.cnt_above, o.in_cnt, c.red);
+    return o;
+}
+
+// Walk a sorted key list from a starting mass, on one warp: first j with
+// start + cum(j) >= T (mode 0), > T (mode 1), or j == j2 (mode 2).
+__device__ __forceinline__ void warp_walk(const unsigned long long *keys, int n, double start,
+                                          int mode, double T, int j2, Vars *v, int lane) {
+    const int per = (n + 31) / 32;
+    const int b = lane * per, e = min(n, b + per);
+    double s = 0.0;
+    for (int j = b; j < e; ++j) s += (double)key_p(keys[j]);
+    const double inc = warp_iscan(s, lane);
+    const double pre = start + (inc - s);
+    int hit = INT_MAX;
+    double hit_cs = 0.0;
+    double cs = pre;
+    for (int j = b; j < e; ++j) {
+        cs += (double)key_p(keys[j]);
+        const bool ok = (mode == T_MASS_GE) ? (cs >= T) : (mode == T_MASS_GT) ? (cs > T) : (j == j2);
+        if (ok) { hit = j; hit_cs = cs; break; }
+    }
+    const int best = warp_imin(hit);
+    if (best != INT_MAX) {
+        const double hcs = __shfl_sync(FULL, hit_cs, best / per);
+        if (lane == 0) { v->sel_found = 1; v->sel_j = best; v->cs = hcs; }
+    } else {
+        const double tot = __shfl_sync(FULL, inc, 31);
+        if (lane == 0) { v->sel_found = 0; v->sel_j = n; v->cs = start + tot; }
+    }
+}
+
+__device__ __forceinline__ int classify(const PassOut &o, int mode, double T, int m) {
+    // 0 inside, 1 above the window, 2 below it
+    if (mode == T_POS) {
+        if (m < o.cnt_above) return 1;
+        if (m >= o.cnt_above + o.in_cnt) return 2;
+        return 0;
+    }
+    const bool hi = (mode == T_MASS_GE) ? (o.above >= T) : (o.above > T);
+    if (hi && o.cnt_above > 0) return 1;
+    const double tot = o.above + o.in_mass;
+    const bool reach = (mode == T_MASS_GE) ? (tot >= T) : (tot > T);
+    return reach ? 0 : 2;
+}
+
+// Resolve one target from a collected, sorted window list.  Returns 1 and
+// fills `out` when the crossing lies in the list.
+__device__ __forceinline__ int resolve_list(Ctx &c, const unsigned long long *list,
+                                            const PassOut &o, int mode, double T, int m,
+                                            Sel &out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    Vars *v = c.v;
+    const int n = o.in_cnt;
+    if (classify(o, mode, T, m) != 0) return 0;
+    if (warp == 0) warp_walk(list, n, o.above, mode, T, m - o.cnt_above, v, lane);
+    __syncthreads();
+    const int f = v->sel_found, j = v->sel_j;
+    const double cs = v->cs;
+    __syncthreads();
+    if (!f) return 0;
+    const unsigned long long kk = list[j];
+    out.found = 1;
+    out.pos = o.cnt_above + j;
+    out.id = key_id(kk);
+    out.p = key_p(kk);
+    out.cs = cs;
+    out.tie = (j > 0 && key_p(list[j - 1]) == out.p) || (j + 1 < n && key_p(list[j + 1]) == out.p);
+    return 1;
+}
+
+// Last candidate in canonical order (smallest p, then largest id), and
+// whether its probability is shared; from global memory.
+__device__ __forceinline__ Sel last_canon(Ctx &c, bool scale) {
+    Vars *v = c.v;
+    const float inv_sum = v->inv_sum;
+    float pmin = PINF;
+    for (int e = threadIdx.x; e < c.V; e += NT) {
+        const float ev = e_global(c, e, scale);
+        if (__float_as_int(ev) >= 0) pmin = fminf(pmin, __fmul_rn(ev, inv_sum));
+    }
+    float dummy = 0.f;
+    block_maxmin_f(dummy, pmin, c.red);
+    int idmax = -1, cnt = 0;
+    for (int e = threadIdx.x; e < c.V; e += NT) {
+        const float ev = e_global(c, e, scale);
+        if (__float_as_int(ev) >= 0 && __fmul_rn(ev, inv_sum) == pmin) {
+            idmax = max(idmax, e);
+            ++cnt;
+        }
+    }
+    idmax = block_max_i(idmax, c.red);
+    cnt = block_sum_i(cnt, c.red);
+    Sel out;
+    out.found = 0;
+    out.pos = v->n_cand - 1;
+    out.id = idmax;
+    out.p = pmin;
+    out.cs = 0.0;
+    out.tie = cnt > 1;
+    return out;
+}
+
+// j-th (0-based, id order) candidate whose p equals pv; from global memory.
+__device__ __forceinline__ int ordered_pick(Ctx &c, bool scale, float pv, int j) {
+    Vars *v = c.v;
+    const float inv_sum = v->inv_sum;
+    const int V = c.V;
+    const int Q = (V + NT - 1) / NT;
+    const int e0 = threadIdx.x * Q, e1 = min(V, e0 + Q);
+    int cnt = 0;
+    for (int e = e0; e < e1; ++e) {
+        const float ev = e_global(c, e, scale);
+        cnt += (__float_as_int(ev) >= 0) && (__fmul_rn(ev, inv_sum) == pv);
+    }
+    int tot;
+    const int ex = block_xscan_i(cnt, tot, c.red);
+    if (threadIdx.x == 0) v->own = -1;
+    __syncthreads();
+    if (j >= ex && j < ex + cnt) {
+        int k = ex;
+        for (int e = e0; e < e1; ++e) {
+            const float ev = e_global(c, e, scale);
+            if ((__float_as_int(ev) >= 0) && (__fmul_rn(ev, inv_sum) == pv)) {
+                if (k == j) v->own = e;
+                ++k;
+            }
+        }
+    }
+    __syncthreads();
+    const int id = v->own;
+    __syncthreads();
+    return id;
+}
+
+// General select (rare path, after the estimated window missed): wider
+// bucket windows around the estimate, then bisection of the probability
+// interval, each step one exact pass over global memory.  Uses the
+// histogram area (its counts are no longer needed).
+__device__ __noinline__ Sel select_slow(Ctx c, bool scale, int mode, double T, int m, int bh) {
+    c.attach();
+    Vars *v = c.v;
+    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr);
+    int *rank = reinterpret_cast<int *>(c.scr + SLOW_CAP * 8);
+    const float inv_sum = v->inv_sum, w = v->w;
+    Sel out;
+    out.found = 0; out.pos = v->n_cand - 1; out.id = -1; out.p = 0.f; out.cs = 0.0; out.tie = 0;
+    unsigned lb = 0u, ub = 0x7f800000u;  // probability interval as bits
+    const int deltas[2] = {2, 24};
+    for (int it = 0; it < 100; ++it) {
+        float plo, phi;
+        if (it < 2) {
+            const int blo = max(0, bh - deltas[it]), bhi = min(NB - 1, bh + deltas[it]);
+            phi = (blo == 0) ? PINF : __fmul_rn(exp_one(-((float)blo - 0.5f) * w), inv_sum);
+            plo = (bhi == NB - 1) ? 0.0f : __fmul_rn(exp_one(-((float)bhi + 0.5f) * w), inv_sum);
+        } else {
+            phi = __uint_as_float(ub);
+            plo = __uint_as_float(lb);
+        }
+        PassOut o = exact_pass_g(c, scale, plo, phi, list, SLOW_CAP);
+        const int cl = classify(o, mode, T, m);
+        if (cl == 2 && __float_as_uint(plo) == 0u) {
+            // beyond the last candidate: total mass under the target
+            out = last_canon(c, scale);
+            out.found = 0;
+            out.cs = o.above + o.in_mass;
+            return out;
+        }
+        if (cl == 1) { lb = __float_as_uint(phi) + 1u; continue; }
+        if (cl == 2) { ub = __float_as_uint(plo) - 1u; continue; }
+        lb = __float_as_uint(plo);
+        ub = __float_as_uint(phi);
+        if (o.in_cnt <= SLOW_CAP) {
+            sort_keys(list, o.in_cnt, rank, SLOW_CAP);
+            if (resolve_list(c, list, o, mode, T, m, out)) return out;
+        }
+        if (lb == ub) {
+            // more than SLOW_CAP candidates share one probability value: the
+            // position inside the tie group is arithmetic, then the j-th id
+            const float pv = __uint_as_float(lb);
+            const int n = o.in_cnt;
+            int j = 0;
+            if (mode == T_POS) {
+                j = m - o.cnt_above;
+            } else {
+                while (j < n - 1 && !((mode == T_MASS_GE) ? (o.above + (double)(j + 1) * pv >= T)
+                                                           : (o.above + (double)(j + 1) * pv > T))) {
+                    const double need = (T - o.above) / (double)pv;
+                    const int jj = (int)need - 1;
+                    j = (jj > j) ? jj : j + 1;
+                    if (j > n - 1) j = n - 1;
+                }
+            }
+            out.found = 1;
+            out.pos = o.cnt_above + j;
+            out.p = pv;
+            out.cs = o.above + (double)(j + 1) * pv;
+            out.tie = (n > 1);
+            out.id = ordered_pick(c, scale, pv, j);
+            return out;
+        }
+        // keep the half that holds the crossing
+        const unsigned mid = lb + (ub - lb) / 2;
+        const PassOut u = exact_pass_g(c, scale, __uint_as_float(mid + 1u), __uint_as_float(ub),
+                                       list, SLOW_CAP);
+        if (classify(u, mode, T, m) == 0) lb = mid + 1u;
+        else ub = mid;
+        it = max(it, 1);
+    }
+    if (threadIdx.x == 0) atomicOr(c.err, 2);
+    return out;
+}
+
+// Exact replay of the reference's top-256 heap (src/model.c:327-356) over the
+// candidates in id order, by one warp, from global memory; `outk` ends up
+// sorted as the stable qsort leaves it (ties in heap-array order; low word =
+// heap slot).
+__device__ __noinline__ void replay_top256(Ctx c, bool scale, int n) {
+    c.attach();
+    unsigned long long *outk = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
+    float *hv = reinterpret_cast<float *>(c.scr + NB * 4 + 256 * 8);
+    int *hi = reinterpret_cast<int *>(c.scr + NB * 4 + 256 * 8 + 256 * 4);
+    int *rank = reinterpret_cast<int *>(c.scr);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float inv_sum = c.v->inv_sum;
+    const int V = c.V;
+    if (warp == 0) {
+        int filled = 0;
+        for (int base = 0; base < V; base += 32) {
+            const int id = base + lane;
+            float ev = -0.0f;
+            if (id < V) ev = e_global(c, id, scale);
+            const bool cand = __float_as_int(ev) >= 0;
+            const float p = __fmul_rn(cand ? ev : 0.0f, inv_sum);
+            const unsigned mk = __ballot_sync(FULL, cand);
+            bool rest = cand;
+            if (filled < 256) {
+                const int rk = __popc(mk & ((1u << lane) - 1));
+                const int take = min(__popc(mk), 256 - filled);
+                if (cand && rk < take) { hv[filled + rk] = p; hi[filled + rk] = id; }
+                rest = cand && rk >= take;
+                filled += take;
+                __syncwarp();
+                if (filled < 256) continue;
+                if (take > 0) warp_heapify(hv, hi, 256, lane);
+            }
+            const float root = hv[0];
+            unsigned mr = __ballot_sync(FULL, rest && p > root);
+            while (mr) {
+                const int src = __ffs(mr) - 1;
+                const float pb = __shfl_sync(FULL, p, src);
+                const int ib = __shfl_sync(FULL, id, src);
+                if (lane == 0 && pb > hv[0]) { hv[0] = pb; hi[0] = ib; heap_down(hv, hi, 256, 0); }
+                __syncwarp();
+                mr &= mr - 1;
+            }
+        }
+        __syncwarp();
+        for (int q = lane; q < 256; q += 32) outk[q] = canon_key(hv[q], q);
+    }
+    __syncthreads();
+    sort_keys(outk, 256, rank, 256);
+    if (threadIdx.x == 0) {
+        const float r = c.v->aux1 == 0.0 ? 0.0f : (float)c.v->aux1;
+        double cs = 0.0;
+        int pos = n - 1;
+        for (int j = 0; j < n; ++j) {
+            cs += (double)key_p(outk[j]);
+            if ((double)r < cs) { pos = j; break; }
+        }
+        const int hp = key_id(outk[pos]);
+        c.v->res_id = hi[hp];
+        c.v->res_p = hv[hp];
+    }
+    __syncthreads();
+}
+
+// Mass of a key list (all threads; fp64).
+__device__ __forceinline__ double list_mass(const unsigned long long *keys, int n, Red r) {
+    double s = 0.0;
+    for (int j = threadIdx.x; j < n; j += NT) s += (double)key_p(keys[j]);
+    return block_sum_d(s, r);
+}
+
+// One exact pass over the resident probabilities for the active windows of
+// MASK (bit t = window t): mass / count above each window (fp32 groups of
+// four, flushed to fp64 every eight slots) and the in-window elements
+// appended to the window lists.  In-window count = list length.
+template <int MASK>
+__device__ __forceinline__ void window_pass(Ctx &c, int ph0, int ph1, int ph2, int pl0, int pl1,
+                                            int pl2) {
+    const int phb[3] = {ph0, ph1, ph2}, plb[3] = {pl0, pl1, pl2};
+    unsigned long long *lists = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    Vars *v = c.v;
+    const int sh = v->sh, nslots = v->nslots;
+    const float inv_sum = v->inv_sum;
+    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
+    const float2 is2 = make_float2(inv_sum, inv_sum);
+    float au[3] = {0.f, 0.f, 0.f};
+    double du[3] = {0.0, 0.0, 0.0};
+    int cu[3] = {0, 0, 0};
+    int *lnp[3] = {&v->ln0, &v->ln1, &v->ln2};
+    int iter = 0;
+    for (int base = warp * 32; base < nslots; base += NT, ++iter) {
+        const int s = base + lane;
+        float4 x = make_float4(-0.f, -0.f, -0.f, -0.f);
+        if (s < nslots) x = r4[s];
+        const float2 pa = __fmul2_rn(make_float2(x.x, x.y), is2);
+        const float2 pb = __fmul2_rn(make_float2(x.z, x.w), is2);
+        const float p[4] = {pa.x, pa.y, pb.x, pb.y};
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            if (!((MASK >> t) & 1)) continue;
+            bool up[4];
+            bool any_in = false;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int b = __float_as_int(p[q]);
+                up[q] = b > phb[t];
+                any_in |= (!up[q] && b >= plb[t]);
+                cu[t] += up[q];
+            }
+            const float2 ga = __fadd2_rn(make_float2(up[0] ? p[0] : 0.f, up[1] ? p[1] : 0.f),
+                                         make_float2(up[2] ? p[2] : 0.f, up[3] ? p[3] : 0.f));
+            au[t] = __fadd_rn(au[t], __fadd_rn(ga.x, ga.y));
+            if (__ballot_sync(FULL, any_in)) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const bool in = !up[q] && __float_as_int(p[q]) >= plb[t];
+                    const unsigned mq = __ballot_sync(FULL, in);
+                    if (!mq) continue;
+                    const int leader = __ffs(mq) - 1;
+                    int bpos = 0;
+                    if (lane == leader) bpos = atomicAdd(lnp[t], __popc(mq));
+                    bpos = __shfl_sync(FULL, bpos, leader);
+                    if (in) {
+                        const int pos = bpos + __popc(mq & ((1u << lane) - 1));
+                        if (pos < LCAP) lists[t * LCAP + pos] = canon_key(p[q], 4 * s + q - sh);
+                    }
+                }
+            }
+        }
+        if ((iter & 7) == 7) {
+#pragma unroll
+            for (int t = 0; t < 3; ++t) {
+                if (!((MASK >> t) & 1)) continue;
+                du[t] += (double)au[t];
+                au[t] = 0.f;
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        if (!((MASK >> t) & 1)) continue;
+        double a = du[t] + (double)au[t], dummy = 0.0;
+        int ca = cu[t], dz = 0;
+        block_sum4(a, dummy, ca, dz, c.red);
+        if (threadIdx.x == 0) { v->wab[t] = a; v->wca[t] = ca; }
+    }
+    __syncthreads();
+}
+
+// exp pass of the full-vocabulary path (src/model.c:306-310): e = exp(l -
+// max) for l >= thr stored in place, -0 for non-candidates (adds nothing; the
+// sign marks them); counts of max - l buckets; returns the fp64 sum of fp32
+// groups of four.
+template <bool SCALE>
+__device__ __forceinline__ double exp_pass(Ctx &c, float dmax, float inv_w) {
+    Vars *v = c.v;
+    const int nslots = v->nslots;
     const float mx = v->mx, thr = v->thr, inv_temp = v->inv_temp;
-    const bool scale = (inv_temp != 1.0f);
     float4 *r4 = reinterpret_cast<float4 *>(c.row);
     uint32_t *hcnt = reinterpret_cast<uint32_t *>(c.scr);
+    uint32_t *hsh = hcnt - MAGIC_I;
+    const float2 mx2 = make_float2(-mx, -mx);
+    const float2 it2 = make_float2(inv_temp, inv_temp);
+    const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
+    double S = 0.0;
+    int tail = 0;
+    const int KTAIL = __float_as_int(__ffma2_rn(make_float2(dmax, dmax), iw2, mg2).x);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int base = warp * 32; base < nslots; base += NT) {
+        const int s = base + lane;
+        const float QN = __int_as_float(0x7fc00000);
+        const float4 x = (s < nslots) ? r4[s] : make_float4(QN, QN, QN, QN);
+        float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
+        if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
+        const bool k0 = a.x >= thr, k1 = a.y >= thr, k2 = b.x >= thr, k3 = b.y >= thr;
+        const float2 xa = __fadd2_rn(a, mx2), xb = __fadd2_rn(b, mx2);  // l - max
+        float2 ea = exp_pair(xa), eb = exp_pair(xb);
+        ea.x = k0 ? ea.x : -0.0f;
+        ea.y = k1 ? ea.y : -0.0f;
+        eb.x = k2 ? eb.x : -0.0f;
+        eb.y = k3 ? eb.y : -0.0f;
+        const float2 ka = __ffma2_rn(make_float2(fminf(-xa.x, dmax), fminf(-xa.y, dmax)), iw2, mg2);
+        const float2 kb = __ffma2_rn(make_float2(fminf(-xb.x, dmax), fminf(-xb.y, dmax)), iw2, mg2);
+        // the clamped tail bucket (masked or far-below logits) is counted in
+        // a register: it would serialise the shared atomics
+        const int kk[4] = {k0 ? __float_as_int(ka.x) : -1, k1 ? __float_as_int(ka.y) : -1,
+                           k2 ? __float_as_int(kb.x) : -1, k3 ? __float_as_int(kb.y) : -1};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (kk[q] == KTAIL) ++tail;
+            else if (kk[q] >= 0) atomicAdd(&hsh[kk[q]], 1u);
+        }
+        const float2 g = __fadd2_rn(ea, eb);
+        S += (double)__fadd_rn(g.x, g.y);
+        if (s < nslots) r4[s] = make_float4(ea.x, ea.y, eb.x, eb.y);
+    }
+    if (tail) atomicAdd(&hsh[KTAIL], (unsigned)tail);
+    return block_sum_d(S, c.red);
+}
 
+template <bool SCALE>
+__device__ __forceinline__ void full_path(Ctx &c) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    Vars *v = c.v;
+    const int sh = v->sh, nslots = v->nslots;
+    const float mx = v->mx, thr = v->thr, inv_temp = v->inv_temp;
+    float4 *r4 = reinterpret_cast<float4 *>(c.row);
+    uint32_t *hcnt = reinterpret_cast<uint32_t *>(c.scr);
+    unsigned long long *lists = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
+    const float top_p = v->top_p;
+    const int top_k = v->top_k;
+
+    if (mx == PINF) {
+        // +inf logit: expf(inf - inf) is NaN, the reference's sums are NaN and
+        // every walk falls through to the last candidate
+        int last = -1, cnt = 0;
+        for (int e = threadIdx.x; e < c.V; e += NT)
+            if (logit_g(c, e, SCALE) >= thr) { last = max(last, e); ++cnt; }
+        last = block_max_i(last, c.red);
+        cnt = block_sum_i(cnt, c.red);
+        release_row(c);
+        const bool lazy = (top_p >= 1.0f) && (top_k <= 0 || top_k >= cnt);
+        write_result(c, last, __int_as_float(0x7fc00000), lazy ? 5 : 7, cnt, cnt, 1);
+        return;
+    }
     for (int i = threadIdx.x; i < NB; i += NT) hcnt[i] = 0;
     // bucket geometry over d = max - l
     float dmax = __fsub_rn(mx, v->xmin);
@@ -1234,97 +1497,80 @@ __device__ void full_path(Ctx &c) {
     const float inv_w = __fdiv_rn((float)NB - 1.5f, dmax);
     const float w = __fdiv_rn(1.0f, inv_w);
     __syncthreads();
-    // exp pass (src/model.c:306-310): e = expf(l - max) for l >= thr, stored in
-    // place; non-candidates -1.  fp64 sum in groups of four.
-    double S = 0.0;
-    int ncand = 0, last = -1;
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        float4 x = r4[s];
-        float t[4] = {x.x, x.y, x.z, x.w};
-        float ev[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            int e = 4 * s + q - sh;
-            float l = scale ? __fmul_rn(t[q], inv_temp) : t[q];
-            bool cand = (e >= 0 && e < V) && (l >= thr);
-            ev[q] = -1.0f;
-            if (cand) {
-                ev[q] = expf(__fsub_rn(l, mx));
-                ++ncand;
-                last = e;
-                float d = fminf(__fsub_rn(mx, l), dmax);
-                int key = __float_as_int(__fmaf_rn(d, inv_w, MAGIC)) - __float_as_int(MAGIC);
-                key = min(max(key, 0), NB - 1);
-                atomicAdd(&hcnt[key], 1u);
-            }
-        }
-        float g0 = __fadd_rn(fmaxf(ev[0], 0.f), fmaxf(ev[1], 0.f));
-        float g1 = __fadd_rn(fmaxf(ev[2], 0.f), fmaxf(ev[3], 0.f));
-        // NaN e (inf logits) must poison the sum like the reference's
-        if (ev[0] != ev[0] || ev[1] != ev[1] || ev[2] != ev[2] || ev[3] != ev[3])
-            S += (double)__int_as_float(0x7fc00000);
-        else
-            S += (double)__fadd_rn(g0, g1);
-        r4[s] = make_float4(ev[0], ev[1], ev[2], ev[3]);
-    }
-    S = block_sum_d(S, c.red);
-    ncand = block_sum_i(ncand, c.red);
-    last = block_max_i(last, c.red);
-    const float top_p = v->top_p;
-    const int top_k = v->top_k;
-    const bool lazy = (top_p >= 1.0f) && (top_k <= 0 || top_k >= ncand);
-    if (ncand == 0) {  // argmax guard (src/model.c:296-303)
-        int id = guard_argmax(c);
-        write_result(c, id, 1.0f, 4, 0, 0, 0);
-        return;
-    }
-    if (S != S) {  // NaN mass: the walk falls through to the last candidate
-        write_result(c, last, __int_as_float(0x7fc00000), lazy ? 5 : 7, ncand, ncand, 1);
-        return;
-    }
+    // exp pass (src/model.c:306-310): e = exp(l - max) for l >= thr stored in
+    // place, -0 for non-candidates (adds nothing; the sign marks them);
+    // counts of max - l buckets; fp64 sum of fp32 groups of four
+    double S = exp_pass<SCALE>(c, dmax, inv_w);
     const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
+    // estimate from bucket counts x bucket-centre probabilities; each thread
+    // owns BPT consecutive buckets
+    const int bb = BPT * threadIdx.x;
+    int cb[BPT];
+    double mb[BPT];
+    int csum = 0;
+    double msum = 0.0;
+#pragma unroll
+    for (int q = 0; q < BPT; ++q) {
+        cb[q] = (int)hcnt[bb + q];
+        mb[q] = (double)cb[q] * (double)__fmul_rn(exp_one(-(float)(bb + q) * w), inv_sum);
+        csum += cb[q];
+        msum += mb[q];
+    }
+    double mt;
+    const double mex = block_xscan_d(msum, mt, c.red);
+    int ncand;
+    const int cex = block_xscan_i(csum, ncand, c.red);
     if (threadIdx.x == 0) {
         v->inv_sum = inv_sum;
         v->n_cand = ncand;
         v->w = w;
-        v->inv_w = inv_w;
-        v->last_cand = last;
+        v->S = S;
     }
-    __syncthreads();
-
+    if (ncand == 0) {  // argmax guard (src/model.c:296-303)
+        release_row(c);
+        const int id = guard_argmax(c);
+        write_result(c, id, 1.0f, 4, 0, 0, 0);
+        return;
+    }
+    const bool lazy = (top_p >= 1.0f) && (top_k <= 0 || top_k >= ncand);
     if (lazy) {
         // CDF walk in id order (src/model.c:319-320): contiguous segments
         const int Q = (nslots + NT - 1) / NT;
         const int s0 = threadIdx.x * Q, s1 = min(nslots, s0 + Q);
+        const float2 is2 = make_float2(inv_sum, inv_sum);
         double seg = 0.0;
+        int last = -1;
         for (int s = s0; s < s1; ++s) {
-            float4 x = r4[s];
-            float ev[4] = {x.x, x.y, x.z, x.w};
-            float g = 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                g = __fadd_rn(g, ev[q] >= 0.f ? __fmul_rn(ev[q], inv_sum) : 0.f);
-            seg += (double)g;
+            const float4 x = r4[s];
+            const float2 pa = __fmul2_rn(make_float2(x.x, x.y), is2);
+            const float2 pb = __fmul2_rn(make_float2(x.z, x.w), is2);
+            const float2 gg = __fadd2_rn(pa, pb);
+            seg += (double)__fadd_rn(gg.x, gg.y);
+            if (__float_as_int(x.w) >= 0) last = 4 * s + 3 - sh;
+            else if (__float_as_int(x.z) >= 0) last = 4 * s + 2 - sh;
+            else if (__float_as_int(x.y) >= 0) last = 4 * s + 1 - sh;
+            else if (__float_as_int(x.x) >= 0) last = 4 * s - sh;
         }
+        last = block_max_i(last, c.red);
         double total;
-        double pre = block_xscan_d(seg, total, c.red);
+        const double pre = block_xscan_d(seg, total, c.red);
         const float r = __fmul_rn(v->u, __double2float_rn(total));
-        int cand_t = ((double)r < pre + seg && seg > 0.0) ? (int)threadIdx.x : INT_MAX;
-        int owner = block_min_i(cand_t, c.red);
+        const int cand_t = ((double)r < pre + seg && seg > 0.0) ? (int)threadIdx.x : INT_MAX;
+        const int owner = block_min_i(cand_t, c.red);
         if (threadIdx.x == 0) { v->res_id = -1; v->res_p = 0.f; }
         __syncthreads();
         if ((int)threadIdx.x == owner) {
-            // rescan from this segment on (a rounding difference at the
-            // segment start can push the crossing one segment further)
+            // a rounding difference at a segment start can push the crossing
+            // one segment further: rescan from here on
             double cdf = pre;
             int id = -1;
             float pp = 0.f;
             for (int s = s0; s < nslots && id < 0; ++s) {
-                float4 x = r4[s];
-                float ev[4] = {x.x, x.y, x.z, x.w};
+                const float4 x = r4[s];
+                const float ev[4] = {x.x, x.y, x.z, x.w};
                 for (int q = 0; q < 4; ++q) {
-                    if (ev[q] >= 0.f) {
-                        float p = __fmul_rn(ev[q], inv_sum);
+                    if (__float_as_int(ev[q]) >= 0) {
+                        const float p = __fmul_rn(ev[q], inv_sum);
                         cdf += (double)p;
                         if ((double)r < cdf) { id = 4 * s + q - sh; pp = p; break; }
                     }
@@ -1335,42 +1581,133 @@ __device__ void full_path(Ctx &c) {
         __syncthreads();
         int id = v->res_id;
         float pp = v->res_p;
-        if (id < 0) {
-            // r at or beyond the last cdf: the reference returns the last
-            // candidate (src/model.c:117)
+        if (id < 0) {  // r at or beyond the last cdf: the last candidate (src/model.c:117)
             id = last;
             pp = __fmul_rn(c.row[last + sh], inv_sum);
         }
+        release_row(c);
         write_result(c, id, pp, 5, ncand, ncand, 1);
         return;
     }
 
-    // sorted order: nucleus cut, optional top_k truncation, draw
-    int n = ncand;
-    double new_sum = 0.0;
-    Sel tail;  // the element at position n-1
-    tail.found = 0;
-    bool partial = false;
-    if (top_p < 1.0f) {
-        Sel cut = select_canon(c, 0, (double)top_p, 0);
-        if (cut.found) {
-            n = cut.pos + 1;
-            new_sum = cut.cs;
-            tail = cut;
-            partial = (ncand > 256) && (cut.pos < 256);  // src/model.c:327-356
-        } else {
-            new_sum = cut.cs;  // whole candidate mass
-            tail = cut;
+    // ---- sorted order: nucleus cut, top_k truncation, draw -----------------
+    // targets: 0 = cut (cs >= top_p), 1 = top_k position, 2 = draw (cs > r).
+    // The draw's r = u * (float)new_sum is predicted from the estimate.
+    const bool want_cut = top_p < 1.0f;
+    const bool want_k = top_k > 0 && top_k < ncand;
+    // first owned bucket whose running estimate reaches T (or INT_MAX)
+    auto est_mass = [&](double T, bool strict) {
+        double run = mex;
+        int hit = INT_MAX;
+#pragma unroll
+        for (int q = 0; q < BPT; ++q) {
+            run += mb[q];
+            if (hit == INT_MAX && (strict ? (run > T) : (run >= T))) hit = bb + q;
+        }
+        return hit;
+    };
+    const int hit_c = want_cut ? est_mass((double)top_p, false) : INT_MAX;
+    int hit_k = INT_MAX;
+    double mass_k = 0.0;
+    if (want_k) {
+        const int mpos = top_k - 1;
+        int run = cex;
+        double mrun = mex;
+#pragma unroll
+        for (int q = 0; q < BPT; ++q) {
+            mrun += mb[q];
+            if (hit_k == INT_MAX && mpos >= run && mpos < run + cb[q]) { hit_k = bb + q; mass_k = mrun; }
+            run += cb[q];
         }
     }
-    if (top_k > 0 && top_k < n) {  // src/model.c:102-103
-        Sel tk = select_canon(c, 2, 0.0, top_k - 1);
+    if (threadIdx.x == 0) { v->bh0 = NB - 1; v->bh1 = NB - 1; v->bh2 = NB - 1; v->aux0 = mt; }
+    __syncthreads();
+    if (hit_c != INT_MAX) atomicMin(&v->bh0, hit_c);
+    if (hit_k != INT_MAX) {
+        atomicMin(&v->bh1, hit_k);
+        v->aux0 = mass_k;  // estimated mass through it
+    }
+    __syncthreads();
+    // predicted new_sum: the nucleus mass, or the top_k mass when smaller
+    double ns_est = want_cut ? (double)top_p : mt;
+    if (want_k) ns_est = fmin(ns_est, v->aux0);
+    const int hit_d = est_mass((double)v->u * ns_est, true);
+    if (hit_d != INT_MAX) atomicMin(&v->bh2, hit_d);
+    __syncthreads();
+    // windows: the estimated bucket of each target, as probability intervals
+    const bool act[3] = {want_cut, want_k, true};
+    const int bh[3] = {v->bh0, v->bh1, v->bh2};
+    int phb[3], plb[3];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        const float phi = (bh[t] == 0) ? PINF
+                                       : __fmul_rn(exp_one(-((float)bh[t] - 0.5f) * w), inv_sum);
+        const float plo = (bh[t] == NB - 1)
+                              ? 0.0f
+                              : __fmul_rn(exp_one(-((float)bh[t] + 0.5f) * w), inv_sum);
+        phb[t] = act[t] ? __float_as_int(phi) : INT_MAX;
+        plb[t] = act[t] ? __float_as_int(plo) : INT_MAX;
+    }
+    if (threadIdx.x == 0) { v->ln0 = 0; v->ln1 = 0; v->ln2 = 0; }
+    __syncthreads();
+    const int mask = (want_cut ? 1 : 0) | (want_k ? 2 : 0) | 4;
+    switch (mask) {
+        case 5: window_pass<5>(c, phb[0], phb[1], phb[2], plb[0], plb[1], plb[2]); break;
+        case 6: window_pass<6>(c, phb[0], phb[1], phb[2], plb[0], plb[1], plb[2]); break;
+        default: window_pass<7>(c, phb[0], phb[1], phb[2], plb[0], plb[1], plb[2]); break;
+    }
+    PassOut o[3];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        o[t].above = act[t] ? v->wab[t] : 0.0;
+        o[t].cnt_above = act[t] ? v->wca[t] : 0;
+        o[t].in_cnt = act[t] ? (t == 0 ? v->ln0 : t == 1 ? v->ln1 : v->ln2) : 0;
+        o[t].in_mass = 0.0;
+    }
+    // the row buffer is free: the next row's copy overlaps what follows
+    release_row(c);
+    __syncthreads();
+    int *rank = reinterpret_cast<int *>(c.scr);  // reuses the histogram area
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        if (!act[t]) continue;
+        if (o[t].in_cnt <= LCAP) {
+            sort_keys(lists + t * LCAP, o[t].in_cnt, rank, LCAP);
+            o[t].in_mass = list_mass(lists + t * LCAP, o[t].in_cnt, c.red);
+        }
+    }
+
+    int n = ncand;
+    double new_sum = 0.0;
+    Sel tail;
+    tail.found = 0; tail.id = -1; tail.p = 0.f; tail.tie = 0; tail.pos = ncand - 1; tail.cs = 0.0;
+    bool partial = false;
+    if (want_cut) {
+        Sel cut;
+        if (!(o[0].in_cnt <= LCAP &&
+              resolve_list(c, lists, o[0], T_MASS_GE, (double)top_p, 0, cut)))
+            cut = select_slow(c, SCALE, T_MASS_GE, (double)top_p, 0, bh[0]);
+        if (cut.found) {
+            n = cut.pos + 1;
+            partial = (ncand > 256) && (cut.pos < 256);  // src/model.c:327-356
+        }
+        new_sum = cut.cs;
+        tail = cut;
+    }
+    if (want_k && top_k < n) {  // src/model.c:102-103
+        Sel tk;
+        if (!(o[1].in_cnt <= LCAP &&
+              resolve_list(c, lists + LCAP, o[1], T_POS, 0.0, top_k - 1, tk)))
+            tk = select_slow(c, SCALE, T_POS, 0.0, top_k - 1, bh[1]);
         n = top_k;
         new_sum = tk.cs;
         tail = tk;
     }
     const float r = __fmul_rn(v->u, __double2float_rn(new_sum));
-    Sel d = select_canon(c, 1, (double)r, 0);
+    Sel d;
+    if (!(o[2].in_cnt <= LCAP &&
+          resolve_list(c, lists + 2 * LCAP, o[2], T_MASS_GT, (double)r, 0, d)))
+        d = select_slow(c, SCALE, T_MASS_GT, (double)r, 0, bh[2]);
     int id;
     float pp;
     if (d.found && d.pos < n) { id = d.id; pp = d.p; }
@@ -1378,25 +1715,9 @@ __device__ void full_path(Ctx &c) {
     if (partial && d.tie) {
         // the reference's heap layout decides the order among equal
         // probabilities: replay it exactly
-        unsigned long long *hk = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
-        float *hv = reinterpret_cast<float *>(c.scr + NB * 4 + WCAP * 8);
-        int *hix = reinterpret_cast<int *>(c.scr + NB * 4 + WCAP * 8 + 256 * 4);
-        replay_top256(c, hk, hv, hix);
-        if (warp == 0) {
-            // walk the replayed order with the same cut and draw
-            double cs = 0.0;
-            int pos = n - 1;
-            if (lane == 0) {
-                for (int j = 0; j < n; ++j) {
-                    cs += (double)key_p(hk[j]);
-                    if ((double)r < cs) { pos = j; break; }
-                }
-                int hp = key_id(hk[pos]);
-                v->res_id = hix[hp];
-                v->res_p = hv[hp];
-            }
-        }
+        if (threadIdx.x == 0) v->aux1 = (double)r;
         __syncthreads();
+        replay_top256(c, SCALE, n);
         id = v->res_id;
         pp = v->res_p;
     }
@@ -1404,18 +1725,17 @@ __device__ void full_path(Ctx &c) {
 }
 
 __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
-    extern __shared__ __align__(128) unsigned char smem[];
+    const Layout L = layout(P.V);
     Ctx c;
-    c.P = P;
-    c.L = layout(P.V);
-    c.mbar = reinterpret_cast<uint64_t *>(smem + c.L.mbar);
-    c.red.d = reinterpret_cast<double *>(smem + c.L.red);
-    c.red.i = reinterpret_cast<int *>(smem + c.L.red + NW * 8);
-    c.red.f = reinterpret_cast<float *>(smem + c.L.red + NW * 12);
-    c.v = reinterpret_cast<Vars *>(smem + c.L.vars);
-    c.bits = reinterpret_cast<uint32_t *>(smem + c.L.bits);
-    c.scr = smem + c.L.scr;
-    c.row = reinterpret_cast<float *>(smem + c.L.row);
+    c.logits = P.logits;
+    c.ld = P.ld;
+    c.B = P.B;
+    c.V = P.V;
+    c.err = P.err;
+    c.out_id = P.out_id;
+    c.out_prob = P.out_prob;
+    c.stats = P.stats;
+    c.attach();
     Vars *v = c.v;
     const int V = P.V;
     const int tid = threadIdx.x;
@@ -1424,6 +1744,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         for (int i = 0; i < NCHUNK; ++i) mbar_init(&c.mbar[i], 1);
         fence_mbar_init();
         v->fail = 0;
+        if ((int)blockIdx.x < P.B) issue_row(P.logits + (int64_t)blockIdx.x * P.ld, V, c.mbar, c.row);
     }
     __syncthreads();
 
@@ -1432,37 +1753,29 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         c.rowid = row;
         c.parity = it & 1u;
         c.g = P.logits + (int64_t)row * P.ld;
-        // geometry of this row inside 16-byte slots
-        const int sh = (int)(((uintptr_t)c.g & 15u) >> 2);
-        const int nslots = (V + sh + 3) >> 2;
-        int i0 = sh ? 4 - sh : 0;
-        if (i0 > V) i0 = V;
-        int n4 = ((V - i0) >> 2) << 2;
-        if (n4 < 4 * NCHUNK * 4) n4 = 0;  // tiny rows: plain loads only
-        const int s_int0 = (i0 + sh) >> 2, s_int1 = s_int0 + (n4 >> 2);
         if (tid == 0) {
-            // issue this row's bulk copies (the buffer is free: previous row
-            // finished with a barrier and an async-proxy fence)
-            const int nint = s_int1 - s_int0;
-            for (int ch = 0; ch < NCHUNK; ++ch) {
-                int a = (ch * nint) / NCHUNK, b = ((ch + 1) * nint) / NCHUNK;
-                uint32_t bytes = (uint32_t)(b - a) * 16u;
-                mbar_expect_tx(&c.mbar[ch], bytes);
-                if (bytes)
-                    bulk_load(c.row + 4 * (s_int0 + a), c.g + i0 + 4 * a, bytes, &c.mbar[ch]);
-            }
-            // and warm L2 with the next row this CTA will take
-            const int nrow = row + gridDim.x;
+            const int sh = (int)(((uintptr_t)c.g & 15u) >> 2);
+            int i0 = sh ? 4 - sh : 0;
+            if (i0 > V) i0 = V;
+            int n4 = ((V - i0) >> 2) << 2;
+            if (n4 < 4 * NCHUNK * 4) n4 = 0;
+            v->sh = sh;
+            v->nslots = (V + sh + 3) >> 2;
+            v->s_int0 = (i0 + sh) >> 2;
+            v->s_int1 = v->s_int0 + (n4 >> 2);
+            v->released = 0;
+            // warm L2 with the row after the next one (the next row's copy is
+            // issued during this row)
+            const int nrow = row + 2 * (int)gridDim.x;
             if (nrow < P.B) {
                 const float *ng = P.logits + (int64_t)nrow * P.ld;
-                int nsh = (int)(((uintptr_t)ng & 15u) >> 2);
-                int ni0 = nsh ? 4 - nsh : 0;
+                const int nsh = (int)(((uintptr_t)ng & 15u) >> 2);
+                const int ni0 = nsh ? 4 - nsh : 0;
                 if (ni0 < V) {
-                    int nn4 = ((V - ni0) >> 2) << 2;
+                    const int nn4 = ((V - ni0) >> 2) << 2;
                     if (nn4 >= 16) prefetch_l2(ng + ni0, (uint32_t)nn4 * 4u);
                 }
             }
-            // knobs of this row
             const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
             v->temp = kn.temp;
             v->penalty = kn.penalty;
@@ -1473,35 +1786,42 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             v->log_min_p = kn.log_min_p;
             v->u = P.uniform ? P.uniform[row] : 0.0f;
             v->greedy = (kn.temp < 0.05f);  // src/model.c:144
-            v->sh = sh;
-            v->nslots = nslots;
-            v->s_int0 = s_int0;
-            v->s_int1 = s_int1;
             int h0 = 0, h1 = 0;
             if (P.hist && P.hist_off) { h0 = (int)P.hist_off[row]; h1 = (int)P.hist_off[row + 1]; }
             v->pen = (h1 > h0) && (kn.penalty > 0.0f) && (kn.penalty != 1.0f);
-            v->kcut = h0;
-            v->kcnt = h1;
+            v->h0 = h0;
+            v->h1 = h1;
         }
         __syncthreads();
+        const int sh = v->sh;
         // penalty bitset over this row's distinct, in-range, unprotected ids
         if (v->pen) {
-            const int h0 = v->kcut, h1 = v->kcnt;
-            for (int i = tid; i < c.L.nbw; i += NT) c.bits[i] = 0u;
+            const int h0 = v->h0, h1 = v->h1;
+            for (int i = tid; i < L.nbw; i += NT) c.bits[i] = 0u;
             __syncthreads();
             for (int i = h0 + tid; i < h1; i += NT) {
-                int id = P.hist[i];
+                const int id = P.hist[i];
                 if (id >= 0 && id < V && !protected_id(id)) {
-                    int b = id + sh;
+                    const int b = id + sh;
                     atomicOr(&c.bits[b >> 5], 1u << (b & 31));
                 }
             }
             __syncthreads();
         }
-        const bool greedy = v->greedy != 0;
+        const bool greedy = v->greedy != 0, pen = v->pen != 0;
+        const bool scale = v->inv_temp != 1.0f;
         float mx, xmin, gv;
         int gi;
-        load_pass(c, greedy, mx, xmin, gv, gi);
+        if (greedy) {
+            if (pen) load_pass<true, true, false>(c, mx, xmin, gv, gi);
+            else load_pass<true, false, false>(c, mx, xmin, gv, gi);
+        } else if (pen) {
+            if (scale) load_pass<false, true, true>(c, mx, xmin, gv, gi);
+            else load_pass<false, true, false>(c, mx, xmin, gv, gi);
+        } else {
+            if (scale) load_pass<false, false, true>(c, mx, xmin, gv, gi);
+            else load_pass<false, false, false>(c, mx, xmin, gv, gi);
+        }
         if (__syncthreads_or(v->fail)) {
             // a bounded wait expired: wait (bounded) for this row's copies,
             // then stop; the host sees the error flag
@@ -1512,6 +1832,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         }
         if (greedy) {
             block_argmax(gv, gi, c.red);
+            release_row(c);
             write_result(c, gi == INT_MAX ? 0 : gi, 1.0f, 1, 0, 0, 0);
         } else {
             block_maxmin_f(mx, xmin, c.red);
@@ -1526,12 +1847,20 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
                 v->k = (v->top_k > 0 && v->top_k <= 256) ? v->top_k : 0;  // src/model.c:175
             }
             __syncthreads();
-            if (v->k > 0) topk_path(c);
-            else full_path(c);
+            if (v->k > 0) {
+                if (scale) topk_path<true>(c);
+                else topk_path<false>(c);
+            } else {
+                if (scale) full_path<true>(c);
+                else full_path<false>(c);
+            }
         }
-        fence_proxy_async();
+        __syncthreads();
+        if (!v->released) release_row(c);
         __syncthreads();
     }
+    // the last release of this CTA targets a row >= B and issues nothing, so
+    // no copy is in flight when the kernel ends
 }
 
 }  // namespace
@@ -1542,7 +1871,7 @@ int max_vocab(size_t limit) {
     int lo = 1, hi = 1 << 20;
     if (smem_bytes(1) > limit) return 0;
     while (lo < hi) {
-        int mid = lo + (hi - lo + 1) / 2;
+        const int mid = lo + (hi - lo + 1) / 2;
         if (smem_bytes(mid) <= limit) lo = mid;
         else hi = mid - 1;
     }

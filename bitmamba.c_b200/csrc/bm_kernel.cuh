@@ -9,7 +9,7 @@
 
 namespace bmk {
 
-constexpr int NT = 1024;      // threads per CTA (one CTA per SM)
+constexpr int NT = 512;       // threads per CTA (one CTA per SM)
 constexpr int NW = NT / 32;   // warps per CTA
 constexpr int HB = 128;       // reference histogram buckets (src/model.c:132)
 constexpr int NB = 2048;      // full-vocabulary path: logit buckets
