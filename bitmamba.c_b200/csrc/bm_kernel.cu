@@ -42,9 +42,10 @@ constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 constexpr float DCAP = 40.0f;                          // bucket range cap
 constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
 constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
-constexpr int LCAP = 512;                              // per-window list cap
+constexpr int LISTCAP = 2048;                          // window list cap (entries)
 constexpr int BPT = NB / NT;                            // estimate buckets per thread
-constexpr int SLOW_CAP = 512;                          // rare-path list cap
+constexpr int SLOW_CAP = 256;                          // rare-path list cap
+constexpr int SLOW_OFF = LISTCAP * 8 + 2048;           // rare-path scratch offset
 constexpr float PINF = __builtin_huge_valf();
 constexpr size_t RED_BYTES = 2048;
 
@@ -66,8 +67,9 @@ struct __align__(16) Vars {
     int sel_found, sel_j, res_id, n_final;
     float res_p, pad1, pad2, pad3;
     double S, cs, aux0, aux1;
-    double wab[3];
-    int wca[3], pad4;
+    double mc, ec, mk, ek, md;
+    int bc, bk, bd0, bd1, cc, ck, cd, tail_cnt;
+    int bc_hi, bd_hi, next_row, pad5;
 };
 
 struct Layout {
@@ -390,7 +392,7 @@ __device__ void sort_keys(unsigned long long *a, int n, int *rank, int cap) {
         __syncthreads();
         return;
     }
-    if (n > NT) {
+    if (n > 256) {  // rank sort costs n*n/NT comparisons per thread
         bitonic_u64(a, n, cap);
         return;
     }
@@ -446,6 +448,7 @@ struct Ctx {
     int64_t ld;
     int B, V;
     int *err;
+    int *sched;
     uint64_t *mbar;
     Red red;
     Vars *v;
@@ -493,14 +496,33 @@ __device__ __forceinline__ void issue_row(const float *g, int V, uint64_t *mbar,
     }
 }
 
+// L2 prefetch of a row's 16-byte-aligned interior.
+__device__ __forceinline__ void prefetch_row(const float *g, int V) {
+    const int sh = (int)(((uintptr_t)g & 15u) >> 2);
+    const int i0 = sh ? 4 - sh : 0;
+    if (i0 < V) {
+        const int n4 = ((V - i0) >> 2) << 2;
+        if (n4 >= 16) prefetch_l2(g + i0, (uint32_t)n4 * 4u);
+    }
+}
+
 // The row buffer is no longer read for this row: let the next row's copy in.
 __device__ __forceinline__ void release_row(Ctx &c) {
     fence_proxy_async();
     __syncthreads();
     if (threadIdx.x == 0) {
         c.v->released = 1;
-        const int next_row = c.rowid + gridDim.x;
-        if (next_row < c.B) issue_row(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row);
+        // dynamic schedule: the first gridDim.x rows go one per CTA, every
+        // later row to the CTA that frees its buffer first (rows of unequal
+        // cost would otherwise leave SMs idle at the end of the launch)
+        const int next_row = (int)gridDim.x + atomicAdd(&c.sched[0], 1);
+        c.v->next_row = next_row;
+        if (next_row < c.B) {
+            issue_row(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row);
+            // warm L2 with the row claimed about one round later
+            const int pre = next_row + (int)gridDim.x;
+            if (pre < c.B) prefetch_row(c.logits + (int64_t)pre * c.ld, c.V);
+        }
     }
 }
 
@@ -1184,26 +1206,24 @@ __device__ __forceinline__ int ordered_pick(Ctx &c, bool scale, float pv, int j)
     return id;
 }
 
-// General select (rare path, after the estimated window missed): wider
-// bucket windows around the estimate, then bisection of the probability
-// interval, each step one exact pass over global memory.  Uses the
-// histogram area (its counts are no longer needed).
-__device__ __noinline__ Sel select_slow(Ctx c, bool scale, int mode, double T, int m, int bh) {
+// General select (rare path: the exact bucket windows could not decide):
+// the probability window [plo0, phi0] first, then bisection of the
+// probability interval, each step one exact pass over global memory.  Uses
+// the upper part of the scratch area.
+__device__ __noinline__ Sel select_slow(Ctx c, bool scale, int mode, double T, int m, float plo0,
+                                        float phi0) {
     c.attach();
     Vars *v = c.v;
-    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr);
-    int *rank = reinterpret_cast<int *>(c.scr + SLOW_CAP * 8);
-    const float inv_sum = v->inv_sum, w = v->w;
+    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr + SLOW_OFF);
+    int *rank = reinterpret_cast<int *>(c.scr + SLOW_OFF + SLOW_CAP * 8);
     Sel out;
     out.found = 0; out.pos = v->n_cand - 1; out.id = -1; out.p = 0.f; out.cs = 0.0; out.tie = 0;
     unsigned lb = 0u, ub = 0x7f800000u;  // probability interval as bits
-    const int deltas[2] = {2, 24};
     for (int it = 0; it < 100; ++it) {
         float plo, phi;
-        if (it < 2) {
-            const int blo = max(0, bh - deltas[it]), bhi = min(NB - 1, bh + deltas[it]);
-            phi = (blo == 0) ? PINF : __fmul_rn(exp_one(-((float)blo - 0.5f) * w), inv_sum);
-            plo = (bhi == NB - 1) ? 0.0f : __fmul_rn(exp_one(-((float)bhi + 0.5f) * w), inv_sum);
+        if (it == 0) {
+            phi = phi0;
+            plo = plo0;
         } else {
             phi = __uint_as_float(ub);
             plo = __uint_as_float(lb);
@@ -1256,22 +1276,22 @@ __device__ __noinline__ Sel select_slow(Ctx c, bool scale, int mode, double T, i
                                        list, SLOW_CAP);
         if (classify(u, mode, T, m) == 0) lb = mid + 1u;
         else ub = mid;
-        it = max(it, 1);
     }
     if (threadIdx.x == 0) atomicOr(c.err, 2);
     return out;
 }
 
 // Exact replay of the reference's top-256 heap (src/model.c:327-356) over the
-// candidates in id order, by one warp, from global memory; `outk` ends up
-// sorted as the stable qsort leaves it (ties in heap-array order; low word =
-// heap slot).
+// candidates in id order, by one warp, from global memory; then the walk over
+// the replayed order (stable sort: ties in heap-array order) for the nucleus
+// of n elements and the draw r held in vars.
 __device__ __noinline__ void replay_top256(Ctx c, bool scale, int n) {
     c.attach();
-    unsigned long long *outk = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
-    float *hv = reinterpret_cast<float *>(c.scr + NB * 4 + 256 * 8);
-    int *hi = reinterpret_cast<int *>(c.scr + NB * 4 + 256 * 8 + 256 * 4);
-    int *rank = reinterpret_cast<int *>(c.scr);
+    // runs after every walk: the window list area is free
+    unsigned long long *outk = reinterpret_cast<unsigned long long *>(c.scr);
+    float *hv = reinterpret_cast<float *>(c.scr + 256 * 8);
+    int *hi = reinterpret_cast<int *>(c.scr + 256 * 8 + 256 * 4);
+    int *rank = reinterpret_cast<int *>(c.scr + 256 * 8 + 512 * 4);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float inv_sum = c.v->inv_sum;
     const int V = c.V;
@@ -1312,7 +1332,7 @@ __device__ __noinline__ void replay_top256(Ctx c, bool scale, int n) {
     __syncthreads();
     sort_keys(outk, 256, rank, 256);
     if (threadIdx.x == 0) {
-        const float r = c.v->aux1 == 0.0 ? 0.0f : (float)c.v->aux1;
+        const float r = (float)c.v->aux1;
         double cs = 0.0;
         int pos = n - 1;
         for (int j = 0; j < n; ++j) {
@@ -1326,152 +1346,294 @@ __device__ __noinline__ void replay_top256(Ctx c, bool scale, int n) {
     __syncthreads();
 }
 
-// Mass of a key list (all threads; fp64).
-__device__ __forceinline__ double list_mass(const unsigned long long *keys, int n, Red r) {
-    double s = 0.0;
-    for (int j = threadIdx.x; j < n; j += NT) s += (double)key_p(keys[j]);
-    return block_sum_d(s, r);
+// ---- full-vocabulary path: buckets over d = max - l ------------------------
+// A candidate's bucket is key = round(d * inv_w), d = max - l, computed as
+// kf = fma(d, inv_w, MAGIC) on the FMA pipe (kf - MAGIC = key, exactly).
+// Non-candidates get d = 1e30: exp(-d) is then 0 and every bucket test fails.
+// Bucket tests use saturating multiplies (FMA pipe), not compares/selects.
+__device__ __forceinline__ float mul_sat(float a, float b) {
+    float r;
+    asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+// 1 when key < b (kf < MAGIC + b), else 0; tb = MAGIC + b
+__device__ __forceinline__ float2 step_lt2(float2 kf, float tb) {
+    const float2 df = __fadd2_rn(make_float2(tb, tb), make_float2(-kf.x, -kf.y));
+    return make_float2(mul_sat(df.x, 0x1p100f), mul_sat(df.y, 0x1p100f));
+}
+constexpr float DNC = 1e30f;  // d of non-candidates
+
+// d = max - l for a pair of scaled logits; DNC for non-candidates (l < thr)
+__device__ __forceinline__ float2 d_pair(float2 l, float mx, float thr) {
+    const float2 d = __fadd2_rn(make_float2(mx, mx), make_float2(-l.x, -l.y));
+    return make_float2(l.x >= thr ? d.x : DNC, l.y >= thr ? d.y : DNC);
+}
+// bucket key floats of a pair (clamped to the last bucket when CLAMP)
+template <bool CLAMP>
+__device__ __forceinline__ float2 kf_pair(float2 d, float2 iw2, float2 mg2, float dmax) {
+    // non-candidates keep d = DNC (clamping them would file them in the last
+    // bucket)
+    if (CLAMP)
+        d = make_float2(d.x == DNC ? DNC : fminf(d.x, dmax), d.y == DNC ? DNC : fminf(d.y, dmax));
+    return __ffma2_rn(d, iw2, mg2);
 }
 
-// One exact pass over the resident probabilities for the active windows of
-// MASK (bit t = window t): mass / count above each window (fp32 groups of
-// four, flushed to fp64 every eight slots) and the in-window elements
-// appended to the window lists.  In-window count = list length.
-template <int MASK>
-__device__ __forceinline__ void window_pass(Ctx &c, int ph0, int ph1, int ph2, int pl0, int pl1,
-                                            int pl2) {
-    const int phb[3] = {ph0, ph1, ph2}, plb[3] = {pl0, pl1, pl2};
-    unsigned long long *lists = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    Vars *v = c.v;
-    const int sh = v->sh, nslots = v->nslots;
-    const float inv_sum = v->inv_sum;
-    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    const float2 is2 = make_float2(inv_sum, inv_sum);
-    float au[3] = {0.f, 0.f, 0.f};
-    double du[3] = {0.0, 0.0, 0.0};
-    int cu[3] = {0, 0, 0};
-    int *lnp[3] = {&v->ln0, &v->ln1, &v->ln2};
-    int iter = 0;
-    for (int base = warp * 32; base < nslots; base += NT, ++iter) {
-        const int s = base + lane;
-        float4 x = make_float4(-0.f, -0.f, -0.f, -0.f);
-        if (s < nslots) x = r4[s];
-        const float2 pa = __fmul2_rn(make_float2(x.x, x.y), is2);
-        const float2 pb = __fmul2_rn(make_float2(x.z, x.w), is2);
-        const float p[4] = {pa.x, pa.y, pb.x, pb.y};
-#pragma unroll
-        for (int t = 0; t < 3; ++t) {
-            if (!((MASK >> t) & 1)) continue;
-            bool up[4];
-            bool any_in = false;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int b = __float_as_int(p[q]);
-                up[q] = b > phb[t];
-                any_in |= (!up[q] && b >= plb[t]);
-                cu[t] += up[q];
-            }
-            const float2 ga = __fadd2_rn(make_float2(up[0] ? p[0] : 0.f, up[1] ? p[1] : 0.f),
-                                         make_float2(up[2] ? p[2] : 0.f, up[3] ? p[3] : 0.f));
-            au[t] = __fadd_rn(au[t], __fadd_rn(ga.x, ga.y));
-            if (__ballot_sync(FULL, any_in)) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const bool in = !up[q] && __float_as_int(p[q]) >= plb[t];
-                    const unsigned mq = __ballot_sync(FULL, in);
-                    if (!mq) continue;
-                    const int leader = __ffs(mq) - 1;
-                    int bpos = 0;
-                    if (lane == leader) bpos = atomicAdd(lnp[t], __popc(mq));
-                    bpos = __shfl_sync(FULL, bpos, leader);
-                    if (in) {
-                        const int pos = bpos + __popc(mq & ((1u << lane) - 1));
-                        if (pos < LCAP) lists[t * LCAP + pos] = canon_key(p[q], 4 * s + q - sh);
-                    }
-                }
-            }
-        }
-        if ((iter & 7) == 7) {
-#pragma unroll
-            for (int t = 0; t < 3; ++t) {
-                if (!((MASK >> t) & 1)) continue;
-                du[t] += (double)au[t];
-                au[t] = 0.f;
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < 3; ++t) {
-        if (!((MASK >> t) & 1)) continue;
-        double a = du[t] + (double)au[t], dummy = 0.0;
-        int ca = cu[t], dz = 0;
-        block_sum4(a, dummy, ca, dz, c.red);
-        if (threadIdx.x == 0) { v->wab[t] = a; v->wca[t] = ca; }
-    }
-    __syncthreads();
-}
-
-// exp pass of the full-vocabulary path (src/model.c:306-310): e = exp(l -
-// max) for l >= thr stored in place, -0 for non-candidates (adds nothing; the
-// sign marks them); counts of max - l buckets; returns the fp64 sum of fp32
-// groups of four.
-template <bool SCALE>
-__device__ __forceinline__ double exp_pass(Ctx &c, float dmax, float inv_w) {
+// Pass 1 of the sorted path: bucket counts (one shared atomic per candidate;
+// the clamped last bucket is counted in a register).
+template <bool SCALE, bool CLAMP>
+__device__ __forceinline__ void hist_pass(Ctx &c, float inv_w, float dmax) {
     Vars *v = c.v;
     const int nslots = v->nslots;
-    const float mx = v->mx, thr = v->thr, inv_temp = v->inv_temp;
-    float4 *r4 = reinterpret_cast<float4 *>(c.row);
-    uint32_t *hcnt = reinterpret_cast<uint32_t *>(c.scr);
-    uint32_t *hsh = hcnt - MAGIC_I;
-    const float2 mx2 = make_float2(-mx, -mx);
-    const float2 it2 = make_float2(inv_temp, inv_temp);
+    const float mx = v->mx, thr = v->thr;
+    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
+    uint32_t *hc = reinterpret_cast<uint32_t *>(c.scr);
+    uint32_t *hsh = hc - MAGIC_I;
+    const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
     const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
-    double S = 0.0;
+    const int KT = MAGIC_I + NB - 1;
     int tail = 0;
-    const int KTAIL = __float_as_int(__ffma2_rn(make_float2(dmax, dmax), iw2, mg2).x);
+    for (int s = threadIdx.x; s < nslots; s += NT) {
+        const float4 x = r4[s];
+        float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
+        if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
+        const float2 ka = kf_pair<CLAMP>(d_pair(a, mx, thr), iw2, mg2, dmax);
+        const float2 kb = kf_pair<CLAMP>(d_pair(b, mx, thr), iw2, mg2, dmax);
+        const int kk[4] = {__float_as_int(ka.x), __float_as_int(ka.y), __float_as_int(kb.x),
+                           __float_as_int(kb.y)};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (kk[q] > KT) continue;  // non-candidate (d = 1e30)
+            if (CLAMP && kk[q] == KT) ++tail;
+            else atomicAdd(&hsh[kk[q]], 1u);
+        }
+    }
+    if (CLAMP && tail) atomicAdd(&hc[NB - 1], (unsigned)tail);
+}
+
+// Pass 2 of the sorted path: exp and its fp64 sum, per window the e-mass of
+// the candidates above it (key < b_t), and the elements of the union of the
+// windows appended to the list as (id, l).
+template <bool SCALE, bool CLAMP, int NTG>
+__device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, const float *tl,
+                                              const float *th, double *mass, double &S) {
+    Vars *v = c.v;
+    const int sh = v->sh, nslots = v->nslots;
+    const float mx = v->mx, thr = v->thr;
+    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
+    // the histogram is dead once the windows are chosen: the list reuses it
+    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr);
+    const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
+    const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int base = warp * 32; base < nslots; base += NT) {
+    double acc = 0.0;
+    double dm[NTG];
+    float fm[NTG];
+#pragma unroll
+    for (int t = 0; t < NTG; ++t) { dm[t] = 0.0; fm[t] = 0.f; }
+    float fs = 0.f;
+    int iter = 0;
+    for (int base = warp * 32; base < nslots; base += NT, ++iter) {
         const int s = base + lane;
         const float QN = __int_as_float(0x7fc00000);
         const float4 x = (s < nslots) ? r4[s] : make_float4(QN, QN, QN, QN);
         float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
         if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
-        const bool k0 = a.x >= thr, k1 = a.y >= thr, k2 = b.x >= thr, k3 = b.y >= thr;
-        const float2 xa = __fadd2_rn(a, mx2), xb = __fadd2_rn(b, mx2);  // l - max
-        float2 ea = exp_pair(xa), eb = exp_pair(xb);
-        ea.x = k0 ? ea.x : -0.0f;
-        ea.y = k1 ? ea.y : -0.0f;
-        eb.x = k2 ? eb.x : -0.0f;
-        eb.y = k3 ? eb.y : -0.0f;
-        const float2 ka = __ffma2_rn(make_float2(fminf(-xa.x, dmax), fminf(-xa.y, dmax)), iw2, mg2);
-        const float2 kb = __ffma2_rn(make_float2(fminf(-xb.x, dmax), fminf(-xb.y, dmax)), iw2, mg2);
-        // the clamped tail bucket (masked or far-below logits) is counted in
-        // a register: it would serialise the shared atomics
-        const int kk[4] = {k0 ? __float_as_int(ka.x) : -1, k1 ? __float_as_int(ka.y) : -1,
-                           k2 ? __float_as_int(kb.x) : -1, k3 ? __float_as_int(kb.y) : -1};
+        const float2 da = d_pair(a, mx, thr), db = d_pair(b, mx, thr);
+        // e = exp(l - max) = exp(-d); fl(l - max) = -fl(max - l) exactly
+        const float2 ea = exp_pair(make_float2(-da.x, -da.y));
+        const float2 eb = exp_pair(make_float2(-db.x, -db.y));
+        const float2 ka = kf_pair<CLAMP>(da, iw2, mg2, dmax), kb = kf_pair<CLAMP>(db, iw2, mg2, dmax);
+        const float2 g = __fadd2_rn(ea, eb);
+        fs = __fadd_rn(fs, __fadd_rn(g.x, g.y));
+        // per target: mass above its bucket (key < b), and membership
+        // (key == b) accumulated over the targets
+        float2 ia = make_float2(0.f, 0.f), ib = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            if (kk[q] == KTAIL) ++tail;
-            else if (kk[q] >= 0) atomicAdd(&hsh[kk[q]], 1u);
+        for (int t = 0; t < NTG; ++t) {
+            const float2 ua = step_lt2(ka, tl[t]), ub = step_lt2(kb, tl[t]);
+            const float2 m2 = __ffma2_rn(ea, ua, __fmul2_rn(eb, ub));
+            fm[t] = __fadd_rn(fm[t], __fadd_rn(m2.x, m2.y));
+            const float2 va = step_lt2(ka, th[t]), vb = step_lt2(kb, th[t]);
+            ia = __fadd2_rn(ia, __fadd2_rn(va, make_float2(-ua.x, -ua.y)));
+            ib = __fadd2_rn(ib, __fadd2_rn(vb, make_float2(-ub.x, -ub.y)));
         }
+        const float inb[4] = {ia.x, ia.y, ib.x, ib.y};
+        const bool any = (inb[0] + inb[1]) + (inb[2] + inb[3]) > 0.5f;
+        if (__ballot_sync(FULL, any)) {
+            const float lv[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const bool in = inb[q] > 0.5f;
+                const unsigned mq = __ballot_sync(FULL, in);
+                if (!mq) continue;
+                const int leader = __ffs(mq) - 1;
+                int bpos = 0;
+                if (lane == leader) bpos = atomicAdd(&v->ln0, __popc(mq));
+                bpos = __shfl_sync(FULL, bpos, leader);
+                if (in) {
+                    const int pos = bpos + __popc(mq & ((1u << lane) - 1));
+                    if (pos < LISTCAP)
+                        list[pos] = ((unsigned long long)(unsigned)(4 * s + q - sh) << 32) |
+                                    __float_as_uint(lv[q]);
+                }
+            }
+        }
+        if ((iter & 7) == 7) {
+            acc += (double)fs;
+            fs = 0.f;
+#pragma unroll
+            for (int t = 0; t < NTG; ++t) { dm[t] += (double)fm[t]; fm[t] = 0.f; }
+        }
+    }
+    acc += (double)fs;
+#pragma unroll
+    for (int t = 0; t < NTG; ++t) dm[t] += (double)fm[t];
+    double m0 = NTG > 0 ? dm[0] : 0.0, m1 = NTG > 1 ? dm[1] : 0.0;
+    int z0 = 0, z1 = 0;
+    block_sum4(acc, m0, z0, z1, c.red);
+    S = acc;
+    if (NTG > 0) mass[0] = m0;
+    if (NTG > 1) {
+        double m2 = NTG > 2 ? dm[2] : 0.0, dz = 0.0;
+        block_sum4(m1, m2, z0, z1, c.red);
+        mass[1] = m1;
+        if (NTG > 2) mass[2] = m2;
+        (void)dz;
+    }
+}
+
+// exp pass of the id-order path: e stored in place (-0 for non-candidates),
+// fp64 sum of fp32 groups of four.
+template <bool SCALE>
+__device__ __forceinline__ double exp_store_pass(Ctx &c) {
+    Vars *v = c.v;
+    const int nslots = v->nslots;
+    const float mx = v->mx, thr = v->thr;
+    float4 *r4 = reinterpret_cast<float4 *>(c.row);
+    const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
+    double S = 0.0;
+    for (int s = threadIdx.x; s < nslots; s += NT) {
+        const float4 x = r4[s];
+        float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
+        if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
+        const float2 xa = make_float2(a.x >= thr ? __fsub_rn(a.x, mx) : -DNC,
+                                      a.y >= thr ? __fsub_rn(a.y, mx) : -DNC);
+        const float2 xb = make_float2(b.x >= thr ? __fsub_rn(b.x, mx) : -DNC,
+                                      b.y >= thr ? __fsub_rn(b.y, mx) : -DNC);
+        float2 ea = exp_pair(xa), eb = exp_pair(xb);
         const float2 g = __fadd2_rn(ea, eb);
         S += (double)__fadd_rn(g.x, g.y);
-        if (s < nslots) r4[s] = make_float4(ea.x, ea.y, eb.x, eb.y);
+        ea.x = a.x >= thr ? ea.x : -0.0f;
+        ea.y = a.y >= thr ? ea.y : -0.0f;
+        eb.x = b.x >= thr ? eb.x : -0.0f;
+        eb.y = b.y >= thr ? eb.y : -0.0f;
+        r4[s] = make_float4(ea.x, ea.y, eb.x, eb.y);
     }
-    if (tail) atomicAdd(&hsh[KTAIL], (unsigned)tail);
     return block_sum_d(S, c.red);
+}
+
+// Window list entries after the exact pass, self-contained 64-bit keys:
+//   bits 63..32  ~bits(p)        (probability descending)
+//   bits 31..15  id              (then id ascending: the stable sort's order)
+//   bits 12..2   bucket of d = max - l
+//   bits  1..0   edge + 1        (edge: -1 / +1 within rounding of the lower /
+//                                 upper bucket edge, else 0)
+static_assert(NB == 2048, "list keys hold an 11-bit bucket");
+__device__ __forceinline__ unsigned long long list_key(float p, int id, int bkt, int edge) {
+    return ((unsigned long long)(~__float_as_uint(p)) << 32) |
+           (((unsigned)id << 15) | ((unsigned)bkt << 2) | (unsigned)(edge + 1));
+}
+__device__ __forceinline__ int lk_id(unsigned long long k) { return (int)((unsigned)k >> 15); }
+__device__ __forceinline__ int lk_bkt(unsigned long long k) {
+    return (int)(((unsigned)k >> 2) & 2047u);
+}
+__device__ __forceinline__ int lk_edge(unsigned long long k) { return (int)((unsigned)k & 3u) - 1; }
+
+// Exclusive block scan of three doubles and three ints (scratch `wd`, `wi`:
+// 3 * NW each).
+__device__ __forceinline__ void block_xscan3(double (&m)[3], int (&n)[3], double *wd, int *wi) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    double im[3];
+    int in[3];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) { im[t] = warp_iscan(m[t], lane); in[t] = warp_iscan(n[t], lane); }
+    if (lane == 31) {
+#pragma unroll
+        for (int t = 0; t < 3; ++t) { wd[3 * warp + t] = im[t]; wi[3 * warp + t] = in[t]; }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        double bm = 0.0;
+        int bn = 0;
+        for (int w = 0; w < warp; ++w) { bm += wd[3 * w + t]; bn += wi[3 * w + t]; }
+        m[t] = bm + (im[t] - m[t]);
+        n[t] = bn + (in[t] - n[t]);
+    }
+    __syncthreads();
+}
+
+// One target over the sorted window list: the first entry of window
+// [lo, hi] (in list order) where the running mass from m0 crosses T (GE /
+// GT), or whose position from cnt0 equals m (POS).  Thread-contiguous runs
+// [j0, j1) with the window's exclusive prefix (pre_m, pre_n) in front.
+// True when found and clear of the window's outer edges (a logit a few ulps
+// across an outer edge can share the probability and belong on either side).
+__device__ __forceinline__ bool resolve_fast(Ctx &c, const unsigned long long *list, int nl,
+                                             int j0, int j1, int lo, int hi, double m0, int cnt0,
+                                             double pre_m, int pre_n, int mode, double T, int m,
+                                             Sel &out) {
+    Vars *v = c.v;
+    if (mode == T_POS ? (m < cnt0)
+                      : (((mode == T_MASS_GE) ? (m0 >= T) : (m0 > T)) && cnt0 > 0))
+        return false;  // the crossing lies above the window
+    double cs = m0 + pre_m;
+    int pos = cnt0 + pre_n;
+    int hit = INT_MAX, hpos = 0;
+    double hcs = 0.0;
+    for (int j = j0; j < j1; ++j) {
+        const unsigned long long k = list[j];
+        const int b = lk_bkt(k);
+        if (b < lo || b > hi) continue;
+        cs += (double)key_p(k);
+        const bool ok = (mode == T_MASS_GE) ? (cs >= T) : (mode == T_MASS_GT) ? (cs > T)
+                                                                              : (pos == m);
+        if (ok) { hit = j; hcs = cs; hpos = pos; break; }
+        ++pos;
+    }
+    const int best = block_min_i(hit, c.red);
+    if (best == INT_MAX) return false;  // below the window
+    if (hit == best) { v->cs = hcs; v->own = hpos; }
+    __syncthreads();
+    const unsigned long long k = list[best];
+    out.found = 1;
+    out.pos = v->own;
+    out.cs = v->cs;
+    out.id = lk_id(k);
+    out.p = key_p(k);
+    out.tie = (best > 0 && key_p(list[best - 1]) == out.p) ||
+              (best + 1 < nl && key_p(list[best + 1]) == out.p);
+    __syncthreads();
+    const int b = lk_bkt(k), e = lk_edge(k);
+    return !((b == lo && e < 0) || (b == hi && e > 0));
+}
+
+// Probability window [plo, phi] covering buckets [b0, b1] of width w (for
+// the slow path's first exact pass).
+__device__ __forceinline__ void pwin_of(int b0, int b1, float w, float inv_sum, float &plo,
+                                        float &phi) {
+    phi = (b0 <= 0) ? PINF : __fmul_rn(exp_one(-((float)b0 - 0.5f) * w), inv_sum);
+    plo = __fmul_rn(exp_one(-((float)b1 + 0.5f) * w), inv_sum);
 }
 
 template <bool SCALE>
 __device__ __forceinline__ void full_path(Ctx &c) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots;
-    const float mx = v->mx, thr = v->thr, inv_temp = v->inv_temp;
+    const float mx = v->mx, thr = v->thr;
     float4 *r4 = reinterpret_cast<float4 *>(c.row);
-    uint32_t *hcnt = reinterpret_cast<uint32_t *>(c.scr);
-    unsigned long long *lists = reinterpret_cast<unsigned long long *>(c.scr + NB * 4);
+    uint32_t *hc = reinterpret_cast<uint32_t *>(c.scr);
+    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr);
     const float top_p = v->top_p;
     const int top_k = v->top_k;
 
@@ -1488,22 +1650,21 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         write_result(c, last, __int_as_float(0x7fc00000), lazy ? 5 : 7, cnt, cnt, 1);
         return;
     }
-    for (int i = threadIdx.x; i < NB; i += NT) hcnt[i] = 0;
     // bucket geometry over d = max - l
     float dmax = __fsub_rn(mx, v->xmin);
     if (v->min_p > 0.0f) dmax = fminf(dmax, __fsub_rn(mx, thr));
+    const bool clamp = !(dmax <= DCAP);
     dmax = fminf(dmax, DCAP);
     if (!(dmax > 1e-30f)) dmax = 1.0f;
     const float inv_w = __fdiv_rn((float)NB - 1.5f, dmax);
     const float w = __fdiv_rn(1.0f, inv_w);
+    for (int i = threadIdx.x; i < NB; i += NT) hc[i] = 0;
+    if (threadIdx.x == 0) v->ln0 = 0;
     __syncthreads();
-    // exp pass (src/model.c:306-310): e = exp(l - max) for l >= thr stored in
-    // place, -0 for non-candidates (adds nothing; the sign marks them);
-    // counts of max - l buckets; fp64 sum of fp32 groups of four
-    double S = exp_pass<SCALE>(c, dmax, inv_w);
-    const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
-    // estimate from bucket counts x bucket-centre probabilities; each thread
-    // owns BPT consecutive buckets
+    if (clamp) hist_pass<SCALE, true>(c, inv_w, dmax);
+    else hist_pass<SCALE, false>(c, inv_w, dmax);
+    __syncthreads();
+    // bucket scan: counts exactly, masses estimated from bucket centres
     const int bb = BPT * threadIdx.x;
     int cb[BPT];
     double mb[BPT];
@@ -1511,8 +1672,8 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     double msum = 0.0;
 #pragma unroll
     for (int q = 0; q < BPT; ++q) {
-        cb[q] = (int)hcnt[bb + q];
-        mb[q] = (double)cb[q] * (double)__fmul_rn(exp_one(-(float)(bb + q) * w), inv_sum);
+        cb[q] = (int)hc[bb + q];
+        mb[q] = (double)cb[q] * (double)exp_one(-(float)(bb + q) * w);
         csum += cb[q];
         msum += mb[q];
     }
@@ -1520,12 +1681,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     const double mex = block_xscan_d(msum, mt, c.red);
     int ncand;
     const int cex = block_xscan_i(csum, ncand, c.red);
-    if (threadIdx.x == 0) {
-        v->inv_sum = inv_sum;
-        v->n_cand = ncand;
-        v->w = w;
-        v->S = S;
-    }
+    if (threadIdx.x == 0) { v->n_cand = ncand; v->bc = NB; v->bk = NB; v->bd0 = NB; }
     if (ncand == 0) {  // argmax guard (src/model.c:296-303)
         release_row(c);
         const int id = guard_argmax(c);
@@ -1534,6 +1690,8 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
     const bool lazy = (top_p >= 1.0f) && (top_k <= 0 || top_k >= ncand);
     if (lazy) {
+        const double S = exp_store_pass<SCALE>(c);
+        const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
         // CDF walk in id order (src/model.c:319-320): contiguous segments
         const int Q = (nslots + NT - 1) / NT;
         const int s0 = threadIdx.x * Q, s1 = min(nslots, s0 + Q);
@@ -1557,7 +1715,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         const float r = __fmul_rn(v->u, __double2float_rn(total));
         const int cand_t = ((double)r < pre + seg && seg > 0.0) ? (int)threadIdx.x : INT_MAX;
         const int owner = block_min_i(cand_t, c.red);
-        if (threadIdx.x == 0) { v->res_id = -1; v->res_p = 0.f; }
+        if (threadIdx.x == 0) { v->res_id = -1; v->res_p = 0.f; v->inv_sum = inv_sum; }
         __syncthreads();
         if ((int)threadIdx.x == owner) {
             // a rounding difference at a segment start can push the crossing
@@ -1591,102 +1749,159 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
 
     // ---- sorted order: nucleus cut, top_k truncation, draw -----------------
-    // targets: 0 = cut (cs >= top_p), 1 = top_k position, 2 = draw (cs > r).
-    // The draw's r = u * (float)new_sum is predicted from the estimate.
+    // Windows: the bucket each target falls in by the estimate.  Exact masses
+    // above each window come from the combined pass (inv_sum * e-mass: within
+    // ~1e-10 of the reference's sums of rounded probabilities), exact counts
+    // from the histogram; the walks inside a window use exact probabilities.
     const bool want_cut = top_p < 1.0f;
     const bool want_k = top_k > 0 && top_k < ncand;
-    // first owned bucket whose running estimate reaches T (or INT_MAX)
-    auto est_mass = [&](double T, bool strict) {
+    {
+        const double fr_c = (double)top_p * mt;  // estimated e-mass fractions
         double run = mex;
-        int hit = INT_MAX;
+        int crun = cex;
 #pragma unroll
         for (int q = 0; q < BPT; ++q) {
-            run += mb[q];
-            if (hit == INT_MAX && (strict ? (run > T) : (run >= T))) hit = bb + q;
+            const double nxt = run + mb[q];
+            if (want_cut && cb[q] > 0 && run < fr_c && nxt >= fr_c) {
+                v->bc = bb + q; v->cc = crun; v->mc = (fr_c - run) / mb[q];
+            }
+            if (want_k && top_k - 1 >= crun && top_k - 1 < crun + cb[q]) {
+                v->bk = bb + q; v->ck = crun;
+                v->ek = (run + (double)(top_k - crun) * (mb[q] / (double)cb[q])) / mt;
+            }
+            run = nxt;
+            crun += cb[q];
         }
-        return hit;
-    };
-    const int hit_c = want_cut ? est_mass((double)top_p, false) : INT_MAX;
-    int hit_k = INT_MAX;
-    double mass_k = 0.0;
-    if (want_k) {
-        const int mpos = top_k - 1;
-        int run = cex;
-        double mrun = mex;
+    }
+    __syncthreads();
+    {
+        // predicted new_sum: the reference stops at the first cumulative
+        // probability >= top_p, i.e. within one probability of top_p; the
+        // top_k estimate interpolates inside its bucket
+        double ns = want_cut ? (double)top_p : 1.0;
+        if (want_k && v->bk < NB) ns = fmin(ns, v->ek);
+        const double fr_d = (double)v->u * ns * mt;
+        double run = mex;
+        int crun = cex;
 #pragma unroll
         for (int q = 0; q < BPT; ++q) {
-            mrun += mb[q];
-            if (hit_k == INT_MAX && mpos >= run && mpos < run + cb[q]) { hit_k = bb + q; mass_k = mrun; }
-            run += cb[q];
+            const double nxt = run + mb[q];
+            if (cb[q] > 0 && run <= fr_d && nxt > fr_d) {
+                v->bd0 = bb + q; v->cd = crun; v->md = (fr_d - run) / mb[q];
+            }
+            run = nxt;
+            crun += cb[q];
         }
     }
-    if (threadIdx.x == 0) { v->bh0 = NB - 1; v->bh1 = NB - 1; v->bh2 = NB - 1; v->aux0 = mt; }
     __syncthreads();
-    if (hit_c != INT_MAX) atomicMin(&v->bh0, hit_c);
-    if (hit_k != INT_MAX) {
-        atomicMin(&v->bh1, hit_k);
-        v->aux0 = mass_k;  // estimated mass through it
+    if (threadIdx.x == 0) {
+        // mass targets get a two-bucket window: the estimated bucket and the
+        // neighbour on the side of the estimated position
+        v->bc_hi = v->bc;
+        if (want_cut && v->bc < NB) {
+            if (v->mc < 0.5 && v->bc > 0) { v->cc -= (int)hc[v->bc - 1]; v->bc -= 1; }
+            else v->bc_hi = min(v->bc + 1, NB - 1);
+        }
+        v->bd_hi = v->bd0;
+        if (v->bd0 < NB) {
+            if (v->md < 0.5 && v->bd0 > 0) { v->cd -= (int)hc[v->bd0 - 1]; v->bd0 -= 1; }
+            else v->bd_hi = min(v->bd0 + 1, NB - 1);
+        }
     }
     __syncthreads();
-    // predicted new_sum: the nucleus mass, or the top_k mass when smaller
-    double ns_est = want_cut ? (double)top_p : mt;
-    if (want_k) ns_est = fmin(ns_est, v->aux0);
-    const int hit_d = est_mass((double)v->u * ns_est, true);
-    if (hit_d != INT_MAX) atomicMin(&v->bh2, hit_d);
-    __syncthreads();
-    // windows: the estimated bucket of each target, as probability intervals
-    const bool act[3] = {want_cut, want_k, true};
-    const int bh[3] = {v->bh0, v->bh1, v->bh2};
-    int phb[3], plb[3];
-#pragma unroll
+    const int bc = want_cut ? v->bc : NB, bk = want_k ? v->bk : NB, bd = v->bd0;
+    const int bc1 = v->bc_hi, bd1 = v->bd_hi;
+    const int blo[3] = {bc, bk, bd}, bhi[3] = {bc1, bk, bd1};
+    // distinct active windows first: slot[t] = index of target t's window
+    float tl[3], th[3];
+    int slot[3] = {-1, -1, -1}, ntg = 0;
     for (int t = 0; t < 3; ++t) {
-        const float phi = (bh[t] == 0) ? PINF
-                                       : __fmul_rn(exp_one(-((float)bh[t] - 0.5f) * w), inv_sum);
-        const float plo = (bh[t] == NB - 1)
-                              ? 0.0f
-                              : __fmul_rn(exp_one(-((float)bh[t] + 0.5f) * w), inv_sum);
-        phb[t] = act[t] ? __float_as_int(phi) : INT_MAX;
-        plb[t] = act[t] ? __float_as_int(plo) : INT_MAX;
+        if (blo[t] >= NB) continue;
+        const float lo = MAGIC + (float)blo[t], hi = MAGIC + (float)(bhi[t] + 1);
+        int q = 0;
+        while (q < ntg && !(tl[q] == lo && th[q] == hi)) ++q;
+        if (q == ntg) { tl[q] = lo; th[q] = hi; ++ntg; }
+        slot[t] = q;
     }
-    if (threadIdx.x == 0) { v->ln0 = 0; v->ln1 = 0; v->ln2 = 0; }
+    for (int t = ntg; t < 3; ++t) { tl[t] = MAGIC; th[t] = MAGIC; }
+    double mass[3] = {0.0, 0.0, 0.0};
+    double S = 0.0;
+    if (clamp) {
+        if (ntg <= 1) combined_pass<SCALE, true, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, true, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, true, 3>(c, inv_w, dmax, tl, th, mass, S);
+    } else {
+        if (ntg <= 1) combined_pass<SCALE, false, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, false, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, false, 3>(c, inv_w, dmax, tl, th, mass, S);
+    }
+    const double mass_c = slot[0] >= 0 ? mass[slot[0]] : 0.0;
+    const double mass_k = slot[1] >= 0 ? mass[slot[1]] : 0.0;
+    const double mass_d = slot[2] >= 0 ? mass[slot[2]] : 0.0;
+    const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
+    if (threadIdx.x == 0) { v->inv_sum = inv_sum; v->S = S; }
     __syncthreads();
-    const int mask = (want_cut ? 1 : 0) | (want_k ? 2 : 0) | 4;
-    switch (mask) {
-        case 5: window_pass<5>(c, phb[0], phb[1], phb[2], plb[0], plb[1], plb[2]); break;
-        case 6: window_pass<6>(c, phb[0], phb[1], phb[2], plb[0], plb[1], plb[2]); break;
-        default: window_pass<7>(c, phb[0], phb[1], phb[2], plb[0], plb[1], plb[2]); break;
+    const int nl = min(v->ln0, LISTCAP);
+    const bool list_ok = v->ln0 <= LISTCAP;
+    // exact probabilities and buckets of the listed elements, canonical sort
+    if (list_ok) {
+        for (int i = threadIdx.x; i < nl; i += NT) {
+            const unsigned long long e0 = list[i];
+            const int id = (int)(e0 >> 32);
+            const float l = __uint_as_float((unsigned)(e0 & 0xffffffffu));
+            const float pe = __fmul_rn(exp_one(__fsub_rn(l, mx)), inv_sum);
+            float d = __fsub_rn(mx, l);
+            if (clamp) d = fminf(d, dmax);
+            const float kf = __fmaf_rn(d, inv_w, MAGIC);
+            const int bk_ = __float_as_int(kf) - MAGIC_I;
+            // within 2e-3 of a bucket edge, a logit a few ulps away (possibly
+            // the same probability) may sit in the neighbouring bucket
+            const float fr = __fmaf_rn(d, inv_w, -(float)bk_);
+            const int eg = (fr > 0.5f - 2e-3f) ? 1 : (fr < -(0.5f - 2e-3f)) ? -1 : 0;
+            list[i] = list_key(pe, id, bk_, eg);
+        }
+        __syncthreads();
+        sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
     }
-    PassOut o[3];
-#pragma unroll
-    for (int t = 0; t < 3; ++t) {
-        o[t].above = act[t] ? v->wab[t] : 0.0;
-        o[t].cnt_above = act[t] ? v->wca[t] : 0;
-        o[t].in_cnt = act[t] ? (t == 0 ? v->ln0 : t == 1 ? v->ln1 : v->ln2) : 0;
-        o[t].in_mass = 0.0;
-    }
-    // the row buffer is free: the next row's copy overlaps what follows
+    // release: the row buffer is no longer read on the common path (the rare
+    // fallbacks read global memory)
     release_row(c);
     __syncthreads();
-    int *rank = reinterpret_cast<int *>(c.scr);  // reuses the histogram area
+
+    const double ip = (double)inv_sum;
+    // per-thread runs of the sorted list and each window's prefix in front
+    const int RQ = (nl + NT - 1) / NT;
+    const int j0 = list_ok ? min(nl, (int)threadIdx.x * RQ) : 0;
+    const int j1 = list_ok ? min(nl, j0 + RQ) : 0;
+    const int wlo[3] = {bc, bk, bd}, whi[3] = {bc1, bk, bd1};
+    double pm[3] = {0.0, 0.0, 0.0};
+    int pn[3] = {0, 0, 0};
+    for (int j = j0; j < j1; ++j) {
+        const unsigned long long k = list[j];
+        const int b = lk_bkt(k);
+        const double p = (double)key_p(k);
 #pragma unroll
-    for (int t = 0; t < 3; ++t) {
-        if (!act[t]) continue;
-        if (o[t].in_cnt <= LCAP) {
-            sort_keys(lists + t * LCAP, o[t].in_cnt, rank, LCAP);
-            o[t].in_mass = list_mass(lists + t * LCAP, o[t].in_cnt, c.red);
-        }
+        for (int t = 0; t < 3; ++t)
+            if (b >= wlo[t] && b <= whi[t]) { pm[t] += p; ++pn[t]; }
     }
+    block_xscan3(pm, pn, reinterpret_cast<double *>(c.scr + LISTCAP * 8),
+                 reinterpret_cast<int *>(c.scr + LISTCAP * 8 + 3 * NW * 8));
 
     int n = ncand;
-    double new_sum = 0.0;
+    double new_sum = S * ip;  // total probability mass (fallback when no cut)
     Sel tail;
     tail.found = 0; tail.id = -1; tail.p = 0.f; tail.tie = 0; tail.pos = ncand - 1; tail.cs = 0.0;
     bool partial = false;
+    float pw_lo = 0.0f, pw_hi = PINF;
     if (want_cut) {
         Sel cut;
-        if (!(o[0].in_cnt <= LCAP &&
-              resolve_list(c, lists, o[0], T_MASS_GE, (double)top_p, 0, cut)))
-            cut = select_slow(c, SCALE, T_MASS_GE, (double)top_p, 0, bh[0]);
+        const bool ok = list_ok && bc < NB &&
+                        resolve_fast(c, list, nl, j0, j1, bc, bc1, mass_c * ip, v->cc, pm[0],
+                                     pn[0], T_MASS_GE, (double)top_p, 0, cut);
+        if (!ok) {
+            if (bc < NB) pwin_of(bc - 4, bc1 + 4, w, inv_sum, pw_lo, pw_hi);
+            cut = select_slow(c, SCALE, T_MASS_GE, (double)top_p, 0, pw_lo, pw_hi);
+        }
         if (cut.found) {
             n = cut.pos + 1;
             partial = (ncand > 256) && (cut.pos < 256);  // src/model.c:327-356
@@ -1696,18 +1911,30 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
     if (want_k && top_k < n) {  // src/model.c:102-103
         Sel tk;
-        if (!(o[1].in_cnt <= LCAP &&
-              resolve_list(c, lists + LCAP, o[1], T_POS, 0.0, top_k - 1, tk)))
-            tk = select_slow(c, SCALE, T_POS, 0.0, top_k - 1, bh[1]);
+        const bool ok = list_ok && bk < NB &&
+                        resolve_fast(c, list, nl, j0, j1, bk, bk, mass_k * ip, v->ck, pm[1],
+                                     pn[1], T_POS, 0.0, top_k - 1, tk);
+        if (!ok) {
+            pw_lo = 0.0f; pw_hi = PINF;
+            if (bk < NB) pwin_of(bk - 4, bk + 4, w, inv_sum, pw_lo, pw_hi);
+            tk = select_slow(c, SCALE, T_POS, 0.0, top_k - 1, pw_lo, pw_hi);
+        }
         n = top_k;
         new_sum = tk.cs;
         tail = tk;
     }
     const float r = __fmul_rn(v->u, __double2float_rn(new_sum));
     Sel d;
-    if (!(o[2].in_cnt <= LCAP &&
-          resolve_list(c, lists + 2 * LCAP, o[2], T_MASS_GT, (double)r, 0, d)))
-        d = select_slow(c, SCALE, T_MASS_GT, (double)r, 0, bh[2]);
+    {
+        const bool ok = list_ok && bd < NB &&
+                        resolve_fast(c, list, nl, j0, j1, bd, bd1, mass_d * ip, v->cd, pm[2],
+                                     pn[2], T_MASS_GT, (double)r, 0, d);
+        if (!ok) {
+            pw_lo = 0.0f; pw_hi = PINF;
+            if (bd < NB) pwin_of(bd - 4, bd1 + 4, w, inv_sum, pw_lo, pw_hi);
+            d = select_slow(c, SCALE, T_MASS_GT, (double)r, 0, pw_lo, pw_hi);
+        }
+    }
     int id;
     float pp;
     if (d.found && d.pos < n) { id = d.id; pp = d.p; }
@@ -1732,6 +1959,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     c.B = P.B;
     c.V = P.V;
     c.err = P.err;
+    c.sched = P.sched;
     c.out_id = P.out_id;
     c.out_prob = P.out_prob;
     c.stats = P.stats;
@@ -1745,11 +1973,13 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         fence_mbar_init();
         v->fail = 0;
         if ((int)blockIdx.x < P.B) issue_row(P.logits + (int64_t)blockIdx.x * P.ld, V, c.mbar, c.row);
+        const int pre = (int)(blockIdx.x + gridDim.x);
+        if (pre < P.B) prefetch_row(P.logits + (int64_t)pre * P.ld, V);
     }
     __syncthreads();
 
     uint32_t it = 0;
-    for (int row = blockIdx.x; row < P.B; row += gridDim.x, ++it) {
+    for (int row = blockIdx.x; row < P.B; ++it) {
         c.rowid = row;
         c.parity = it & 1u;
         c.g = P.logits + (int64_t)row * P.ld;
@@ -1764,18 +1994,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             v->s_int0 = (i0 + sh) >> 2;
             v->s_int1 = v->s_int0 + (n4 >> 2);
             v->released = 0;
-            // warm L2 with the row after the next one (the next row's copy is
-            // issued during this row)
-            const int nrow = row + 2 * (int)gridDim.x;
-            if (nrow < P.B) {
-                const float *ng = P.logits + (int64_t)nrow * P.ld;
-                const int nsh = (int)(((uintptr_t)ng & 15u) >> 2);
-                const int ni0 = nsh ? 4 - nsh : 0;
-                if (ni0 < V) {
-                    const int nn4 = ((V - ni0) >> 2) << 2;
-                    if (nn4 >= 16) prefetch_l2(ng + ni0, (uint32_t)nn4 * 4u);
-                }
-            }
             const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
             v->temp = kn.temp;
             v->penalty = kn.penalty;
@@ -1828,7 +2046,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             if (tid == 0)
                 for (int ch = 0; ch < NCHUNK; ++ch) (void)mbar_wait(&c.mbar[ch], c.parity);
             __syncthreads();
-            return;
+            break;
         }
         if (greedy) {
             block_argmax(gv, gi, c.red);
@@ -1858,9 +2076,19 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         __syncthreads();
         if (!v->released) release_row(c);
         __syncthreads();
+        row = v->next_row;
     }
-    // the last release of this CTA targets a row >= B and issues nothing, so
-    // no copy is in flight when the kernel ends
+    // the last release of this CTA claimed a row >= B and issued nothing, so
+    // no copy is in flight when the kernel ends.  The last CTA to finish
+    // rewinds the schedule for the next launch.
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(&P.sched[1], 1) == (int)gridDim.x - 1) {
+            P.sched[0] = 0;
+            P.sched[1] = 0;
+            __threadfence();
+        }
+    }
 }
 
 }  // namespace

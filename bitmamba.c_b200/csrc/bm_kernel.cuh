@@ -16,7 +16,7 @@ constexpr int NB = 2048;      // full-vocabulary path: logit buckets
 constexpr int WCAP = 1024;    // full-vocabulary path: window list capacity
 constexpr int KCAP = 2048;    // top_k path: candidate list capacity
 constexpr int NCHUNK = 8;     // bulk-copy chunks (one mbarrier each) per row
-constexpr int SCRATCH = 20480;
+constexpr int SCRATCH = 22528;
 
 struct Params {
     const float *logits;
@@ -30,7 +30,9 @@ struct Params {
     int32_t *out_id;
     float *out_prob;
     bm_row_stats_t *stats;
-    int *err;  // device error word: bit 0 = bounded wait expired
+    int *err;    // device error word: bit 0 = bounded wait expired
+    int *sched;  // row schedule: [0] rows claimed past the first grid, [1] CTAs
+                 // finished; both zero between launches
 };
 
 // Dynamic shared memory the kernel needs for vocabulary V.

@@ -143,8 +143,9 @@ int bm_ctx_create(int device, bm_ctx_t **out) {
     c->smem_optin = prop.sharedMemPerBlockOptin;
     c->max_vocab = bmk::max_vocab(c->smem_optin);
     e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    // error word and the two row-schedule counters
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_err, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 4 * sizeof(int));
     if (e == cudaSuccess) e = bmk::prepare(c->max_vocab);
     if (e != cudaSuccess) {
         int rc = cuda_fail(e, "context setup");
@@ -183,7 +184,8 @@ int bm_ctx_check(bm_ctx_t *c) {
     int h = 0;
     CK(cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h) {
-        CK(cudaMemset(c->d_err, 0, sizeof(int)));
+        // a CTA that stopped early may leave the schedule counters behind
+        CK(cudaMemset(c->d_err, 0, 4 * sizeof(int)));
         return fail(BM_ERR_DEVICE, "device error flag 0x%x (bounded wait expired or select "
                                    "did not converge)", h);
     }
@@ -213,6 +215,7 @@ int bm_sample_batch(bm_ctx_t *c, const float *d_logits, int B, int V, int64_t ld
     p.out_prob = d_out_prob;
     p.stats = d_stats;
     p.err = c->d_err;
+    p.sched = c->d_err + 1;
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     int grid = B < c->sms ? B : c->sms;
     CK(bmk::launch(p, grid, s));
