@@ -61,6 +61,25 @@ def make_logits(torch, B, V, seed, device):
     return z.contiguous()
 
 
+def shard_rows(total, world, rank):
+    """Rows [start, start + count) of a global batch of `total` rows owned by
+    `rank` (even split, the remainder to the first ranks).  Rows are
+    independent, so sharding needs no collective."""
+    base, rem = divmod(total, world)
+    start = rank * base + min(rank, rem)
+    return start, base + (1 if rank < rem else 0)
+
+
+def max_over_ranks(dist, x, device=None):
+    """The maximum of a per-rank time over all ranks (identity on 1 rank)."""
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def ref_uniforms(B, seed=RNG_SEED):
     """rng_float() stream of the reference (src/utils.c:117-140)."""
     s = seed if seed else 0x853C49E6748FEA9B
@@ -157,17 +176,25 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback 6650 GB/s (pool measurement)"
 
 
+def oracle_batch(logits_host):
+    """The workload rows as an oracle batch (knobs broadcast)."""
+    sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests", "golden")]
+    import synth
+    B = logits_host.shape[0]
+    return synth.Batch(logits_host, np.zeros(0, np.int32), np.zeros(B + 1, np.int64),
+                       np.full(B, KNOBS["temp"], np.float32),
+                       np.full(B, KNOBS["penalty"], np.float32),
+                       np.full(B, KNOBS["min_p"], np.float32),
+                       np.full(B, KNOBS["top_p"], np.float32),
+                       np.full(B, KNOBS["top_k"], np.int32))
+
+
 def cpu_leg(logits_host, u, threads, kind_pref="reference"):
     """Time the reference's C sampler (oracle/_ref, else the oracle port) on
     host rows.  Returns (ids, seconds, kind)."""
     sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests", "golden")]
     import oracle
-    import synth
-    B, V = logits_host.shape
-    b = synth.Batch(logits_host, np.zeros(0, np.int32), np.zeros(B + 1, np.int64),
-                    np.full(B, KNOBS["temp"], np.float32), np.full(B, KNOBS["penalty"], np.float32),
-                    np.full(B, KNOBS["min_p"], np.float32), np.full(B, KNOBS["top_p"], np.float32),
-                    np.full(B, KNOBS["top_k"], np.int32))
+    b = oracle_batch(logits_host)
     if kind_pref == "reference" and oracle.has_ref():
         t = time.perf_counter()
         ids = oracle.ref_sample_batch_mt(b, u, threads)
@@ -256,7 +283,10 @@ def run_ours(args):
     knobs = bm.knobs_array(KNOBS["temp"], KNOBS["penalty"], KNOBS["min_p"], KNOBS["top_p"],
                            KNOBS["top_k"])
     knobs_d = torch.from_numpy(knobs.view(np.uint8).copy()).to(dev)
-    u_host = ref_uniforms(B)
+    # this rank's rows of the global batch (weak scaling: B rows per rank) and
+    # their slice of the global uniform stream
+    start, count = shard_rows(world * B, world, rank)
+    u_host = ref_uniforms(world * B)[start:start + count]
     u_d = torch.from_numpy(u_host).to(dev)
     out_d = torch.empty(B, dtype=torch.int32, device=dev)
     # a dedicated stream: torch's legacy default stream has handle 0, which the
@@ -297,11 +327,7 @@ def run_ours(args):
     clocks.stop()
     ctx.check()
     ms = e0.elapsed_time(e1)
-    ms_max = ms
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(dist, ms, dev)
     value = world * B * args.steps / (ms_max / 1e3)
     kernel_ms = ms / args.steps
     alg_bytes = B * (4 * V + 4 + 4) + 32  # logits, uniform, id, knobs (no history)
@@ -337,11 +363,7 @@ def run_ours(args):
         f1.record(cs)
         torch.cuda.synchronize(dev)
         barrier()
-        e_ms = f0.elapsed_time(f1)
-        if dist is not None:
-            t = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
+        e_ms = max_over_ranks(dist, f0.elapsed_time(f1), dev)
         if not np.array_equal(h_ids.numpy(), ids_dev):
             raise SystemExit("e2e ids differ from the device-resident run")
         e2e = {"value": world * B * n_e2e / (e_ms / 1e3), "unit": UNIT,
@@ -361,6 +383,18 @@ def run_ours(args):
                          f"row-parallel pthreads"}
         same = int((ids_cpu == ids_dev[:n]).sum())
         parity = {"rows": n, "identical_ids": same}
+        if same < n:
+            # classify the differing rows with the oracle's CDF margins: a row
+            # whose draw or cut lies within 1e-5 of a boundary is exempt
+            sys.path[:0] = [os.path.join(ROOT, "tests")]
+            import oracle
+            import parity as parity_rule
+            rb = oracle_batch(h)
+            _, _, res = oracle.sample_batch(rb, u_host[:n], threads=threads)
+            rep = parity_rule.compare(ids_dev[:n], None, ids_cpu, None, res)
+            parity.update({"exempt_mismatch": rep["exempt_mismatch"], "bad": rep["bad"],
+                           "rule": "ids identical except draws/cuts within 1e-5 of a CDF "
+                                   "boundary"})
 
     if dist is not None:
         dist.barrier()

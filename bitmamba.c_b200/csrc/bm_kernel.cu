@@ -16,15 +16,21 @@
 //             threshold collected in the same pass, exact emulation of its
 //             min-heap (the heap layout decides the CDF walk order), survivor
 //             softmax, stable descending sort, nucleus cut and draw.
-//   full      other top_k: exp(l - max) into shared memory with a bucket-count
-//             histogram over max - l, then either the id-order walk
-//             (src/model.c:319-320) or one exact pass that resolves the
-//             nucleus cut, the top_k position and the draw in
-//             (probability desc, id asc) order -- the order the reference's
-//             stable qsort produces -- through windows estimated from the
-//             histogram.  Rows where the reference's top-256 heap path applies
-//             and ties make its layout visible are replayed exactly
-//             (src/model.c:327-356).
+//   full      other top_k: a bucket-count histogram over d = max - l (one
+//             shared atomic per candidate), then either the id-order walk
+//             (src/model.c:319-320) or, for the sorted order, windows of one
+//             or two buckets around the estimated nucleus cut, top_k position
+//             and draw; one exact pass computes exp(l - max), its fp64 sum,
+//             the exact mass above each window and lists the window elements;
+//             the list is sorted in (probability desc, id asc) order -- the
+//             order the reference's stable qsort produces -- and every target
+//             is resolved block-parallel over it.  Rows where the reference's
+//             top-256 heap path applies and ties make its layout visible are
+//             replayed exactly (src/model.c:327-356); a target that falls
+//             outside its window takes exact passes over global memory.
+//   schedule  the first gridDim.x rows go one per CTA, every later row to the
+//             CTA that frees its row buffer first (atomic counter, rewound by
+//             the last CTA to finish).
 //
 // Arithmetic that decides ids uses the reference's fp32 operations (no
 // contraction: explicit __fmul_rn/__fadd_rn/__fdiv_rn; the library is built

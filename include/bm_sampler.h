@@ -132,7 +132,9 @@ void *bm_ctx_stream(bm_ctx_t *ctx);
  *   stream              a cudaStream_t (NULL = the context's stream).
  * Logits are read-only (the reference scales them in place; this does not).
  * Asynchronous: returns after enqueueing.  Call bm_ctx_check to collect the
- * device error flag.
+ * device error flag.  Rows are handed to SMs by a counter that lives in the
+ * context: launches on one context must not overlap (issue them on one
+ * stream, or order them); use one context per concurrently running stream.
  */
 int bm_sample_batch(bm_ctx_t *ctx, const float *d_logits, int B, int V,
                     int64_t ld, const int32_t *d_hist,
