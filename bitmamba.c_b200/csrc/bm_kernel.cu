@@ -2049,8 +2049,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         if (__syncthreads_or(v->fail)) {
             // a bounded wait expired: wait (bounded) for this row's copies,
             // then stop; the host sees the error flag
-            if (tid == 0)
+            if (tid == 0) {
                 for (int ch = 0; ch < NCHUNK; ++ch) (void)mbar_wait(&c.mbar[ch], c.parity);
+                if (P.mark_failed_rows) P.out_id[row] = -1;
+            }
             __syncthreads();
             break;
         }
@@ -2097,9 +2099,16 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     }
 }
 
+// Scratch of the allocation-free entry point (one copy per device).
+static __device__ __align__(256) int g_noalloc_scratch[NOALLOC_WORDS];
+
 }  // namespace
 
 size_t smem_bytes(int V) { return layout(V).total; }
+
+cudaError_t noalloc_scratch(int **out) {
+    return cudaGetSymbolAddress(reinterpret_cast<void **>(out), g_noalloc_scratch);
+}
 
 int max_vocab(size_t limit) {
     int lo = 1, hi = 1 << 20;

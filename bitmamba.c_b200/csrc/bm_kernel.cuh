@@ -33,6 +33,8 @@ struct Params {
     int *err;    // device error word: bit 0 = bounded wait expired
     int *sched;  // row schedule: [0] rows claimed past the first grid, [1] CTAs
                  // finished; both zero between launches
+    int mark_failed_rows = 0;  // nonzero: a row whose bounded wait expired
+                               // gets id -1
 };
 
 // Dynamic shared memory the kernel needs for vocabulary V.
@@ -43,5 +45,10 @@ int max_vocab(size_t smem_limit);
 cudaError_t launch(const Params &p, int grid, cudaStream_t s);
 // One-time per-device attribute setup (dynamic shared memory opt-in).
 cudaError_t prepare(int V);
+// The calling thread's current device's copy of a file-scope device array of
+// NOALLOC_WORDS ints (256-byte aligned): word 0 error bits, words 1-2 the row
+// schedule counters (zero at module load, returned to zero by every launch).
+constexpr int NOALLOC_WORDS = 64;
+cudaError_t noalloc_scratch(int **out);
 
 }  // namespace bmk

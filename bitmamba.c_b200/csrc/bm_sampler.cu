@@ -74,16 +74,15 @@ int grow(T **p, size_t *cap, size_t need) {
     return BM_OK;
 }
 
-int check_batch_args(const bm_ctx_t *ctx, const void *logits, int B, int V, int64_t ld,
-                     const void *hist, const void *off, const void *knobs,
-                     int64_t knob_stride, const void *uniform, const void *out_id) {
-    if (!ctx) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+int check_args(int max_vocab, const void *logits, int B, int V, int64_t ld, const void *hist,
+               const void *off, const void *knobs, int64_t knob_stride, const void *uniform,
+               const void *out_id) {
     if (B < 0) return fail(BM_ERR_INVALID_ARG, "B = %d < 0", B);
     if (B == 0) return BM_OK;
     if (V < 1) return fail(BM_ERR_INVALID_ARG, "V = %d < 1", V);
-    if (V > ctx->max_vocab)
+    if (V > max_vocab)
         return fail(BM_ERR_UNSUPPORTED, "V = %d exceeds the row buffer limit %d", V,
-                    ctx->max_vocab);
+                    max_vocab);
     if (ld < V) return fail(BM_ERR_INVALID_ARG, "ld = %lld < V = %d", (long long)ld, V);
     if (!logits || !knobs || !out_id)
         return fail(BM_ERR_INVALID_ARG, "logits, knobs and out_id must be non-NULL");
@@ -94,6 +93,54 @@ int check_batch_args(const bm_ctx_t *ctx, const void *logits, int B, int V, int6
         return fail(BM_ERR_INVALID_ARG, "knob_stride must be 0 or 1");
     if (reinterpret_cast<uintptr_t>(logits) % 4)
         return fail(BM_ERR_INVALID_ARG, "logits not 4-byte aligned");
+    return BM_OK;
+}
+
+int check_batch_args(const bm_ctx_t *ctx, const void *logits, int B, int V, int64_t ld,
+                     const void *hist, const void *off, const void *knobs,
+                     int64_t knob_stride, const void *uniform, const void *out_id) {
+    if (!ctx) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    return check_args(ctx->max_vocab, logits, B, V, ld, hist, off, knobs, knob_stride, uniform,
+                      out_id);
+}
+
+// Per-device state of the allocation-free entry point: the scratch address
+// and the launch shape, set up once.
+constexpr int NOALLOC_MAXDEV = 64;
+constexpr int NOALLOC_MAX_ROWS = 1 << 30;  // keeps the row counter inside int
+struct NoallocDev {
+    int ready;
+    int sms;
+    int max_vocab;
+    int *scratch;
+};
+NoallocDev g_noalloc[NOALLOC_MAXDEV];
+std::mutex g_noalloc_mu;
+
+int noalloc_setup(int dev, const NoallocDev **out) {
+    if (dev < 0 || dev >= NOALLOC_MAXDEV)
+        return fail(BM_ERR_UNSUPPORTED, "device %d beyond the %d devices supported", dev,
+                    NOALLOC_MAXDEV);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoallocDev &d = g_noalloc[dev];
+    if (!d.ready) {
+        int major = 0, sms = 0, optin = 0;
+        CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+        if (major != 10)
+            return fail(BM_ERR_NO_DEVICE, "device %d is sm_%dx; this library is built for sm_100a",
+                        dev, major);
+        CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        int *scratch = nullptr;
+        CK(bmk::noalloc_scratch(&scratch));
+        const int mv = bmk::max_vocab((size_t)optin);
+        CK(bmk::prepare(mv));
+        d.sms = sms;
+        d.max_vocab = mv;
+        d.scratch = scratch;
+        d.ready = 1;
+    }
+    *out = &d;
     return BM_OK;
 }
 
@@ -219,6 +266,42 @@ int bm_sample_batch(bm_ctx_t *c, const float *d_logits, int B, int V, int64_t ld
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     int grid = B < c->sms ? B : c->sms;
     CK(bmk::launch(p, grid, s));
+    return BM_OK;
+}
+
+int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,
+                            const int32_t *d_hist, const int64_t *d_hist_off,
+                            const bm_knobs_t *d_knobs, int64_t knob_stride,
+                            const float *d_uniform, int32_t *d_out_id, float *d_out_prob,
+                            bm_row_stats_t *d_stats, void *stream) {
+    if (B > NOALLOC_MAX_ROWS)
+        return fail(BM_ERR_INVALID_ARG, "B = %d exceeds %d rows per call", B, NOALLOC_MAX_ROWS);
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    const NoallocDev *d = nullptr;
+    int rc = noalloc_setup(dev, &d);
+    if (rc != BM_OK) return rc;
+    rc = check_args(d->max_vocab, d_logits, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
+                    d_uniform, d_out_id);
+    if (rc != BM_OK || B == 0) return rc;
+    bmk::Params p;
+    p.logits = d_logits;
+    p.ld = ld;
+    p.B = B;
+    p.V = V;
+    p.hist = d_hist;
+    p.hist_off = d_hist_off;
+    p.knobs = d_knobs;
+    p.knob_stride = knob_stride;
+    p.uniform = d_uniform;
+    p.out_id = d_out_id;
+    p.out_prob = d_out_prob;
+    p.stats = d_stats;
+    p.err = d->scratch;
+    p.sched = d->scratch + 1;
+    p.mark_failed_rows = 1;
+    const int grid = B < d->sms ? B : d->sms;
+    CK(bmk::launch(p, grid, static_cast<cudaStream_t>(stream)));
     return BM_OK;
 }
 

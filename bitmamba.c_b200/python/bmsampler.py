@@ -62,6 +62,8 @@ def lib():
         L.bm_ctx_stream.restype = _P
         L.bm_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
                                       _P, _P, _P, ctypes.c_int64, _P, _P, _P, _P, _P]
+        L.bm_sample_batch_noalloc.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                              _P, _P, _P, ctypes.c_int64, _P, _P, _P, _P, _P]
         L.bm_sample_batch_host.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int64, _P, _P, _P, ctypes.c_int64, _P,
                                            _P, _P, _P]

@@ -143,6 +143,35 @@ int bm_sample_batch(bm_ctx_t *ctx, const float *d_logits, int B, int V,
                     int32_t *d_out_id, float *d_out_prob,
                     bm_row_stats_t *d_stats, void *stream);
 
+/*
+ * bm_sample_batch without a context and without any allocation (no
+ * cudaMalloc, no host allocation).  No reference counterpart: the reference
+ * samples one row on the CPU and owns its buffers.  Same arguments and
+ * semantics as bm_sample_batch, on the calling thread's current CUDA device;
+ * stream NULL is the legacy default stream.
+ *
+ * Scratch: one file-scope device array per device (64 ints = 256 bytes,
+ * 256-byte aligned): an error word and the two row-schedule counters.  The
+ * counters must start at zero; they are zero when the module loads and every
+ * launch returns them to zero.  The first call on a device takes the array's
+ * address (cudaGetSymbolAddress) and sets the kernel's shared-memory
+ * attribute; that first call must come before any stream capture on that
+ * device.  All calls on one device share the scratch: calls that overlap in
+ * time (different streams, or threads without ordering) race on the row
+ * schedule and must not be made; order them on one stream.
+ *
+ * Limits: V <= bm_max_vocab (50292 on a B200) else BM_ERR_UNSUPPORTED;
+ * B <= 2^30 rows per call else BM_ERR_INVALID_ARG.  There is no context
+ * error flag to check: a row whose bounded wait in the kernel expired gets
+ * id -1.
+ */
+int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,
+                            const int32_t *d_hist, const int64_t *d_hist_off,
+                            const bm_knobs_t *d_knobs, int64_t knob_stride,
+                            const float *d_uniform, int32_t *d_out_id,
+                            float *d_out_prob, bm_row_stats_t *d_stats,
+                            void *stream);
+
 /* ---- batched sampling, host buffers ---------------------------------------- */
 
 /*
