@@ -53,6 +53,10 @@ constexpr int BPT = NB / NT;                            // estimate buckets per 
 constexpr int SLOW_CAP = 256;                          // rare-path list cap
 constexpr int SLOW_OFF = LISTCAP * 8 + 2048;           // rare-path scratch offset
 constexpr float PINF = __builtin_huge_valf();
+// Junk lanes of the ragged head / tail slots: below every min_p threshold
+// (>= -1e30 - 104), and max - JUNK stays finite, so exp(-(max - JUNK)) is 0
+// and its bucket key lies beyond the last bucket.
+constexpr float JUNK = -1e37f;
 constexpr size_t RED_BYTES = 2048;
 
 // GPT-2 ids the reference never penalises (src/bitmamba.h:21-24).
@@ -68,7 +72,7 @@ struct __align__(16) Vars {
     int sh, nslots, s_int0, s_int1;
     int h0, h1, released, fail;
     int kcut, kcnt, n_cand, own;
-    int bh0, bh1, bh2, pad0;
+    int bh0, bh1, bh2, clean;
     int ln0, ln1, ln2, ln3;
     int sel_found, sel_j, res_id, n_final;
     float res_p, pad1, pad2, pad3;
@@ -302,6 +306,19 @@ __device__ __forceinline__ void block_maxmin_f(float &mx, float &mn, Red r) {
     mn = warp_min(lane < NW ? r.f[NW + lane] : PINF);
     __syncthreads();
 }
+// max, min and sum at once (the sum carries the non-finite check)
+__device__ __forceinline__ void block_maxmin_chk(float &mx, float &mn, float &ck, Red r) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    mx = warp_max(mx);
+    mn = warp_min(mn);
+    ck = warp_sum(ck);
+    if (lane == 0) { r.f[warp] = mx; r.f[NW + warp] = mn; r.f[2 * NW + warp] = ck; }
+    __syncthreads();
+    mx = warp_max(lane < NW ? r.f[lane] : -PINF);
+    mn = warp_min(lane < NW ? r.f[NW + lane] : PINF);
+    ck = warp_sum(lane < NW ? r.f[2 * NW + lane] : 0.0f);
+    __syncthreads();
+}
 __device__ __forceinline__ void block_argmax(float &v, int &i, Red r) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     warp_argmax(v, i);
@@ -466,6 +483,7 @@ struct Ctx {
     float *out_prob;
     bm_row_stats_t *stats;
     int rowid;
+    int claim;  // thread 0: the row claimed to follow this one
     uint32_t parity;
     // Point the shared-memory fields at the dynamic shared array.  Called at
     // the top of every non-inlined function: pointers that arrive as
@@ -518,10 +536,7 @@ __device__ __forceinline__ void release_row(Ctx &c) {
     __syncthreads();
     if (threadIdx.x == 0) {
         c.v->released = 1;
-        // dynamic schedule: the first gridDim.x rows go one per CTA, every
-        // later row to the CTA that frees its buffer first (rows of unequal
-        // cost would otherwise leave SMs idle at the end of the launch)
-        const int next_row = (int)gridDim.x + atomicAdd(&c.sched[0], 1);
+        const int next_row = c.claim;  // claimed when this row started
         c.v->next_row = next_row;
         if (next_row < c.B) {
             issue_row(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row);
@@ -558,18 +573,21 @@ __device__ __forceinline__ float logit_g(const Ctx &c, int e, bool scale) {
 // Consume the freshly loaded row chunk by chunk: apply the penalty, fill the
 // junk lanes of the ragged first / last slots with NaN, and reduce.
 template <bool GREEDY, bool PEN, bool SCALE>
-__device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float &gv, int &gi) {
+__device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float &chk, float &gv,
+                                          int &gi) {
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots, s0 = v->s_int0, s1 = v->s_int1;
     const int V = c.V;
     const float penalty = v->penalty, inv_temp = v->inv_temp;
     float4 *r4 = reinterpret_cast<float4 *>(c.row);
-    const float QNAN = __int_as_float(0x7fc00000);
     mx = -1e30f;
     xmin = PINF;
+    chk = 0.0f;  // stays 0 while every logit is finite (l * 0 is NaN for NaN / inf)
     gv = -1e9f;
     gi = INT_MAX;
-    auto consume = [&](int s, float4 x) {
+    // `valid`: lanes that hold elements (junk lanes of the ragged head / tail
+    // slots hold JUNK and take no part in the reductions)
+    auto consume = [&](int s, float4 x, unsigned valid) {
         float t[4] = {x.x, x.y, x.z, x.w};
         if (PEN) {
             const unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
@@ -582,27 +600,32 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
+            if (!((valid >> q) & 1u)) continue;
             if (GREEDY) {
                 if (t[q] > gv) { gv = t[q]; gi = 4 * s + q - sh; }
             } else {
                 const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
                 mx = fmaxf(mx, l);
                 xmin = fminf(xmin, l);
+                chk = __fmaf_rn(l, 0.0f, chk);
             }
         }
     };
     auto plain = [&](int s) {
         float t[4];
+        unsigned valid = 0;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int e = 4 * s + q - sh;
-            t[q] = (e >= 0 && e < V) ? __ldg(c.g + e) : QNAN;
+            const bool in = e >= 0 && e < V;
+            t[q] = in ? __ldg(c.g + e) : JUNK;
+            valid |= (unsigned)in << q;
         }
         const float4 x = make_float4(t[0], t[1], t[2], t[3]);
         r4[s] = x;
-        consume(s, x);
+        consume(s, x, valid);
     };
-    // plain head slot(s): junk lanes NaN (all slots when the row is tiny)
+    // plain head slot(s) (all slots when the row is tiny)
     for (int s = threadIdx.x; s < s0; s += NT) plain(s);
     // interior, chunk by chunk
     const int nint = s1 - s0;
@@ -616,7 +639,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
                 v->fail = 1;
                 return;
             }
-            for (; s < b; s += NT) consume(s, r4[s]);
+            for (; s < b; s += NT) consume(s, r4[s], 0xfu);
         }
     }
     for (int s = max(s1, s0) + (int)threadIdx.x; s < nslots; s += NT) plain(s);
@@ -1356,17 +1379,7 @@ __device__ __noinline__ void replay_top256(Ctx c, bool scale, int n) {
 // A candidate's bucket is key = round(d * inv_w), d = max - l, computed as
 // kf = fma(d, inv_w, MAGIC) on the FMA pipe (kf - MAGIC = key, exactly).
 // Non-candidates get d = 1e30: exp(-d) is then 0 and every bucket test fails.
-// Bucket tests use saturating multiplies (FMA pipe), not compares/selects.
-__device__ __forceinline__ float mul_sat(float a, float b) {
-    float r;
-    asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-    return r;
-}
-// 1 when key < b (kf < MAGIC + b), else 0; tb = MAGIC + b
-__device__ __forceinline__ float2 step_lt2(float2 kf, float tb) {
-    const float2 df = __fadd2_rn(make_float2(tb, tb), make_float2(-kf.x, -kf.y));
-    return make_float2(mul_sat(df.x, 0x1p100f), mul_sat(df.y, 0x1p100f));
-}
+// Bucket tests use saturating FMAs (FMA pipe), not compares/selects.
 constexpr float DNC = 1e30f;  // d of non-candidates
 
 // d = max - l for a pair of scaled logits; DNC for non-candidates (l < thr)
@@ -1385,8 +1398,10 @@ __device__ __forceinline__ float2 kf_pair(float2 d, float2 iw2, float2 mg2, floa
 }
 
 // Pass 1 of the sorted path: bucket counts (one shared atomic per candidate;
-// the clamped last bucket is counted in a register).
-template <bool SCALE, bool CLAMP>
+// the clamped last bucket is counted in a register).  CLEAN rows (every logit
+// finite and a candidate) skip the candidate test: junk lanes have keys
+// beyond the last bucket.
+template <bool SCALE, bool CLAMP, bool CLEAN>
 __device__ __forceinline__ void hist_pass(Ctx &c, float inv_w, float dmax) {
     Vars *v = c.v;
     const int nslots = v->nslots;
@@ -1396,19 +1411,26 @@ __device__ __forceinline__ void hist_pass(Ctx &c, float inv_w, float dmax) {
     uint32_t *hsh = hc - MAGIC_I;
     const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
     const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
+    const float2 mx2 = make_float2(mx, mx);
     const int KT = MAGIC_I + NB - 1;
     int tail = 0;
     for (int s = threadIdx.x; s < nslots; s += NT) {
         const float4 x = r4[s];
         float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
         if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
-        const float2 ka = kf_pair<CLAMP>(d_pair(a, mx, thr), iw2, mg2, dmax);
-        const float2 kb = kf_pair<CLAMP>(d_pair(b, mx, thr), iw2, mg2, dmax);
+        float2 ka, kb;
+        if (CLEAN) {
+            ka = __ffma2_rn(__fadd2_rn(mx2, make_float2(-a.x, -a.y)), iw2, mg2);
+            kb = __ffma2_rn(__fadd2_rn(mx2, make_float2(-b.x, -b.y)), iw2, mg2);
+        } else {
+            ka = kf_pair<CLAMP>(d_pair(a, mx, thr), iw2, mg2, dmax);
+            kb = kf_pair<CLAMP>(d_pair(b, mx, thr), iw2, mg2, dmax);
+        }
         const int kk[4] = {__float_as_int(ka.x), __float_as_int(ka.y), __float_as_int(kb.x),
                            __float_as_int(kb.y)};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            if (kk[q] > KT) continue;  // non-candidate (d = 1e30)
+            if (kk[q] > KT) continue;  // non-candidate or junk lane
             if (CLAMP && kk[q] == KT) ++tail;
             else atomicAdd(&hsh[kk[q]], 1u);
         }
@@ -1416,10 +1438,20 @@ __device__ __forceinline__ void hist_pass(Ctx &c, float inv_w, float dmax) {
     if (CLAMP && tail) atomicAdd(&hc[NB - 1], (unsigned)tail);
 }
 
+// 1 when kf < t, else 0, as sat(kf * -2^100 + t * 2^100) (FMA pipe; kf and t
+// are integers + MAGIC, so the product difference is exact); ts = t * 2^100.
+__device__ __forceinline__ float step_lt(float kf, float ts) {
+    float r;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(kf), "f"(-0x1p100f), "f"(ts));
+    return r;
+}
+
 // Pass 2 of the sorted path: exp and its fp64 sum, per window the e-mass of
-// the candidates above it (key < b_t), and the elements of the union of the
-// windows appended to the list as (id, l).
-template <bool SCALE, bool CLAMP, int NTG>
+// the candidates above it (key < lo_t), and the elements of the union of the
+// windows appended to the list as (id, l).  Two 16-byte slots per thread and
+// trip; fp32 partial sums (16 values per lane and component) go to fp64 every
+// 4 trips.
+template <bool SCALE, bool CLAMP, bool CLEAN, int NTG>
 __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, const float *tl,
                                               const float *th, double *mass, double &S) {
     Vars *v = c.v;
@@ -1430,81 +1462,125 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
     unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr);
     const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
     const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float2 mx2 = make_float2(mx, mx);
+    const int lane = threadIdx.x & 31;
+    float tls[NTG > 0 ? NTG : 1], ths[NTG > 0 ? NTG : 1];
+#pragma unroll
+    for (int t = 0; t < NTG; ++t) { tls[t] = tl[t] * 0x1p100f; ths[t] = th[t] * 0x1p100f; }
     double acc = 0.0;
     double dm[NTG];
-    float fm[NTG];
+    float2 fm[NTG];
 #pragma unroll
-    for (int t = 0; t < NTG; ++t) { dm[t] = 0.0; fm[t] = 0.f; }
-    float fs = 0.f;
-    int iter = 0;
-    for (int base = warp * 32; base < nslots; base += NT, ++iter) {
-        const int s = base + lane;
-        const float QN = __int_as_float(0x7fc00000);
-        const float4 x = (s < nslots) ? r4[s] : make_float4(QN, QN, QN, QN);
-        float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
-        if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
-        const float2 da = d_pair(a, mx, thr), db = d_pair(b, mx, thr);
-        // e = exp(l - max) = exp(-d); fl(l - max) = -fl(max - l) exactly
-        const float2 ea = exp_pair(make_float2(-da.x, -da.y));
-        const float2 eb = exp_pair(make_float2(-db.x, -db.y));
-        const float2 ka = kf_pair<CLAMP>(da, iw2, mg2, dmax), kb = kf_pair<CLAMP>(db, iw2, mg2, dmax);
-        const float2 g = __fadd2_rn(ea, eb);
-        fs = __fadd_rn(fs, __fadd_rn(g.x, g.y));
-        // per target: mass above its bucket (key < b), and membership
-        // (key == b) accumulated over the targets
-        float2 ia = make_float2(0.f, 0.f), ib = make_float2(0.f, 0.f);
+    for (int t = 0; t < NTG; ++t) { dm[t] = 0.0; fm[t] = make_float2(0.f, 0.f); }
+    float2 fs = make_float2(0.f, 0.f);
+    // d = max - l of a pair (DNC for non-candidates unless CLEAN)
+    auto dpair = [&](float2 l) -> float2 {
+        if (SCALE) l = __fmul2_rn(l, it2);
+        if (CLEAN) return __fadd2_rn(mx2, make_float2(-l.x, -l.y));
+        return d_pair(l, mx, thr);
+    };
+    auto kpair = [&](float2 d) -> float2 {
+        if (CLEAN) return __ffma2_rn(d, iw2, mg2);
+        return kf_pair<CLAMP>(d, iw2, mg2, dmax);
+    };
+    // e = exp(-d): the exp_pair arithmetic on x = -d with the sign folded in
+    auto epair = [&](float2 d) -> float2 {
+        const float2 nL1 = make_float2(-1.4426950216293335f, -1.4426950216293335f);
+        const float2 nL2 = make_float2(-1.925963033500011e-08f, -1.925963033500011e-08f);
+        const float2 LN2 = make_float2(0.6931471824645996f, 0.6931471824645996f);
+        const float2 y = __fmul2_rn(d, nL1);
+        float2 cc = __ffma2_rn(d, nL1, make_float2(-y.x, -y.y));
+        cc = __ffma2_rn(d, nL2, cc);
+        const float2 e = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+        return __ffma2_rn(__fmul2_rn(e, cc), LN2, e);
+    };
+    // one slot: sums, masses above each window, membership count of the slot
+    auto slot = [&](float4 x, float (&inb)[4]) {
+        const float2 da = dpair(make_float2(x.x, x.y)), db = dpair(make_float2(x.z, x.w));
+        const float2 ea = epair(da), eb = epair(db);
+        const float2 ka = kpair(da), kb = kpair(db);
+        fs = __fadd2_rn(fs, ea);
+        fs = __fadd2_rn(fs, eb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) inb[q] = 0.f;
 #pragma unroll
         for (int t = 0; t < NTG; ++t) {
-            const float2 ua = step_lt2(ka, tl[t]), ub = step_lt2(kb, tl[t]);
-            const float2 m2 = __ffma2_rn(ea, ua, __fmul2_rn(eb, ub));
-            fm[t] = __fadd_rn(fm[t], __fadd_rn(m2.x, m2.y));
-            const float2 va = step_lt2(ka, th[t]), vb = step_lt2(kb, th[t]);
-            ia = __fadd2_rn(ia, __fadd2_rn(va, make_float2(-ua.x, -ua.y)));
-            ib = __fadd2_rn(ib, __fadd2_rn(vb, make_float2(-ub.x, -ub.y)));
+            const float2 ua = make_float2(step_lt(ka.x, tls[t]), step_lt(ka.y, tls[t]));
+            const float2 ub = make_float2(step_lt(kb.x, tls[t]), step_lt(kb.y, tls[t]));
+            fm[t] = __ffma2_rn(ea, ua, fm[t]);
+            fm[t] = __ffma2_rn(eb, ub, fm[t]);
+            inb[0] += step_lt(ka.x, ths[t]) - ua.x;
+            inb[1] += step_lt(ka.y, ths[t]) - ua.y;
+            inb[2] += step_lt(kb.x, ths[t]) - ub.x;
+            inb[3] += step_lt(kb.y, ths[t]) - ub.y;
         }
-        const float inb[4] = {ia.x, ia.y, ib.x, ib.y};
-        const bool any = (inb[0] + inb[1]) + (inb[2] + inb[3]) > 0.5f;
-        if (__ballot_sync(FULL, any)) {
-            const float lv[4] = {a.x, a.y, b.x, b.y};
+    };
+    // the trip's window elements: one shared atomic per warp reserves room
+    const unsigned lt = (1u << lane) - 1;
+    auto append = [&](int s0, float4 x0, const float (&in0)[4], int s1, float4 x1,
+                       const float (&in1)[4]) {
+        unsigned m[8];
+        int tot = 0;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const bool in = inb[q] > 0.5f;
-                const unsigned mq = __ballot_sync(FULL, in);
-                if (!mq) continue;
-                const int leader = __ffs(mq) - 1;
-                int bpos = 0;
-                if (lane == leader) bpos = atomicAdd(&v->ln0, __popc(mq));
-                bpos = __shfl_sync(FULL, bpos, leader);
-                if (in) {
-                    const int pos = bpos + __popc(mq & ((1u << lane) - 1));
-                    if (pos < LISTCAP)
-                        list[pos] = ((unsigned long long)(unsigned)(4 * s + q - sh) << 32) |
-                                    __float_as_uint(lv[q]);
-                }
+        for (int q = 0; q < 4; ++q) {
+            m[q] = __ballot_sync(FULL, in0[q] > 0.5f);
+            m[4 + q] = __ballot_sync(FULL, in1[q] > 0.5f);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) tot += __popc(m[k]);
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&v->ln0, tot);
+        base = __shfl_sync(FULL, base, 0);
+        const float lv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if ((m[k] >> lane) & 1u) {
+                const int pos = base + __popc(m[k] & lt);
+                const int e = 4 * (k < 4 ? s0 : s1) + (k & 3) - sh;
+                const float l = SCALE ? __fmul_rn(lv[k], it2.x) : lv[k];
+                if (pos < LISTCAP)
+                    list[pos] = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
+            }
+            base += __popc(m[k]);
+        }
+    };
+    const float4 OUT = make_float4(JUNK, JUNK, JUNK, JUNK);
+    int iter = 0;
+    // warp-uniform trip count: every lane of a warp takes the same trips
+    const int wbase = (threadIdx.x & ~31);
+    for (int base = wbase; base < nslots; base += 2 * NT, ++iter) {
+        const int s0 = base + lane, s1 = base + NT + lane;
+        const float4 x0 = (s0 < nslots) ? r4[s0] : OUT;
+        const float4 x1 = (s1 < nslots) ? r4[s1] : OUT;
+        float in0[4], in1[4];
+        slot(x0, in0);
+        slot(x1, in1);
+        const bool any = ((in0[0] + in0[1]) + (in0[2] + in0[3])) +
+                         ((in1[0] + in1[1]) + (in1[2] + in1[3])) > 0.5f;
+        if (__ballot_sync(FULL, any)) append(s0, x0, in0, s1, x1, in1);
+        if ((iter & 3) == 3) {
+            acc += (double)(fs.x + fs.y);
+            fs = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int t = 0; t < NTG; ++t) {
+                dm[t] += (double)(fm[t].x + fm[t].y);
+                fm[t] = make_float2(0.f, 0.f);
             }
         }
-        if ((iter & 7) == 7) {
-            acc += (double)fs;
-            fs = 0.f;
-#pragma unroll
-            for (int t = 0; t < NTG; ++t) { dm[t] += (double)fm[t]; fm[t] = 0.f; }
-        }
     }
-    acc += (double)fs;
+    acc += (double)(fs.x + fs.y);
 #pragma unroll
-    for (int t = 0; t < NTG; ++t) dm[t] += (double)fm[t];
+    for (int t = 0; t < NTG; ++t) dm[t] += (double)(fm[t].x + fm[t].y);
     double m0 = NTG > 0 ? dm[0] : 0.0, m1 = NTG > 1 ? dm[1] : 0.0;
     int z0 = 0, z1 = 0;
     block_sum4(acc, m0, z0, z1, c.red);
     S = acc;
     if (NTG > 0) mass[0] = m0;
     if (NTG > 1) {
-        double m2 = NTG > 2 ? dm[2] : 0.0, dz = 0.0;
+        double m2 = NTG > 2 ? dm[2] : 0.0;
         block_sum4(m1, m2, z0, z1, c.red);
         mass[1] = m1;
         if (NTG > 2) mass[2] = m2;
-        (void)dz;
     }
 }
 
@@ -1579,49 +1655,108 @@ __device__ __forceinline__ void block_xscan3(double (&m)[3], int (&n)[3], double
     __syncthreads();
 }
 
-// One target over the sorted window list: the first entry of window
-// [lo, hi] (in list order) where the running mass from m0 crosses T (GE /
-// GT), or whose position from cnt0 equals m (POS).  Thread-contiguous runs
-// [j0, j1) with the window's exclusive prefix (pre_m, pre_n) in front.
-// True when found and clear of the window's outer edges (a logit a few ulps
-// across an outer edge can share the probability and belong on either side).
-__device__ __forceinline__ bool resolve_fast(Ctx &c, const unsigned long long *list, int nl,
-                                             int j0, int j1, int lo, int hi, double m0, int cnt0,
-                                             double pre_m, int pre_n, int mode, double T, int m,
-                                             Sel &out) {
-    Vars *v = c.v;
-    if (mode == T_POS ? (m < cnt0)
-                      : (((mode == T_MASS_GE) ? (m0 >= T) : (m0 > T)) && cnt0 > 0))
-        return false;  // the crossing lies above the window
+// A target's crossing over the sorted window list, published by its owner.
+struct Hit {
+    double cs;
+    float p;
+    int id, pos, flags;  // flags: 1 found, 2 near an outer window edge, 4 tie
+    int jmin;            // list index of the crossing (lowest claimant)
+};
+struct Cand {
+    int j, pos;
+    double cs;
+};
+
+// The first entry of this thread's run [j0, j1) of the sorted list that lies
+// in window [lo, hi] and where the running mass from m0 crosses T (GE / GT)
+// or whose position from cnt0 equals m (POS); (pre_m, pre_n) is the window's
+// exclusive prefix in front of the run.  j = INT_MAX when none.  Runs of two
+// threads can both claim a crossing within fp64 rounding of T: the lowest
+// list index wins (run_publish).
+__device__ __forceinline__ Cand run_find(const unsigned long long *list, int j0, int j1, int lo,
+                                         int hi, double m0, int cnt0, double pre_m, int pre_n,
+                                         int mode, double T, int m) {
+    Cand r;
+    r.j = INT_MAX;
+    r.pos = 0;
+    r.cs = 0.0;
     double cs = m0 + pre_m;
     int pos = cnt0 + pre_n;
-    int hit = INT_MAX, hpos = 0;
-    double hcs = 0.0;
     for (int j = j0; j < j1; ++j) {
         const unsigned long long k = list[j];
         const int b = lk_bkt(k);
         if (b < lo || b > hi) continue;
+        const double prev = cs;
         cs += (double)key_p(k);
-        const bool ok = (mode == T_MASS_GE) ? (cs >= T) : (mode == T_MASS_GT) ? (cs > T)
-                                                                              : (pos == m);
-        if (ok) { hit = j; hcs = cs; hpos = pos; break; }
+        const bool hit = (mode == T_MASS_GE) ? ((pos == 0 || prev < T) && cs >= T)
+                         : (mode == T_MASS_GT) ? ((pos == 0 || prev <= T) && cs > T)
+                                               : (pos == m);
+        if (hit) { r.j = j; r.pos = pos; r.cs = cs; return r; }
         ++pos;
     }
-    const int best = block_min_i(hit, c.red);
-    if (best == INT_MAX) return false;  // below the window
-    if (hit == best) { v->cs = hcs; v->own = hpos; }
-    __syncthreads();
-    const unsigned long long k = list[best];
+    return r;
+}
+
+__device__ __forceinline__ void run_publish(const unsigned long long *list, int nl, const Cand &h,
+                                            int lo, int hi, Hit *out) {
+    const unsigned long long k = list[h.j];
+    const int j = h.j, b = lk_bkt(k), e = lk_edge(k);
+    const float p = key_p(k);
+    const bool tie = (j > 0 && key_p(list[j - 1]) == p) || (j + 1 < nl && key_p(list[j + 1]) == p);
+    // an element within rounding of the window's outer edges can share its
+    // probability with one across the edge
+    const bool outer = (b == lo && e < 0) || (b == hi && e > 0);
+    out->cs = h.cs;
+    out->p = p;
+    out->id = lk_id(k);
+    out->pos = h.pos;
+    out->flags = 1 | (outer ? 2 : 0) | (tie ? 4 : 0);
+}
+
+// A published crossing as a selection; false when missing or at an outer edge.
+__device__ __forceinline__ bool hit_sel(const Hit &h, Sel &out) {
+    const int f = h.flags;
+    if (!(f & 1)) return false;
     out.found = 1;
-    out.pos = v->own;
-    out.cs = v->cs;
-    out.id = lk_id(k);
-    out.p = key_p(k);
-    out.tie = (best > 0 && key_p(list[best - 1]) == out.p) ||
-              (best + 1 < nl && key_p(list[best + 1]) == out.p);
+    out.cs = h.cs;
+    out.p = h.p;
+    out.id = h.id;
+    out.pos = h.pos;
+    out.tie = (f & 4) ? 1 : 0;
+    return !(f & 2);
+}
+
+// Ascending bitonic sort of n <= NT keys in shared memory `a`, one key per
+// thread in registers: exchanges within a warp by shuffles, across warps
+// through two alternating shared buffers (a and a + NT; one barrier each).
+__device__ __forceinline__ void sort_reg(unsigned long long *a, int n) {
+    const int t = threadIdx.x;
+    unsigned long long k = (t < n) ? a[t] : ~0ull;
+    int P = 2;
+    while (P < n) P <<= 1;
+    int buf = 0;
+    __syncthreads();  // every thread has read its key before a is reused
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            unsigned long long o;
+            if (j >= 32) {
+                unsigned long long *x = a + buf * NT;
+                x[t] = k;
+                __syncthreads();
+                o = x[t ^ j];
+                buf ^= 1;
+            } else {
+                const unsigned lo32 = __shfl_xor_sync(FULL, (unsigned)k, j);
+                const unsigned hi32 = __shfl_xor_sync(FULL, (unsigned)(k >> 32), j);
+                o = ((unsigned long long)hi32 << 32) | lo32;
+            }
+            const bool up = (t & size) == 0, lower = (t & j) == 0;
+            k = (lower == up) ? (o < k ? o : k) : (o > k ? o : k);
+        }
+    }
+    __syncthreads();  // the last exchange's reads are done
+    if (t < n) a[t] = k;
     __syncthreads();
-    const int b = lk_bkt(k), e = lk_edge(k);
-    return !((b == lo && e < 0) || (b == hi && e > 0));
 }
 
 // Probability window [plo, phi] covering buckets [b0, b1] of width w (for
@@ -1667,8 +1802,12 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     for (int i = threadIdx.x; i < NB; i += NT) hc[i] = 0;
     if (threadIdx.x == 0) v->ln0 = 0;
     __syncthreads();
-    if (clamp) hist_pass<SCALE, true>(c, inv_w, dmax);
-    else hist_pass<SCALE, false>(c, inv_w, dmax);
+    // CLEAN variants only without clamping (junk lanes must stay beyond the
+    // last bucket)
+    const bool clean = v->clean && !clamp;
+    if (clamp) hist_pass<SCALE, true, false>(c, inv_w, dmax);
+    else if (clean) hist_pass<SCALE, false, true>(c, inv_w, dmax);
+    else hist_pass<SCALE, false, false>(c, inv_w, dmax);
     __syncthreads();
     // bucket scan: counts exactly, masses estimated from bucket centres
     const int bb = BPT * threadIdx.x;
@@ -1833,23 +1972,31 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     double mass[3] = {0.0, 0.0, 0.0};
     double S = 0.0;
     if (clamp) {
-        if (ntg <= 1) combined_pass<SCALE, true, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, true, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, true, 3>(c, inv_w, dmax, tl, th, mass, S);
+        if (ntg <= 1) combined_pass<SCALE, true, false, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, true, false, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, true, false, 3>(c, inv_w, dmax, tl, th, mass, S);
+    } else if (clean) {
+        if (ntg <= 1) combined_pass<SCALE, false, true, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, false, true, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, false, true, 3>(c, inv_w, dmax, tl, th, mass, S);
     } else {
-        if (ntg <= 1) combined_pass<SCALE, false, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, false, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, false, 3>(c, inv_w, dmax, tl, th, mass, S);
+        if (ntg <= 1) combined_pass<SCALE, false, false, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S);
     }
     const double mass_c = slot[0] >= 0 ? mass[slot[0]] : 0.0;
     const double mass_k = slot[1] >= 0 ? mass[slot[1]] : 0.0;
     const double mass_d = slot[2] >= 0 ? mass[slot[2]] : 0.0;
     const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
     if (threadIdx.x == 0) { v->inv_sum = inv_sum; v->S = S; }
+    // release: the row buffer is no longer read on the common path (the list
+    // holds the window elements; the rare fallbacks read global memory)
+    release_row(c);
     __syncthreads();
     const int nl = min(v->ln0, LISTCAP);
     const bool list_ok = v->ln0 <= LISTCAP;
     // exact probabilities and buckets of the listed elements, canonical sort
+    Hit *hits = reinterpret_cast<Hit *>(c.scr + LISTCAP * 8 + 1024);
     if (list_ok) {
         for (int i = threadIdx.x; i < nl; i += NT) {
             const unsigned long long e0 = list[i];
@@ -1867,12 +2014,10 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             list[i] = list_key(pe, id, bk_, eg);
         }
         __syncthreads();
-        sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
+        if (nl <= NT) sort_reg(list, nl);
+        else sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
     }
-    // release: the row buffer is no longer read on the common path (the rare
-    // fallbacks read global memory)
-    release_row(c);
-    __syncthreads();
+    if (threadIdx.x < 3) { hits[threadIdx.x].flags = 0; hits[threadIdx.x].jmin = INT_MAX; }
 
     const double ip = (double)inv_sum;
     // per-thread runs of the sorted list and each window's prefix in front
@@ -1893,6 +2038,22 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     block_xscan3(pm, pn, reinterpret_cast<double *>(c.scr + LISTCAP * 8),
                  reinterpret_cast<int *>(c.scr + LISTCAP * 8 + 3 * NW * 8));
 
+    // nucleus cut and top_k position: the owners of the crossings publish them
+    const double m0c = mass_c * ip, m0k = mass_k * ip, m0d = mass_d * ip;
+    const bool try_c = want_cut && list_ok && bc < NB && !(m0c >= (double)top_p && v->cc > 0);
+    const bool try_k = want_k && list_ok && bk < NB && !(top_k - 1 < v->ck);
+    Cand hc_ = {INT_MAX, 0, 0.0}, hk_ = {INT_MAX, 0, 0.0};
+    if (try_c)
+        hc_ = run_find(list, j0, j1, bc, bc1, m0c, v->cc, pm[0], pn[0], T_MASS_GE, (double)top_p, 0);
+    if (try_k)
+        hk_ = run_find(list, j0, j1, bk, bk, m0k, v->ck, pm[1], pn[1], T_POS, 0.0, top_k - 1);
+    if (hc_.j != INT_MAX) atomicMin(&hits[0].jmin, hc_.j);
+    if (hk_.j != INT_MAX) atomicMin(&hits[1].jmin, hk_.j);
+    __syncthreads();
+    if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) run_publish(list, nl, hc_, bc, bc1, &hits[0]);
+    if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) run_publish(list, nl, hk_, bk, bk, &hits[1]);
+    __syncthreads();
+
     int n = ncand;
     double new_sum = S * ip;  // total probability mass (fallback when no cut)
     Sel tail;
@@ -1901,10 +2062,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     float pw_lo = 0.0f, pw_hi = PINF;
     if (want_cut) {
         Sel cut;
-        const bool ok = list_ok && bc < NB &&
-                        resolve_fast(c, list, nl, j0, j1, bc, bc1, mass_c * ip, v->cc, pm[0],
-                                     pn[0], T_MASS_GE, (double)top_p, 0, cut);
-        if (!ok) {
+        if (!(try_c && hit_sel(hits[0], cut))) {
             if (bc < NB) pwin_of(bc - 4, bc1 + 4, w, inv_sum, pw_lo, pw_hi);
             cut = select_slow(c, SCALE, T_MASS_GE, (double)top_p, 0, pw_lo, pw_hi);
         }
@@ -1917,10 +2075,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
     if (want_k && top_k < n) {  // src/model.c:102-103
         Sel tk;
-        const bool ok = list_ok && bk < NB &&
-                        resolve_fast(c, list, nl, j0, j1, bk, bk, mass_k * ip, v->ck, pm[1],
-                                     pn[1], T_POS, 0.0, top_k - 1, tk);
-        if (!ok) {
+        if (!(try_k && hit_sel(hits[1], tk))) {
             pw_lo = 0.0f; pw_hi = PINF;
             if (bk < NB) pwin_of(bk - 4, bk + 4, w, inv_sum, pw_lo, pw_hi);
             tk = select_slow(c, SCALE, T_POS, 0.0, top_k - 1, pw_lo, pw_hi);
@@ -1932,10 +2087,15 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     const float r = __fmul_rn(v->u, __double2float_rn(new_sum));
     Sel d;
     {
-        const bool ok = list_ok && bd < NB &&
-                        resolve_fast(c, list, nl, j0, j1, bd, bd1, mass_d * ip, v->cd, pm[2],
-                                     pn[2], T_MASS_GT, (double)r, 0, d);
-        if (!ok) {
+        const bool try_d = list_ok && bd < NB && !(m0d > (double)r && v->cd > 0);
+        Cand hd_ = {INT_MAX, 0, 0.0};
+        if (try_d)
+            hd_ = run_find(list, j0, j1, bd, bd1, m0d, v->cd, pm[2], pn[2], T_MASS_GT, (double)r, 0);
+        if (hd_.j != INT_MAX) atomicMin(&hits[2].jmin, hd_.j);
+        __syncthreads();
+        if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) run_publish(list, nl, hd_, bd, bd1, &hits[2]);
+        __syncthreads();
+        if (!(try_d && hit_sel(hits[2], d))) {
             pw_lo = 0.0f; pw_hi = PINF;
             if (bd < NB) pwin_of(bd - 4, bd1 + 4, w, inv_sum, pw_lo, pw_hi);
             d = select_slow(c, SCALE, T_MASS_GT, (double)r, 0, pw_lo, pw_hi);
@@ -1990,6 +2150,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         c.parity = it & 1u;
         c.g = P.logits + (int64_t)row * P.ld;
         if (tid == 0) {
+            // dynamic schedule: the first gridDim.x rows go one per CTA, every
+            // later row to the CTA that asks first (rows of unequal cost would
+            // otherwise leave SMs idle at the end of the launch); claimed now
+            // (the result is first read when this row's buffer is released),
+            // its copy is issued at the release
+            c.claim = (int)gridDim.x + atomicAdd(&P.sched[0], 1);
             const int sh = (int)(((uintptr_t)c.g & 15u) >> 2);
             int i0 = sh ? 4 - sh : 0;
             if (i0 > V) i0 = V;
@@ -2034,24 +2200,28 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         }
         const bool greedy = v->greedy != 0, pen = v->pen != 0;
         const bool scale = v->inv_temp != 1.0f;
-        float mx, xmin, gv;
+        float mx, xmin, chk, gv;
         int gi;
         if (greedy) {
-            if (pen) load_pass<true, true, false>(c, mx, xmin, gv, gi);
-            else load_pass<true, false, false>(c, mx, xmin, gv, gi);
+            if (pen) load_pass<true, true, false>(c, mx, xmin, chk, gv, gi);
+            else load_pass<true, false, false>(c, mx, xmin, chk, gv, gi);
         } else if (pen) {
-            if (scale) load_pass<false, true, true>(c, mx, xmin, gv, gi);
-            else load_pass<false, true, false>(c, mx, xmin, gv, gi);
+            if (scale) load_pass<false, true, true>(c, mx, xmin, chk, gv, gi);
+            else load_pass<false, true, false>(c, mx, xmin, chk, gv, gi);
         } else {
-            if (scale) load_pass<false, false, true>(c, mx, xmin, gv, gi);
-            else load_pass<false, false, false>(c, mx, xmin, gv, gi);
+            if (scale) load_pass<false, false, true>(c, mx, xmin, chk, gv, gi);
+            else load_pass<false, false, false>(c, mx, xmin, chk, gv, gi);
         }
         if (__syncthreads_or(v->fail)) {
             // a bounded wait expired: wait (bounded) for this row's copies,
             // then stop; the host sees the error flag
             if (tid == 0) {
                 for (int ch = 0; ch < NCHUNK; ++ch) (void)mbar_wait(&c.mbar[ch], c.parity);
-                if (P.mark_failed_rows) P.out_id[row] = -1;
+                if (P.mark_failed_rows) {
+                    // this row and the one claimed for after it stay unsampled
+                    P.out_id[row] = -1;
+                    if (c.claim < P.B) P.out_id[c.claim] = -1;
+                }
             }
             __syncthreads();
             break;
@@ -2061,7 +2231,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             release_row(c);
             write_result(c, gi == INT_MAX ? 0 : gi, 1.0f, 1, 0, 0, 0);
         } else {
-            block_maxmin_f(mx, xmin, c.red);
+            block_maxmin_chk(mx, xmin, chk, c.red);
             if (tid == 0) {
                 v->mx = mx;
                 v->xmin = xmin;
@@ -2070,6 +2240,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
                 if (v->min_p >= 1.0f) thr = mx;
                 else if (v->min_p > 0.0f) thr = __fadd_rn(mx, v->log_min_p);
                 v->thr = thr;
+                // every logit finite and a candidate: the streaming passes
+                // need no candidate test
+                v->clean = (chk == 0.0f) && (xmin >= thr) && (fabsf(mx) < 1e30f);
                 v->k = (v->top_k > 0 && v->top_k <= 256) ? v->top_k : 0;  // src/model.c:175
             }
             __syncthreads();
