@@ -49,6 +49,7 @@ constexpr float DCAP = 40.0f;                          // bucket range cap
 constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
 constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
 constexpr int LISTCAP = 2048;                          // window list cap (entries)
+constexpr int LREG = 2;                                // list slots of each thread
 constexpr int BPT = NB / NT;                            // estimate buckets per thread
 constexpr int SLOW_CAP = 256;                          // rare-path list cap
 constexpr int SLOW_OFF = LISTCAP * 8 + 2048;           // rare-path scratch offset
@@ -1453,7 +1454,8 @@ __device__ __forceinline__ float step_lt(float kf, float ts) {
 // 4 trips.
 template <bool SCALE, bool CLAMP, bool CLEAN, int NTG>
 __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, const float *tl,
-                                              const float *th, double *mass, double &S) {
+                                              const float *th, double *mass, double &S,
+                                              int &mycnt) {
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots;
     const float mx = v->mx, thr = v->thr;
@@ -1515,34 +1517,25 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
             inb[3] += step_lt(kb.y, ths[t]) - ub.y;
         }
     };
-    // the trip's window elements: one shared atomic per warp reserves room
-    const unsigned lt = (1u << lane) - 1;
-    auto append = [&](int s0, float4 x0, const float (&in0)[4], int s1, float4 x1,
-                       const float (&in1)[4]) {
-        unsigned m[8];
-        int tot = 0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            m[q] = __ballot_sync(FULL, in0[q] > 0.5f);
-            m[4 + q] = __ballot_sync(FULL, in1[q] > 0.5f);
+    // Window elements: every thread keeps its first LREG in its own list slots
+    // (index q * NT + tid), further ones go to the shared overflow half of the
+    // list through an atomic (v->ln0); no warp-wide step per element.
+    int cnt = 0;
+    auto put = [&](int e, float l) {
+        const unsigned long long ent = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
+        if (cnt < LREG) {
+            list[cnt * NT + threadIdx.x] = ent;
+        } else {
+            const int pos = atomicAdd(&v->ln0, 1);
+            if (pos < LISTCAP - LREG * NT) list[LREG * NT + pos] = ent;
         }
+        ++cnt;
+    };
+    auto append = [&](int s, float4 x, const float (&inb)[4]) {
+        const float lv[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) tot += __popc(m[k]);
-        int base = 0;
-        if (lane == 0) base = atomicAdd(&v->ln0, tot);
-        base = __shfl_sync(FULL, base, 0);
-        const float lv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            if ((m[k] >> lane) & 1u) {
-                const int pos = base + __popc(m[k] & lt);
-                const int e = 4 * (k < 4 ? s0 : s1) + (k & 3) - sh;
-                const float l = SCALE ? __fmul_rn(lv[k], it2.x) : lv[k];
-                if (pos < LISTCAP)
-                    list[pos] = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
-            }
-            base += __popc(m[k]);
-        }
+        for (int q = 0; q < 4; ++q)
+            if (inb[q] > 0.5f) put(4 * s + q - sh, SCALE ? __fmul_rn(lv[q], it2.x) : lv[q]);
     };
     const float4 OUT = make_float4(JUNK, JUNK, JUNK, JUNK);
     int iter = 0;
@@ -1555,9 +1548,8 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
         float in0[4], in1[4];
         slot(x0, in0);
         slot(x1, in1);
-        const bool any = ((in0[0] + in0[1]) + (in0[2] + in0[3])) +
-                         ((in1[0] + in1[1]) + (in1[2] + in1[3])) > 0.5f;
-        if (__ballot_sync(FULL, any)) append(s0, x0, in0, s1, x1, in1);
+        append(s0, x0, in0);
+        append(s1, x1, in1);
         if ((iter & 3) == 3) {
             acc += (double)(fs.x + fs.y);
             fs = make_float2(0.f, 0.f);
@@ -1568,6 +1560,7 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
             }
         }
     }
+    mycnt = cnt;
     acc += (double)(fs.x + fs.y);
 #pragma unroll
     for (int t = 0; t < NTG; ++t) dm[t] += (double)(fm[t].x + fm[t].y);
@@ -1971,18 +1964,19 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     for (int t = ntg; t < 3; ++t) { tl[t] = MAGIC; th[t] = MAGIC; }
     double mass[3] = {0.0, 0.0, 0.0};
     double S = 0.0;
+    int mycnt = 0;
     if (clamp) {
-        if (ntg <= 1) combined_pass<SCALE, true, false, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, true, false, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, true, false, 3>(c, inv_w, dmax, tl, th, mass, S);
+        if (ntg <= 1) combined_pass<SCALE, true, false, 1>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        else if (ntg == 2) combined_pass<SCALE, true, false, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        else combined_pass<SCALE, true, false, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
     } else if (clean) {
-        if (ntg <= 1) combined_pass<SCALE, false, true, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, false, true, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, false, true, 3>(c, inv_w, dmax, tl, th, mass, S);
+        if (ntg <= 1) combined_pass<SCALE, false, true, 1>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        else if (ntg == 2) combined_pass<SCALE, false, true, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        else combined_pass<SCALE, false, true, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
     } else {
-        if (ntg <= 1) combined_pass<SCALE, false, false, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S);
+        if (ntg <= 1) combined_pass<SCALE, false, false, 1>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
     }
     const double mass_c = slot[0] >= 0 ? mass[slot[0]] : 0.0;
     const double mass_k = slot[1] >= 0 ? mass[slot[1]] : 0.0;
@@ -1993,8 +1987,35 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     // holds the window elements; the rare fallbacks read global memory)
     release_row(c);
     __syncthreads();
-    const int nl = min(v->ln0, LISTCAP);
-    const bool list_ok = v->ln0 <= LISTCAP;
+    // compact the list: per-thread slots by a block scan of the counts, then
+    // the overflow entries
+    const int nov = v->ln0;
+    const bool list_ok = nov <= LISTCAP - LREG * NT;
+    {
+        int tot;
+        const int mine = min(mycnt, LREG);
+        const int ofs = block_xscan_i(mine, tot, c.red);
+        unsigned long long ev[LREG], ov[LISTCAP / NT - LREG];
+#pragma unroll
+        for (int q = 0; q < LREG; ++q) ev[q] = (q < mine) ? list[q * NT + threadIdx.x] : 0ull;
+#pragma unroll
+        for (int q = 0; q < LISTCAP / NT - LREG; ++q) {
+            const int i = threadIdx.x + q * NT;
+            ov[q] = (list_ok && i < nov) ? list[LREG * NT + i] : 0ull;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < LREG; ++q)
+            if (q < mine) list[ofs + q] = ev[q];
+#pragma unroll
+        for (int q = 0; q < LISTCAP / NT - LREG; ++q) {
+            const int i = threadIdx.x + q * NT;
+            if (list_ok && i < nov) list[tot + i] = ov[q];
+        }
+        if (threadIdx.x == 0) v->ln1 = tot + (list_ok ? nov : 0);
+        __syncthreads();
+    }
+    const int nl = list_ok ? v->ln1 : 0;
     // exact probabilities and buckets of the listed elements, canonical sort
     Hit *hits = reinterpret_cast<Hit *>(c.scr + LISTCAP * 8 + 1024);
     if (list_ok) {
