@@ -1518,24 +1518,41 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
         }
     };
     // Window elements: every thread keeps its first LREG in its own list slots
-    // (index q * NT + tid), further ones go to the shared overflow half of the
-    // list through an atomic (v->ln0); no warp-wide step per element.
+    // (index q * NT + tid) by predicated stores; further ones (rare) go to the
+    // shared overflow half of the list through an atomic (v->ln0).
     int cnt = 0;
-    auto put = [&](int e, float l) {
-        const unsigned long long ent = ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
-        if (cnt < LREG) {
-            list[cnt * NT + threadIdx.x] = ent;
-        } else {
-            const int pos = atomicAdd(&v->ln0, 1);
-            if (pos < LISTCAP - LREG * NT) list[LREG * NT + pos] = ent;
-        }
-        ++cnt;
-    };
-    auto append = [&](int s, float4 x, const float (&inb)[4]) {
-        const float lv[4] = {x.x, x.y, x.z, x.w};
+    auto append = [&](int s0, float4 x0, const float (&in0)[4], int s1, float4 x1,
+                      const float (&in1)[4]) {
+        const float lv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const float ib[8] = {in0[0], in0[1], in0[2], in0[3], in1[0], in1[1], in1[2], in1[3]};
+        const int c0 = cnt;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (inb[q] > 0.5f) put(4 * s + q - sh, SCALE ? __fmul_rn(lv[q], it2.x) : lv[q]);
+        for (int k = 0; k < 8; ++k) {
+            const bool in = ib[k] > 0.5f;
+            if (in && cnt < LREG) {
+                const int e = 4 * (k < 4 ? s0 : s1) + (k & 3) - sh;
+                const float l = SCALE ? __fmul_rn(lv[k], it2.x) : lv[k];
+                list[cnt * NT + threadIdx.x] =
+                    ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
+            }
+            cnt += in ? 1 : 0;
+        }
+        if (cnt > LREG && cnt > c0) {
+            // this trip's elements beyond the thread's slots
+            int idx = c0;
+            for (int k = 0; k < 8; ++k) {
+                if (!(ib[k] > 0.5f)) continue;
+                if (idx >= LREG) {
+                    const int e = 4 * (k < 4 ? s0 : s1) + (k & 3) - sh;
+                    const float l = SCALE ? __fmul_rn(lv[k], it2.x) : lv[k];
+                    const int pos = atomicAdd(&v->ln0, 1);
+                    if (pos < LISTCAP - LREG * NT)
+                        list[LREG * NT + pos] =
+                            ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
+                }
+                ++idx;
+            }
+        }
     };
     const float4 OUT = make_float4(JUNK, JUNK, JUNK, JUNK);
     int iter = 0;
@@ -1548,8 +1565,7 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
         float in0[4], in1[4];
         slot(x0, in0);
         slot(x1, in1);
-        append(s0, x0, in0);
-        append(s1, x1, in1);
+        append(s0, x0, in0, s1, x1, in1);
         if ((iter & 3) == 3) {
             acc += (double)(fs.x + fs.y);
             fs = make_float2(0.f, 0.f);
