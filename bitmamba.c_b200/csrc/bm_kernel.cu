@@ -505,7 +505,8 @@ struct Ctx {
 };
 
 // Issue the bulk copies of one row into the row buffer (one thread).
-__device__ __forceinline__ void issue_row(const float *g, int V, uint64_t *mbar, float *rowbuf) {
+__device__ __forceinline__ void issue_chunk(const float *g, int V, uint64_t *mbar, float *rowbuf,
+                                            int ch) {
     const int sh = (int)(((uintptr_t)g & 15u) >> 2);
     int i0 = sh ? 4 - sh : 0;
     if (i0 > V) i0 = V;
@@ -513,12 +514,13 @@ __device__ __forceinline__ void issue_row(const float *g, int V, uint64_t *mbar,
     if (n4 < 4 * NCHUNK * 4) n4 = 0;  // tiny rows: plain loads only
     const int s_int0 = (i0 + sh) >> 2;
     const int nint = n4 >> 2;
-    for (int ch = 0; ch < NCHUNK; ++ch) {
-        const int a = (ch * nint) / NCHUNK, b = ((ch + 1) * nint) / NCHUNK;
-        const uint32_t bytes = (uint32_t)(b - a) * 16u;
-        mbar_expect_tx(&mbar[ch], bytes);
-        if (bytes) bulk_load(rowbuf + 4 * (s_int0 + a), g + i0 + 4 * a, bytes, &mbar[ch]);
-    }
+    const int a = (ch * nint) / NCHUNK, b = ((ch + 1) * nint) / NCHUNK;
+    const uint32_t bytes = (uint32_t)(b - a) * 16u;
+    mbar_expect_tx(&mbar[ch], bytes);
+    if (bytes) bulk_load(rowbuf + 4 * (s_int0 + a), g + i0 + 4 * a, bytes, &mbar[ch]);
+}
+__device__ __forceinline__ void issue_row(const float *g, int V, uint64_t *mbar, float *rowbuf) {
+    for (int ch = 0; ch < NCHUNK; ++ch) issue_chunk(g, V, mbar, rowbuf, ch);
 }
 
 // L2 prefetch of a row's 16-byte-aligned interior.
@@ -535,15 +537,21 @@ __device__ __forceinline__ void prefetch_row(const float *g, int V) {
 __device__ __forceinline__ void release_row(Ctx &c) {
     fence_proxy_async();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        c.v->released = 1;
-        const int next_row = c.claim;  // claimed when this row started
-        c.v->next_row = next_row;
+    if (threadIdx.x < 32) {
+        // the row claimed when this one started (thread 0 holds it); one lane
+        // per chunk issues the copies
+        const int next_row = __shfl_sync(FULL, c.claim, 0);
+        const int lane = threadIdx.x;
+        if (lane == 0) {
+            c.v->released = 1;
+            c.v->next_row = next_row;
+        }
         if (next_row < c.B) {
-            issue_row(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row);
+            if (lane < NCHUNK)
+                issue_chunk(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row, lane);
             // warm L2 with the row claimed about one round later
             const int pre = next_row + (int)gridDim.x;
-            if (pre < c.B) prefetch_row(c.logits + (int64_t)pre * c.ld, c.V);
+            if (lane == NCHUNK && pre < c.B) prefetch_row(c.logits + (int64_t)pre * c.ld, c.V);
         }
     }
 }
@@ -1540,6 +1548,7 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
         if (cnt > LREG && cnt > c0) {
             // this trip's elements beyond the thread's slots
             int idx = c0;
+#pragma unroll
             for (int k = 0; k < 8; ++k) {
                 if (!(ib[k] > 0.5f)) continue;
                 if (idx >= LREG) {
@@ -1744,7 +1753,7 @@ __device__ __forceinline__ void sort_reg(unsigned long long *a, int n) {
     int P = 2;
     while (P < n) P <<= 1;
     int buf = 0;
-    __syncthreads();  // every thread has read its key before a is reused
+    // (each thread read its own a[t]; the first exchange writes only a[t])
     for (int size = 2; size <= P; size <<= 1) {
         for (int j = size >> 1; j > 0; j >>= 1) {
             unsigned long long o;
@@ -1965,19 +1974,22 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     __syncthreads();
     const int bc = want_cut ? v->bc : NB, bk = want_k ? v->bk : NB, bd = v->bd0;
     const int bc1 = v->bc_hi, bd1 = v->bd_hi;
-    const int blo[3] = {bc, bk, bd}, bhi[3] = {bc1, bk, bd1};
-    // distinct active windows first: slot[t] = index of target t's window
-    float tl[3], th[3];
-    int slot[3] = {-1, -1, -1}, ntg = 0;
-    for (int t = 0; t < 3; ++t) {
-        if (blo[t] >= NB) continue;
-        const float lo = MAGIC + (float)blo[t], hi = MAGIC + (float)(bhi[t] + 1);
-        int q = 0;
-        while (q < ntg && !(tl[q] == lo && th[q] == hi)) ++q;
-        if (q == ntg) { tl[q] = lo; th[q] = hi; ++ntg; }
-        slot[t] = q;
-    }
-    for (int t = ntg; t < 3; ++t) { tl[t] = MAGIC; th[t] = MAGIC; }
+    // distinct active windows first: slot_* = index of the target's window
+    // (straight-line code: the small arrays stay in registers)
+    float tl[3] = {MAGIC, MAGIC, MAGIC}, th[3] = {MAGIC, MAGIC, MAGIC};
+    int ntg = 0, slot_c = -1, slot_k = -1, slot_d = -1;
+    auto add_window = [&](int lo_b, int hi_b) -> int {
+        const float lo = MAGIC + (float)lo_b, hi = MAGIC + (float)(hi_b + 1);
+        if (ntg > 0 && tl[0] == lo && th[0] == hi) return 0;
+        if (ntg > 1 && tl[1] == lo && th[1] == hi) return 1;
+        if (ntg == 0) { tl[0] = lo; th[0] = hi; }
+        else if (ntg == 1) { tl[1] = lo; th[1] = hi; }
+        else { tl[2] = lo; th[2] = hi; }
+        return ntg++;
+    };
+    if (bc < NB) slot_c = add_window(bc, bc1);
+    if (bk < NB) slot_k = add_window(bk, bk);
+    if (bd < NB) slot_d = add_window(bd, bd1);
     double mass[3] = {0.0, 0.0, 0.0};
     double S = 0.0;
     int mycnt = 0;
@@ -1994,17 +2006,32 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
         else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
     }
-    const double mass_c = slot[0] >= 0 ? mass[slot[0]] : 0.0;
-    const double mass_k = slot[1] >= 0 ? mass[slot[1]] : 0.0;
-    const double mass_d = slot[2] >= 0 ? mass[slot[2]] : 0.0;
+    auto mass_of = [&](int sl) {
+        return sl == 0 ? mass[0] : sl == 1 ? mass[1] : sl == 2 ? mass[2] : 0.0;
+    };
+    const double mass_c = mass_of(slot_c), mass_k = mass_of(slot_k), mass_d = mass_of(slot_d);
     const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
     if (threadIdx.x == 0) { v->inv_sum = inv_sum; v->S = S; }
     // release: the row buffer is no longer read on the common path (the list
     // holds the window elements; the rare fallbacks read global memory)
     release_row(c);
-    __syncthreads();
-    // compact the list: per-thread slots by a block scan of the counts, then
-    // the overflow entries
+    // exact probability, bucket and edge flag of a listed element as its key
+    auto to_key = [&](unsigned long long e0) -> unsigned long long {
+        const int id = (int)(e0 >> 32);
+        const float l = __uint_as_float((unsigned)(e0 & 0xffffffffu));
+        const float pe = __fmul_rn(exp_one(__fsub_rn(l, mx)), inv_sum);
+        float d = __fsub_rn(mx, l);
+        if (clamp) d = fminf(d, dmax);
+        const float kf = __fmaf_rn(d, inv_w, MAGIC);
+        const int bk_ = __float_as_int(kf) - MAGIC_I;
+        // within 2e-3 of a bucket edge, a logit a few ulps away (possibly the
+        // same probability) may sit in the neighbouring bucket
+        const float fr = __fmaf_rn(d, inv_w, -(float)bk_);
+        const int eg = (fr > 0.5f - 2e-3f) ? 1 : (fr < -(0.5f - 2e-3f)) ? -1 : 0;
+        return list_key(pe, id, bk_, eg);
+    };
+    // compact the list into keys: per-thread slots by a block scan of the
+    // counts, then the overflow entries
     const int nov = v->ln0;
     const bool list_ok = nov <= LISTCAP - LREG * NT;
     {
@@ -2019,6 +2046,12 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             const int i = threadIdx.x + q * NT;
             ov[q] = (list_ok && i < nov) ? list[LREG * NT + i] : 0ull;
         }
+#pragma unroll
+        for (int q = 0; q < LREG; ++q)
+            if (q < mine) ev[q] = to_key(ev[q]);
+#pragma unroll
+        for (int q = 0; q < LISTCAP / NT - LREG; ++q)
+            if (list_ok && threadIdx.x + q * NT < nov) ov[q] = to_key(ov[q]);
         __syncthreads();
 #pragma unroll
         for (int q = 0; q < LREG; ++q)
@@ -2032,25 +2065,9 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         __syncthreads();
     }
     const int nl = list_ok ? v->ln1 : 0;
-    // exact probabilities and buckets of the listed elements, canonical sort
+    // canonical sort
     Hit *hits = reinterpret_cast<Hit *>(c.scr + LISTCAP * 8 + 1024);
     if (list_ok) {
-        for (int i = threadIdx.x; i < nl; i += NT) {
-            const unsigned long long e0 = list[i];
-            const int id = (int)(e0 >> 32);
-            const float l = __uint_as_float((unsigned)(e0 & 0xffffffffu));
-            const float pe = __fmul_rn(exp_one(__fsub_rn(l, mx)), inv_sum);
-            float d = __fsub_rn(mx, l);
-            if (clamp) d = fminf(d, dmax);
-            const float kf = __fmaf_rn(d, inv_w, MAGIC);
-            const int bk_ = __float_as_int(kf) - MAGIC_I;
-            // within 2e-3 of a bucket edge, a logit a few ulps away (possibly
-            // the same probability) may sit in the neighbouring bucket
-            const float fr = __fmaf_rn(d, inv_w, -(float)bk_);
-            const int eg = (fr > 0.5f - 2e-3f) ? 1 : (fr < -(0.5f - 2e-3f)) ? -1 : 0;
-            list[i] = list_key(pe, id, bk_, eg);
-        }
-        __syncthreads();
         if (nl <= NT) sort_reg(list, nl);
         else sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
     }
