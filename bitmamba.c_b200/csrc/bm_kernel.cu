@@ -49,13 +49,18 @@ constexpr float DCAP = 40.0f;                          // bucket range cap
 constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
 constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
 constexpr int LISTCAP = 2048;                          // window list cap (entries)
-constexpr int LREG = 2;                                // list slots of each thread
+constexpr int MASKW = 4;                               // membership words per thread
+constexpr int KREG = 2;                                // top_k path: slots per thread
+constexpr int KOVF = KCAP - KREG * NT;                 // top_k path: overflow entries
 constexpr int BPT = NB / NT;                            // estimate buckets per thread
 constexpr int SLOW_CAP = 256;                          // rare-path list cap
 constexpr int SLOW_OFF = LISTCAP * 8 + 2048;           // rare-path scratch offset
 constexpr float PINF = __builtin_huge_valf();
-// Junk lanes of the ragged head / tail slots: below every min_p threshold
-// (>= -1e30 - 104), and max - JUNK stays finite, so exp(-(max - JUNK)) is 0
+// Junk lanes of the ragged head / tail slots hold NaN (never a candidate,
+// whatever the temperature).  The branch-free CLEAN passes need a finite
+// value instead: JUNK, rewritten into those lanes for CLEAN rows, whose
+// temperature-scaled value (1e-6 <= 1/temp <= 20) lies below every min_p
+// threshold (>= -1e30 - 104) while max - value stays finite, so its exp is 0
 // and its bucket key lies beyond the last bucket.
 constexpr float JUNK = -1e37f;
 constexpr size_t RED_BYTES = 2048;
@@ -439,6 +444,39 @@ __device__ void sort_keys(unsigned long long *a, int n, int *rank, int cap) {
     __syncthreads();
 }
 
+// Ascending bitonic sort of n <= NT keys in shared memory `a`, one key per
+// thread in registers: exchanges within a warp by shuffles, across warps
+// through two alternating shared buffers (a and a + NT; one barrier each).
+__device__ __forceinline__ void sort_reg(unsigned long long *a, int n) {
+    const int t = threadIdx.x;
+    unsigned long long k = (t < n) ? a[t] : ~0ull;
+    int P = 2;
+    while (P < n) P <<= 1;
+    int buf = 0;
+    // (each thread read its own a[t]; the first exchange writes only a[t])
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            unsigned long long o;
+            if (j >= 32) {
+                unsigned long long *x = a + buf * NT;
+                x[t] = k;
+                __syncthreads();
+                o = x[t ^ j];
+                buf ^= 1;
+            } else {
+                const unsigned lo32 = __shfl_xor_sync(FULL, (unsigned)k, j);
+                const unsigned hi32 = __shfl_xor_sync(FULL, (unsigned)(k >> 32), j);
+                o = ((unsigned long long)hi32 << 32) | lo32;
+            }
+            const bool up = (t & size) == 0, lower = (t & j) == 0;
+            k = (lower == up) ? (o < k ? o : k) : (o > k ? o : k);
+        }
+    }
+    __syncthreads();  // the last exchange's reads are done
+    if (t < n) a[t] = k;
+    __syncthreads();
+}
+
 // Min-heap sift-down on parallel arrays, exactly src/model.c:50-66
 // (strict '<', left child checked first).
 __device__ void heap_down(float *hv, int *hi, int n, int i) {
@@ -595,7 +633,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
     gv = -1e9f;
     gi = INT_MAX;
     // `valid`: lanes that hold elements (junk lanes of the ragged head / tail
-    // slots hold JUNK and take no part in the reductions)
+    // slots hold NaN and take no part in the reductions)
     auto consume = [&](int s, float4 x, unsigned valid) {
         float t[4] = {x.x, x.y, x.z, x.w};
         if (PEN) {
@@ -627,7 +665,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         for (int q = 0; q < 4; ++q) {
             const int e = 4 * s + q - sh;
             const bool in = e >= 0 && e < V;
-            t[q] = in ? __ldg(c.g + e) : JUNK;
+            t[q] = in ? __ldg(c.g + e) : __int_as_float(0x7fc00000);
             valid |= (unsigned)in << q;
         }
         const float4 x = make_float4(t[0], t[1], t[2], t[3]);
@@ -684,29 +722,38 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
     uint32_t *kh = reinterpret_cast<uint32_t *>(c.scr);                            // 8 x 128
     unsigned long long *kc = reinterpret_cast<unsigned long long *>(c.scr + 4096);  // KCAP
     const float bscale = __fdiv_rn(127.0f, 20.0f);  // src/model.c:184
-    // collect the candidates above the min_p threshold while counting, when
-    // that threshold is a real one (otherwise every logit passes it)
-    const bool collect = v->min_p > 0.0f;
+    // The candidates are listed by a second pass after the cut (about k plus
+    // the cut bucket's population); listing everything above the min_p
+    // threshold during the histogram pass costs more than that pass.
+    constexpr bool collect = false;
 
     for (int i = threadIdx.x; i < 8 * HB; i += NT) kh[i] = 0;
     if (threadIdx.x == 0) v->kcnt = 0;
     __syncthreads();
     uint32_t *myh = kh + (warp & 7) * HB;
     unsigned long long lo8 = 0, hi8 = 0;  // per-thread counts of buckets 0..15
-    bool full = false;  // this warp stopped collecting: the list overflowed
+    // candidates: every thread keeps its first KREG in its own list slots
+    // (index q * NT + tid), further ones go to the shared overflow part
+    // through an atomic (v->kcnt counts them)
+    int cnt = 0;
+    auto put = [&](unsigned long long ent) {
+        if (cnt < KREG) {
+            kc[cnt * NT + threadIdx.x] = ent;
+        } else {
+            const int pos = atomicAdd(&v->kcnt, 1);
+            if (pos < KOVF) kc[KREG * NT + pos] = ent;
+        }
+        ++cnt;
+    };
     // histogram of (max - l) over l >= thr (src/model.c:185-195); the last
     // bucket never decides the cut, so it is not counted
-    for (int base = warp * 32; base < nslots; base += NT) {
-        const int s = base + lane;
-        if (collect && !full) full = *(volatile int *)&v->kcnt > KCAP;
-        float4 x = make_float4(-PINF, -PINF, -PINF, -PINF);
-        if (s < nslots) x = r4[s];
+    for (int s = threadIdx.x; s < nslots; s += NT) {
+        const float4 x = r4[s];
         const float t[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
-            const bool ok = (l >= thr);
-            if (ok) {
+            if (l >= thr) {
                 int b = x86_cvtt(__fmul_rn(__fsub_rn(mx, l), bscale));
                 b = min(max(b, 0), HB - 1);
                 // buckets 0..15 (where the cut of a top_k <= 256 nearly always
@@ -714,21 +761,8 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
                 if (b < 8) lo8 += 1ull << (8 * b);
                 else if (b < 16) hi8 += 1ull << (8 * (b - 8));
                 else if (b < HB - 1) atomicAdd(&myh[b], 1u);
-            }
-            if (collect) {
-                const unsigned m = __ballot_sync(FULL, ok && !full);
-                if (m) {
-                    const int leader = __ffs(m) - 1;
-                    int bpos = 0;
-                    if (lane == leader) bpos = atomicAdd(&v->kcnt, __popc(m));
-                    bpos = __shfl_sync(FULL, bpos, leader);
-                    if (ok) {
-                        const int pos = bpos + __popc(m & ((1u << lane) - 1));
-                        if (pos < KCAP)
-                            kc[pos] = ((unsigned long long)(unsigned)(4 * s + q - sh) << 32) |
-                                      __float_as_uint(l);
-                    }
-                }
+                if (collect)
+                    put(((unsigned long long)(unsigned)(4 * s + q - sh) << 32) | __float_as_uint(l));
             }
         }
     }
@@ -742,8 +776,8 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
         if (lane < 16) {
             const int j = lane >> 3, q = lane & 7;  // bucket = 8j + q
             const unsigned long long fw = f[2 * j + (q & 1)];
-            const unsigned cnt = (unsigned)((fw >> (16 * (q >> 1))) & 0xffffu);
-            if (cnt) atomicAdd(&kh[lane], cnt);
+            const unsigned cnt16 = (unsigned)((fw >> (16 * (q >> 1))) & 0xffffu);
+            if (cnt16) atomicAdd(&kh[lane], cnt16);
         }
     }
     __syncthreads();
@@ -773,48 +807,57 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
     const int cut = v->kcut;
     const float bthr = __fsub_rn(mx, __fdiv_rn((float)(cut + 1), bscale));  // src/model.c:210-211
     const float ethr = bthr > thr ? bthr : thr;                          // src/model.c:213-214
-    const int collected = v->kcnt;
-    __syncthreads();
-    if (collect && collected <= KCAP) {
-        // the extraction set is the collected set filtered by ethr >= thr
-        unsigned long long mine[(KCAP + NT - 1) / NT];
-        int nm = 0;
-        for (int i = threadIdx.x; i < collected; i += NT) {
-            const unsigned long long kk = kc[i];
-            if (__uint_as_float((unsigned)(kk & 0xffffffffu)) >= ethr) mine[nm++] = kk;
-        }
-        if (threadIdx.x == 0) v->kcnt = 0;
-        __syncthreads();
-        for (int i = 0; i < nm; ++i) kc[atomicAdd(&v->kcnt, 1)] = mine[i];
-        __syncthreads();
-    } else {
+    int novf = v->kcnt;
+    if (!(collect && novf <= KOVF)) {
         // extraction pass (src/model.c:217-224), unordered here
-        if (threadIdx.x == 0) v->kcnt = 0;
         __syncthreads();
-        for (int base = warp * 32; base < nslots; base += NT) {
-            const int s = base + lane;
-            float4 x = make_float4(-PINF, -PINF, -PINF, -PINF);
-            if (s < nslots) x = r4[s];
+        if (threadIdx.x == 0) v->kcnt = 0;
+        cnt = 0;
+        __syncthreads();
+        for (int s = threadIdx.x; s < nslots; s += NT) {
+            const float4 x = r4[s];
             const float t[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
-                const bool ok = (l >= ethr);
-                const unsigned m = __ballot_sync(FULL, ok);
-                if (m) {
-                    const int leader = __ffs(m) - 1;
-                    int bpos = 0;
-                    if (lane == leader) bpos = atomicAdd(&v->kcnt, __popc(m));
-                    bpos = __shfl_sync(FULL, bpos, leader);
-                    if (ok) {
-                        const int pos = bpos + __popc(m & ((1u << lane) - 1));
-                        if (pos < KCAP)
-                            kc[pos] = ((unsigned long long)(unsigned)(4 * s + q - sh) << 32) |
-                                      __float_as_uint(l);
-                    }
-                }
+                if (l >= ethr)
+                    put(((unsigned long long)(unsigned)(4 * s + q - sh) << 32) | __float_as_uint(l));
             }
         }
+        __syncthreads();
+        novf = v->kcnt;
+    }
+    // the extraction set: the listed candidates with l >= ethr, compacted
+    // (block scan of the per-thread counts; fixed-size register staging)
+    {
+        constexpr int OQ = KOVF / NT;
+        unsigned long long e[KREG + OQ];
+        bool keep[KREG + OQ];
+        const int own = min(cnt, KREG);
+        const bool fits = novf <= KOVF;
+#pragma unroll
+        for (int q = 0; q < KREG; ++q) {
+            e[q] = (q < own) ? kc[q * NT + threadIdx.x] : 0ull;
+            keep[q] = fits && q < own && __uint_as_float((unsigned)(e[q] & 0xffffffffu)) >= ethr;
+        }
+#pragma unroll
+        for (int q = 0; q < OQ; ++q) {
+            const int i = threadIdx.x + q * NT;
+            e[KREG + q] = (fits && i < novf) ? kc[KREG * NT + i] : 0ull;
+            keep[KREG + q] = fits && i < novf &&
+                             __uint_as_float((unsigned)(e[KREG + q] & 0xffffffffu)) >= ethr;
+        }
+        int mine = 0;
+#pragma unroll
+        for (int q = 0; q < KREG + OQ; ++q) mine += keep[q] ? 1 : 0;
+        int tot;
+        int j = block_xscan_i(mine, tot, c.red);
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < KREG + OQ; ++q)
+            if (keep[q]) kc[j++] = e[q];
+        // more candidates than the list holds: the global-memory path below
+        if (threadIdx.x == 0) v->kcnt = fits ? tot : KCAP + 1;
         __syncthreads();
     }
     const int n = v->kcnt;
@@ -831,8 +874,9 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
     float *pv = reinterpret_cast<float *>(c.scr + 2048);  // 256 probabilities
     int *rk = reinterpret_cast<int *>(c.scr + 3072);      // 256 ranks
     if (n <= KCAP) {
-        // by id (ids are unique); ranks up to NT in the histogram area
-        sort_keys(kc, n, reinterpret_cast<int *>(c.scr), KCAP);
+        // by id (ids are unique)
+        if (n <= NT) sort_reg(kc, n);
+        else sort_keys(kc, n, reinterpret_cast<int *>(c.scr), KCAP);
         if (warp == 0) {
             const int first = min(n, k);
             for (int q = lane; q < first; q += 32) {
@@ -1456,20 +1500,17 @@ __device__ __forceinline__ float step_lt(float kf, float ts) {
 }
 
 // Pass 2 of the sorted path: exp and its fp64 sum, per window the e-mass of
-// the candidates above it (key < lo_t), and the elements of the union of the
-// windows appended to the list as (id, l).  Two 16-byte slots per thread and
+// the candidates above it (key < lo_t), and a membership bit per element of
+// the union of the windows.  Two 16-byte slots per thread and
 // trip; fp32 partial sums (16 values per lane and component) go to fp64 every
 // 4 trips.
 template <bool SCALE, bool CLAMP, bool CLEAN, int NTG>
 __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, const float *tl,
-                                              const float *th, double *mass, double &S,
-                                              int &mycnt) {
+                                              const float *th, double *mass, double &S) {
     Vars *v = c.v;
-    const int sh = v->sh, nslots = v->nslots;
+    const int nslots = v->nslots;
     const float mx = v->mx, thr = v->thr;
     const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    // the histogram is dead once the windows are chosen: the list reuses it
-    unsigned long long *list = reinterpret_cast<unsigned long long *>(c.scr);
     const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
     const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
     const float2 mx2 = make_float2(mx, mx);
@@ -1525,45 +1566,14 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
             inb[3] += step_lt(kb.y, ths[t]) - ub.y;
         }
     };
-    // Window elements: every thread keeps its first LREG in its own list slots
-    // (index q * NT + tid) by predicated stores; further ones (rare) go to the
-    // shared overflow half of the list through an atomic (v->ln0).
-    int cnt = 0;
-    auto append = [&](int s0, float4 x0, const float (&in0)[4], int s1, float4 x1,
-                      const float (&in1)[4]) {
-        const float lv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        const float ib[8] = {in0[0], in0[1], in0[2], in0[3], in1[0], in1[1], in1[2], in1[3]};
-        const int c0 = cnt;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const bool in = ib[k] > 0.5f;
-            if (in && cnt < LREG) {
-                const int e = 4 * (k < 4 ? s0 : s1) + (k & 3) - sh;
-                const float l = SCALE ? __fmul_rn(lv[k], it2.x) : lv[k];
-                list[cnt * NT + threadIdx.x] =
-                    ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
-            }
-            cnt += in ? 1 : 0;
-        }
-        if (cnt > LREG && cnt > c0) {
-            // this trip's elements beyond the thread's slots
-            int idx = c0;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                if (!(ib[k] > 0.5f)) continue;
-                if (idx >= LREG) {
-                    const int e = 4 * (k < 4 ? s0 : s1) + (k & 3) - sh;
-                    const float l = SCALE ? __fmul_rn(lv[k], it2.x) : lv[k];
-                    const int pos = atomicAdd(&v->ln0, 1);
-                    if (pos < LISTCAP - LREG * NT)
-                        list[LREG * NT + pos] =
-                            ((unsigned long long)(unsigned)e << 32) | __float_as_uint(l);
-                }
-                ++idx;
-            }
-        }
-    };
-    const float4 OUT = make_float4(JUNK, JUNK, JUNK, JUNK);
+    // Window membership: one bit per element, 8 per trip (slot 0 lanes 0-3,
+    // slot 1 lanes 4-7), a 32-bit word every 4 trips to the thread's column
+    // of the mask area (the dead histogram); the elements are gathered after
+    // the pass.  No branch or store per element.
+    uint32_t *mw = reinterpret_cast<uint32_t *>(c.scr);
+    uint32_t bits = 0;
+    const float ov_ = CLEAN ? JUNK : __int_as_float(0x7fc00000);
+    const float4 OUT = make_float4(ov_, ov_, ov_, ov_);
     int iter = 0;
     // warp-uniform trip count: every lane of a warp takes the same trips
     const int wbase = (threadIdx.x & ~31);
@@ -1574,8 +1584,16 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
         float in0[4], in1[4];
         slot(x0, in0);
         slot(x1, in1);
-        append(s0, x0, in0, s1, x1, in1);
+        uint32_t tb = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            tb |= (in0[q] > 0.5f ? 1u : 0u) << q;
+            tb |= (in1[q] > 0.5f ? 1u : 0u) << (4 + q);
+        }
+        bits |= tb << (8 * (iter & 3));
         if ((iter & 3) == 3) {
+            mw[(iter >> 2) * NT + threadIdx.x] = bits;
+            bits = 0;
             acc += (double)(fs.x + fs.y);
             fs = make_float2(0.f, 0.f);
 #pragma unroll
@@ -1585,7 +1603,7 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
             }
         }
     }
-    mycnt = cnt;
+    if (iter & 3) mw[(iter >> 2) * NT + threadIdx.x] = bits;
     acc += (double)(fs.x + fs.y);
 #pragma unroll
     for (int t = 0; t < NTG; ++t) dm[t] += (double)(fm[t].x + fm[t].y);
@@ -1744,38 +1762,6 @@ __device__ __forceinline__ bool hit_sel(const Hit &h, Sel &out) {
     return !(f & 2);
 }
 
-// Ascending bitonic sort of n <= NT keys in shared memory `a`, one key per
-// thread in registers: exchanges within a warp by shuffles, across warps
-// through two alternating shared buffers (a and a + NT; one barrier each).
-__device__ __forceinline__ void sort_reg(unsigned long long *a, int n) {
-    const int t = threadIdx.x;
-    unsigned long long k = (t < n) ? a[t] : ~0ull;
-    int P = 2;
-    while (P < n) P <<= 1;
-    int buf = 0;
-    // (each thread read its own a[t]; the first exchange writes only a[t])
-    for (int size = 2; size <= P; size <<= 1) {
-        for (int j = size >> 1; j > 0; j >>= 1) {
-            unsigned long long o;
-            if (j >= 32) {
-                unsigned long long *x = a + buf * NT;
-                x[t] = k;
-                __syncthreads();
-                o = x[t ^ j];
-                buf ^= 1;
-            } else {
-                const unsigned lo32 = __shfl_xor_sync(FULL, (unsigned)k, j);
-                const unsigned hi32 = __shfl_xor_sync(FULL, (unsigned)(k >> 32), j);
-                o = ((unsigned long long)hi32 << 32) | lo32;
-            }
-            const bool up = (t & size) == 0, lower = (t & j) == 0;
-            k = (lower == up) ? (o < k ? o : k) : (o > k ? o : k);
-        }
-    }
-    __syncthreads();  // the last exchange's reads are done
-    if (t < n) a[t] = k;
-    __syncthreads();
-}
 
 // Probability window [plo, phi] covering buckets [b0, b1] of width w (for
 // the slow path's first exact pass).
@@ -1823,6 +1809,21 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     // CLEAN variants only without clamping (junk lanes must stay beyond the
     // last bucket)
     const bool clean = v->clean && !clamp;
+    if (clean) {
+        // junk lanes of the ragged head / tail slots: NaN -> JUNK
+        // (the bulk-copied interior slots [s_int0, s_int1) hold no junk)
+        const int s0 = v->s_int0, s1 = max(v->s_int1, s0), V = c.V;
+        const int nh = s0, nt = nslots - s1;
+        for (int i = threadIdx.x; i < nh + nt; i += NT) {
+            const int s = (i < nh) ? i : s1 + (i - nh);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int e = 4 * s + q - sh;
+                if (e < 0 || e >= V) c.row[4 * s + q] = JUNK;
+            }
+        }
+        __syncthreads();
+    }
     if (clamp) hist_pass<SCALE, true, false>(c, inv_w, dmax);
     else if (clean) hist_pass<SCALE, false, true>(c, inv_w, dmax);
     else hist_pass<SCALE, false, false>(c, inv_w, dmax);
@@ -1992,19 +1993,18 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     if (bd < NB) slot_d = add_window(bd, bd1);
     double mass[3] = {0.0, 0.0, 0.0};
     double S = 0.0;
-    int mycnt = 0;
     if (clamp) {
-        if (ntg <= 1) combined_pass<SCALE, true, false, 1>(c, inv_w, dmax, tl, th, mass, S, mycnt);
-        else if (ntg == 2) combined_pass<SCALE, true, false, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
-        else combined_pass<SCALE, true, false, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        if (ntg <= 1) combined_pass<SCALE, true, false, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, true, false, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, true, false, 3>(c, inv_w, dmax, tl, th, mass, S);
     } else if (clean) {
-        if (ntg <= 1) combined_pass<SCALE, false, true, 1>(c, inv_w, dmax, tl, th, mass, S, mycnt);
-        else if (ntg == 2) combined_pass<SCALE, false, true, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
-        else combined_pass<SCALE, false, true, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        if (ntg <= 1) combined_pass<SCALE, false, true, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, false, true, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, false, true, 3>(c, inv_w, dmax, tl, th, mass, S);
     } else {
-        if (ntg <= 1) combined_pass<SCALE, false, false, 1>(c, inv_w, dmax, tl, th, mass, S, mycnt);
-        else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S, mycnt);
-        else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S, mycnt);
+        if (ntg <= 1) combined_pass<SCALE, false, false, 1>(c, inv_w, dmax, tl, th, mass, S);
+        else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S);
+        else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S);
     }
     auto mass_of = [&](int sl) {
         return sl == 0 ? mass[0] : sl == 1 ? mass[1] : sl == 2 ? mass[2] : 0.0;
@@ -2012,13 +2012,8 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     const double mass_c = mass_of(slot_c), mass_k = mass_of(slot_k), mass_d = mass_of(slot_d);
     const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
     if (threadIdx.x == 0) { v->inv_sum = inv_sum; v->S = S; }
-    // release: the row buffer is no longer read on the common path (the list
-    // holds the window elements; the rare fallbacks read global memory)
-    release_row(c);
     // exact probability, bucket and edge flag of a listed element as its key
-    auto to_key = [&](unsigned long long e0) -> unsigned long long {
-        const int id = (int)(e0 >> 32);
-        const float l = __uint_as_float((unsigned)(e0 & 0xffffffffu));
+    auto to_key = [&](int id, float l) -> unsigned long long {
         const float pe = __fmul_rn(exp_one(__fsub_rn(l, mx)), inv_sum);
         float d = __fsub_rn(mx, l);
         if (clamp) d = fminf(d, dmax);
@@ -2030,41 +2025,45 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         const int eg = (fr > 0.5f - 2e-3f) ? 1 : (fr < -(0.5f - 2e-3f)) ? -1 : 0;
         return list_key(pe, id, bk_, eg);
     };
-    // compact the list into keys: per-thread slots by a block scan of the
-    // counts, then the overflow entries
-    const int nov = v->ln0;
-    const bool list_ok = nov <= LISTCAP - LREG * NT;
+    // gather the window elements marked by the exact pass into keys: block
+    // scan of the per-thread bit counts, then every thread writes its own
+    int tot;
     {
-        int tot;
-        const int mine = min(mycnt, LREG);
-        const int ofs = block_xscan_i(mine, tot, c.red);
-        unsigned long long ev[LREG], ov[LISTCAP / NT - LREG];
+        const uint32_t *mw = reinterpret_cast<const uint32_t *>(c.scr);
+        const int wbase = threadIdx.x & ~31, lane = threadIdx.x & 31;
+        const int ntrips = (nslots - wbase + 2 * NT - 1) / (2 * NT);  // this warp's trips
+        uint32_t w[MASKW];
+        int nb = 0;
 #pragma unroll
-        for (int q = 0; q < LREG; ++q) ev[q] = (q < mine) ? list[q * NT + threadIdx.x] : 0ull;
-#pragma unroll
-        for (int q = 0; q < LISTCAP / NT - LREG; ++q) {
-            const int i = threadIdx.x + q * NT;
-            ov[q] = (list_ok && i < nov) ? list[LREG * NT + i] : 0ull;
+        for (int q = 0; q < MASKW; ++q) {
+            w[q] = (4 * q < ntrips) ? mw[q * NT + threadIdx.x] : 0u;
+            nb += __popc(w[q]);
         }
+        int j = block_xscan_i(nb, tot, c.red);  // (its barriers end the mask reads)
+        const float it = v->inv_temp;
 #pragma unroll
-        for (int q = 0; q < LREG; ++q)
-            if (q < mine) ev[q] = to_key(ev[q]);
-#pragma unroll
-        for (int q = 0; q < LISTCAP / NT - LREG; ++q)
-            if (list_ok && threadIdx.x + q * NT < nov) ov[q] = to_key(ov[q]);
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < LREG; ++q)
-            if (q < mine) list[ofs + q] = ev[q];
-#pragma unroll
-        for (int q = 0; q < LISTCAP / NT - LREG; ++q) {
-            const int i = threadIdx.x + q * NT;
-            if (list_ok && i < nov) list[tot + i] = ov[q];
+        for (int q = 0; q < MASKW; ++q) {
+            uint32_t m = w[q];
+            while (m) {
+                const int bpos = __ffs(m) - 1;
+                m &= m - 1;
+                const int trip = 4 * q + (bpos >> 3), k = bpos & 7;
+                const int sl = wbase + trip * 2 * NT + (k < 4 ? 0 : NT) + lane;
+                // marked lanes lie in slots < nslots; the clamp only keeps a
+                // read inside the row buffer whatever the bits say
+                const int r = min(4 * sl + (k & 3), 4 * nslots - 1);
+                const float l = SCALE ? __fmul_rn(c.row[r], it) : c.row[r];
+                if (j < LISTCAP) list[j] = to_key(r - sh, l);
+                ++j;
+            }
         }
-        if (threadIdx.x == 0) v->ln1 = tot + (list_ok ? nov : 0);
-        __syncthreads();
     }
-    const int nl = list_ok ? v->ln1 : 0;
+    // release: the row buffer is no longer read on the common path (the list
+    // holds the window elements; the rare fallbacks read global memory)
+    release_row(c);
+    __syncthreads();
+    const bool list_ok = tot <= LISTCAP;
+    const int nl = list_ok ? tot : 0;
     // canonical sort
     Hit *hits = reinterpret_cast<Hit *>(c.scr + LISTCAP * 8 + 1024);
     if (list_ok) {
@@ -2296,7 +2295,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
                 v->thr = thr;
                 // every logit finite and a candidate: the streaming passes
                 // need no candidate test
-                v->clean = (chk == 0.0f) && (xmin >= thr) && (fabsf(mx) < 1e30f);
+                v->clean = (chk == 0.0f) && (xmin >= thr) && (fabsf(mx) < 1e30f) &&
+                           (v->inv_temp >= 1e-6f);
                 v->k = (v->top_k > 0 && v->top_k <= 256) ? v->top_k : 0;  // src/model.c:175
             }
             __syncthreads();
