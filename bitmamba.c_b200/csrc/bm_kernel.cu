@@ -873,33 +873,76 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
     int *hi = reinterpret_cast<int *>(c.scr + 1024);      // 256
     float *pv = reinterpret_cast<float *>(c.scr + 2048);  // 256 probabilities
     int *rk = reinterpret_cast<int *>(c.scr + 3072);      // 256 ranks
-    if (n <= KCAP) {
-        // by id (ids are unique)
-        if (n <= NT) sort_reg(kc, n);
-        else sort_keys(kc, n, reinterpret_cast<int *>(c.scr), KCAP);
-        if (warp == 0) {
-            const int first = min(n, k);
-            for (int q = lane; q < first; q += 32) {
-                hv[q] = __uint_as_float((unsigned)(kc[q] & 0xffffffffu));
-                hi[q] = (int)(kc[q] >> 32);
+    const float top_p = v->top_p;
+    const int ns = min(n, k);
+    // Survivors in the reference's heap layout (src/model.c:239-254): the
+    // candidates by id, a Floyd heap of the first k, root replacements.
+    auto exact_select = [&]() {
+        if (n <= KCAP) {
+            // by id (ids are unique)
+            if (n <= NT) sort_reg(kc, n);
+            else sort_keys(kc, n, reinterpret_cast<int *>(c.scr), KCAP);
+            if (warp == 0) {
+                const int first = min(n, k);
+                for (int q = lane; q < first; q += 32) {
+                    hv[q] = __uint_as_float((unsigned)(kc[q] & 0xffffffffu));
+                    hi[q] = (int)(kc[q] >> 32);
+                }
+                __syncwarp();
+                if (n > k) {  // heap top-k (src/model.c:240-254)
+                    warp_heapify(hv, hi, k, lane);
+                    for (int base = k; base < n; base += 32) {
+                        const int j = base + lane;
+                        float val = 0.f;
+                        int id = 0;
+                        if (j < n) {
+                            val = __uint_as_float((unsigned)(kc[j] & 0xffffffffu));
+                            id = (int)(kc[j] >> 32);
+                        }
+                        const float root = hv[0];
+                        unsigned mr = __ballot_sync(FULL, j < n && val > root);
+                        while (mr) {
+                            const int src = __ffs(mr) - 1;
+                            const float vb = __shfl_sync(FULL, val, src);
+                            const int ib = __shfl_sync(FULL, id, src);
+                            if (lane == 0 && vb > hv[0]) { hv[0] = vb; hi[0] = ib; heap_down(hv, hi, k, 0); }
+                            __syncwarp();
+                            mr &= mr - 1;
+                        }
+                    }
+                }
             }
-            __syncwarp();
-            if (n > k) {  // heap top-k (src/model.c:240-254)
-                warp_heapify(hv, hi, k, lane);
-                for (int base = k; base < n; base += 32) {
-                    const int j = base + lane;
-                    float val = 0.f;
-                    int id = 0;
-                    if (j < n) {
-                        val = __uint_as_float((unsigned)(kc[j] & 0xffffffffu));
-                        id = (int)(kc[j] >> 32);
+        } else {
+            // more candidates than the list holds: stream them in id order from
+            // global memory through the same heap rules
+            if (warp == 0) {
+                int filled = 0;
+                for (int base = 0; base < V; base += 32) {
+                    const int e = base + lane;
+                    float l = 0.f;
+                    bool ok = false;
+                    if (e < V) {
+                        l = logit_g(c, e, SCALE);
+                        ok = (l >= ethr);
+                    }
+                    const unsigned mk = __ballot_sync(FULL, ok);
+                    bool rest = ok;
+                    if (filled < k) {
+                        const int rank = __popc(mk & ((1u << lane) - 1));
+                        const int take = min(__popc(mk), k - filled);
+                        if (ok && rank < take) { hv[filled + rank] = l; hi[filled + rank] = e; }
+                        rest = ok && rank >= take;
+                        filled += take;
+                        __syncwarp();
+                        if (filled < k) continue;
+                        if (take > 0) warp_heapify(hv, hi, k, lane);
                     }
                     const float root = hv[0];
-                    unsigned mr = __ballot_sync(FULL, j < n && val > root);
+                    unsigned mr = __ballot_sync(FULL, rest && l > root);
                     while (mr) {
                         const int src = __ffs(mr) - 1;
-                        const float vb = __shfl_sync(FULL, val, src);
-                        const int ib = __shfl_sync(FULL, id, src);
+                        const float vb = __shfl_sync(FULL, l, src);
+                        const int ib = __shfl_sync(FULL, e, src);
                         if (lane == 0 && vb > hv[0]) { hv[0] = vb; hi[0] = ib; heap_down(hv, hi, k, 0); }
                         __syncwarp();
                         mr &= mr - 1;
@@ -907,94 +950,109 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
                 }
             }
         }
-    } else {
-        // more candidates than the list holds: stream them in id order from
-        // global memory through the same heap rules
-        if (warp == 0) {
-            int filled = 0;
-            for (int base = 0; base < V; base += 32) {
-                const int e = base + lane;
-                float l = 0.f;
-                bool ok = false;
-                if (e < V) {
-                    l = logit_g(c, e, SCALE);
-                    ok = (l >= ethr);
-                }
-                const unsigned mk = __ballot_sync(FULL, ok);
-                bool rest = ok;
-                if (filled < k) {
-                    const int rank = __popc(mk & ((1u << lane) - 1));
-                    const int take = min(__popc(mk), k - filled);
-                    if (ok && rank < take) { hv[filled + rank] = l; hi[filled + rank] = e; }
-                    rest = ok && rank >= take;
-                    filled += take;
-                    __syncwarp();
-                    if (filled < k) continue;
-                    if (take > 0) warp_heapify(hv, hi, k, lane);
-                }
-                const float root = hv[0];
-                unsigned mr = __ballot_sync(FULL, rest && l > root);
-                while (mr) {
-                    const int src = __ffs(mr) - 1;
-                    const float vb = __shfl_sync(FULL, l, src);
-                    const int ib = __shfl_sync(FULL, e, src);
-                    if (lane == 0 && vb > hv[0]) { hv[0] = vb; hi[0] = ib; heap_down(hv, hi, k, 0); }
-                    __syncwarp();
-                    mr &= mr - 1;
-                }
+    };
+    // Survivors by value: when top_p < 1 and no two of the k + 1 largest
+    // values are equal, the heap holds exactly the k largest and the stable
+    // sort by probability puts them in value order, so the heap layout is not
+    // needed (probability ties are checked after the softmax).  Sorts a copy
+    // of the candidates; false when a tie needs the heap layout.
+    auto value_select = [&]() -> bool {
+        unsigned long long *kv = kc + 1024;  // n <= NT: room for sort_reg's buffers
+        for (int i = threadIdx.x; i < n; i += NT) {
+            const unsigned long long e0 = kc[i];
+            const unsigned u = (unsigned)(e0 & 0xffffffffu);
+            const unsigned ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            kv[i] = ((unsigned long long)(~ord) << 32) | (unsigned)(e0 >> 32);
+        }
+        __syncthreads();
+        sort_reg(kv, n);
+        bool tie = false;
+        const int m = min(n, k + 1);
+        for (int j = threadIdx.x; j + 1 < m; j += NT)
+            tie |= (kv[j] >> 32) == (kv[j + 1] >> 32);
+        // a +inf value makes the sums NaN: the walk's fallback element then
+        // depends on the heap layout
+        if (threadIdx.x == 0) tie |= (~(unsigned)(kv[0] >> 32)) == 0xff800000u;
+        tie = __syncthreads_or(tie);
+        if (!tie) {
+            for (int j = threadIdx.x; j < ns; j += NT) {
+                const unsigned ord = ~(unsigned)(kv[j] >> 32);
+                const unsigned u = (ord & 0x80000000u) ? (ord ^ 0x80000000u) : ~ord;
+                hv[j] = __uint_as_float(u);
+                hi[j] = (int)(unsigned)(kv[j] & 0xffffffffu);
             }
         }
-    }
-    const int ns = min(n, k);
+        __syncthreads();
+        return !tie;
+    };
+    // survivor softmax (src/model.c:257-269) over hv[0..ns), warp 0, <= 8 per
+    // lane in array order; v->ln2 = 1 when the fp64 sum is order-independent
+    auto softmax = [&]() {
+        // survivor softmax (src/model.c:257-269), warp 0, <= 8 per lane in order
+        if (warp == 0) {
+            float val[8];
+            float lm = -1e30f;
+    #pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int j = lane * 8 + q;
+                val[q] = (j < ns) ? hv[j] : -1e30f;
+                if (j < ns) lm = fmaxf(lm, val[q]);
+            }
+            lm = warp_max(lm);
+            float ev[8];
+            double s = 0.0;
+            float emin = PINF;
+    #pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int j = lane * 8 + q;
+                ev[q] = (j < ns) ? expf(__fsub_rn(val[q], lm)) : 0.0f;
+                s += (double)ev[q];
+                if (j < ns && ev[q] > 0.0f) emin = fminf(emin, ev[q]);
+            }
+            emin = warp_min(emin);
+            double S = warp_sum(s);
+            // the tree sum equals the reference's sequential one when every term
+            // is a multiple of ulp(emin) and the sum stays below 2^53 of those
+            if (!(emin >= 0x1p-22f) && S == S) {
+                double q0 = 0.0;
+                for (int j = 0; j < ns; ++j) q0 += (double)__shfl_sync(FULL, ev[j & 7], j >> 3);
+                S = q0;
+            }
+            const float inv = __fdiv_rn(1.0f, __double2float_rn(S));
+    #pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int j = lane * 8 + q;
+                if (j < ns) pv[j] = __fmul_rn(ev[q], inv);
+            }
+            if (lane == 0) { v->S = S; v->ln2 = (emin >= 0x1p-22f) ? 1 : 0; }
+        }
+        __syncthreads();
+    };
+    bool by_value = (top_p < 1.0f) && n <= NT && value_select();
+    if (!by_value) exact_select();
     __syncthreads();
-    // survivor softmax (src/model.c:257-269), warp 0, <= 8 per lane in order
-    if (warp == 0) {
-        float val[8];
-        float lm = -1e30f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int j = lane * 8 + q;
-            val[q] = (j < ns) ? hv[j] : -1e30f;
-            if (j < ns) lm = fmaxf(lm, val[q]);
+    softmax();
+    if (by_value) {
+        // equal probabilities keep heap order in the stable sort; a sum that
+        // depends on the order must follow the heap layout too
+        bool tie = !v->ln2;
+        for (int j = threadIdx.x; j + 1 < ns; j += NT) tie |= pv[j] == pv[j + 1];
+        if (__syncthreads_or(tie)) {
+            by_value = false;
+            exact_select();
+            __syncthreads();
+            softmax();
         }
-        lm = warp_max(lm);
-        float ev[8];
-        double s = 0.0;
-        float emin = PINF;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int j = lane * 8 + q;
-            ev[q] = (j < ns) ? expf(__fsub_rn(val[q], lm)) : 0.0f;
-            s += (double)ev[q];
-            if (j < ns && ev[q] > 0.0f) emin = fminf(emin, ev[q]);
-        }
-        emin = warp_min(emin);
-        double S = warp_sum(s);
-        // the tree sum equals the reference's sequential one when every term
-        // is a multiple of ulp(emin) and the sum stays below 2^53 of those
-        if (!(emin >= 0x1p-22f) && S == S) {
-            double q0 = 0.0;
-            for (int j = 0; j < ns; ++j) q0 += (double)__shfl_sync(FULL, ev[j & 7], j >> 3);
-            S = q0;
-        }
-        const float inv = __fdiv_rn(1.0f, __double2float_rn(S));
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int j = lane * 8 + q;
-            if (j < ns) pv[j] = __fmul_rn(ev[q], inv);
-        }
-        if (lane == 0) v->S = S;
     }
-    __syncthreads();
     const double S = v->S;
-    const float top_p = v->top_p;
     if (S != S) {  // NaN mass: every comparison fails, the walk returns the last
         write_result(c, hi[ns - 1], pv[ns - 1], 3, n, ns, 1);
         return;
     }
-    // stable descending sort when top_p < 1 (src/model.c:275-276)
+    // stable descending sort when top_p < 1 (src/model.c:275-276); the value
+    // selection is in that order already
     unsigned long long *srt = kc;
-    if (top_p < 1.0f) {
+    if (top_p < 1.0f && !by_value) {
         for (int j = threadIdx.x; j < ns; j += NT) rk[j] = 0;
         __syncthreads();
         const int G = NT / ns;
