@@ -189,12 +189,11 @@ def oracle_batch(logits_host):
                        np.full(B, KNOBS["top_k"], np.int32))
 
 
-def cpu_leg(logits_host, u, threads, kind_pref="reference"):
+def cpu_leg(b, u, threads, kind_pref="reference"):
     """Time the reference's C sampler (oracle/_ref, else the oracle port) on
-    host rows.  Returns (ids, seconds, kind)."""
+    the rows of synth.Batch b.  Returns (ids, seconds, kind)."""
     sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests", "golden")]
     import oracle
-    b = oracle_batch(logits_host)
     if kind_pref == "reference" and oracle.has_ref():
         t = time.perf_counter()
         ids = oracle.ref_sample_batch_mt(b, u, threads)
@@ -235,12 +234,12 @@ def run_reference(args):
     for w in range(args.warmup):
         s = (w * rows_per_step) % pool_rows
         sel = np.arange(s, s + rows_per_step) % pool_rows
-        _, _, kind = cpu_leg(np.ascontiguousarray(logits[sel]), u[sel], threads)
+        _, _, kind = cpu_leg(oracle_batch(np.ascontiguousarray(logits[sel])), u[sel], threads)
     total = 0.0
     for k in range(args.steps):
         s = (k * rows_per_step) % pool_rows
         sel = np.arange(s, s + rows_per_step) % pool_rows
-        _, dt, kind = cpu_leg(np.ascontiguousarray(logits[sel]), u[sel], threads)
+        _, dt, kind = cpu_leg(oracle_batch(np.ascontiguousarray(logits[sel])), u[sel], threads)
         total += dt
     value = rows_per_step * args.steps / total
     line = {
@@ -258,6 +257,70 @@ def run_reference(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+class Workload:
+    """One rank's inputs: device tensors, host copies and the oracle view."""
+
+
+def slice_batch(b, n):
+    """The first n rows of a synth.Batch (CSR histories re-based)."""
+    sys.path[:0] = [os.path.join(ROOT, "tests", "golden")]
+    import synth
+    off = b.hist_off[:n + 1] - b.hist_off[0]
+    return synth.Batch(b.logits[:n], b.hist[b.hist_off[0]:b.hist_off[n]], off, b.temp[:n],
+                       b.penalty[:n], b.min_p[:n], b.top_p[:n], b.top_k[:n])
+
+
+def build_workload(args, torch, bm, dev, rank, world):
+    """c3 (the benchmark): generated on the device, knobs broadcast, no
+    history.  c1, c2, c4: the configs' seeded generators (histories, per-row
+    knobs for c4), built on the host and copied once."""
+    w = Workload()
+    B, V = args.B, args.V
+    w.name, w.B, w.V = args.workload, B, V
+    start, count = shard_rows(world * B, world, rank)
+    # this rank's slice of the global uniform stream
+    w.u_host = ref_uniforms(world * B)[start:start + count]
+    if args.workload == "c3":
+        w.logits = make_logits(torch, B, V, 1234 + rank, dev)
+        w.knobs = bm.knobs_array(KNOBS["temp"], KNOBS["penalty"], KNOBS["min_p"],
+                                 KNOBS["top_p"], KNOBS["top_k"])
+        w.knob_stride = 0
+        w.hist_h = w.off_h = None
+        w.batch = lambda h, n: oracle_batch(h)
+        w.desc = workload_config(B, V)
+    else:
+        sys.path[:0] = [os.path.join(ROOT, "tests", "golden")]
+        import synth
+        b = synth.MAKERS[args.workload](1000 + rank, B, V=V)
+        w.logits = torch.from_numpy(b.logits).to(dev)
+        w.knobs = bm.knobs_array(b.temp, b.penalty, b.min_p, b.top_p, b.top_k)
+        w.knob_stride = 1
+        w.hist_h, w.off_h = b.hist, b.hist_off
+        w.batch = lambda h, n, b=b: slice_batch(b, n)
+        w.desc = {"workload": f"{args.workload}: " + CONFIG_DESC[args.workload],
+                  "B_per_gpu": B, "V": V, "history_ids": int(b.hist.size),
+                  "uniforms": "reference XorShift64* rng_float stream, seed 42",
+                  "l2": "inputs larger than the 126 MB L2 when B*V*4 > 126 MB"}
+    w.knobs_d = torch.from_numpy(w.knobs.view(np.uint8).copy()).to(dev)
+    w.hist_d = torch.from_numpy(w.hist_h).to(dev) if w.hist_h is not None else None
+    w.off_d = torch.from_numpy(w.off_h).to(dev) if w.off_h is not None else None
+    H = 0 if w.hist_h is None else int(w.hist_h.size)
+    w.alg_bytes = (B * (4 * V + 4 + 4) + 4 * H + (8 * (B + 1) if H else 0) +
+                   32 * (B if w.knob_stride else 1))
+    w.h2d_bytes = B * V * 4 + B * 4 + 4 * H + (8 * (B + 1) if H else 0) + w.knobs.nbytes
+    return w
+
+
+CONFIG_DESC = {
+    "c1": "fp32 logits N(0, 2.5^2) with 8 ids +8, 400-id uniform history, "
+          "temp 0.8 penalty 1.15 min_p 0.05 top_p 0.9 top_k 40",
+    "c2": "fp32 logits 3*Gumbel(0,1), 1024-id Zipf(1.1) history, default knobs",
+    "c4": "fp32 logits N(0, 2^2), per-row knobs (temp U[0,1.5] 10% greedy, top_k in "
+          "{0,1,40,200}, top_p U[.5,1], min_p U[0,.2], penalty U[1,1.5]), histories "
+          "of U[0,2048] ids",
+}
 
 
 def run_ours(args):
@@ -279,14 +342,11 @@ def run_ours(args):
     B, V = args.B, args.V
     dev = torch.device("cuda", local)
     ctx = bm.Context(local)
-    logits = make_logits(torch, B, V, 1234 + rank, dev)
-    knobs = bm.knobs_array(KNOBS["temp"], KNOBS["penalty"], KNOBS["min_p"], KNOBS["top_p"],
-                           KNOBS["top_k"])
-    knobs_d = torch.from_numpy(knobs.view(np.uint8).copy()).to(dev)
-    # this rank's rows of the global batch (weak scaling: B rows per rank) and
-    # their slice of the global uniform stream
-    start, count = shard_rows(world * B, world, rank)
-    u_host = ref_uniforms(world * B)[start:start + count]
+    # this rank's rows of the global batch (weak scaling: B rows per rank)
+    wl = build_workload(args, torch, bm, dev, rank, world)
+    logits, knobs, knobs_d, u_host = wl.logits, wl.knobs, wl.knobs_d, wl.u_host
+    hist_ptr = wl.hist_d.data_ptr() if wl.hist_d is not None else 0
+    off_ptr = wl.off_d.data_ptr() if wl.off_d is not None else 0
     u_d = torch.from_numpy(u_host).to(dev)
     out_d = torch.empty(B, dtype=torch.int32, device=dev)
     # a dedicated stream: torch's legacy default stream has handle 0, which the
@@ -295,8 +355,9 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
 
     def launch():
-        ctx.sample_device(logits.data_ptr(), B, V, V, 0, 0, knobs_d.data_ptr(), 0,
-                          u_d.data_ptr(), out_d.data_ptr(), None, None, stream.cuda_stream)
+        ctx.sample_device(logits.data_ptr(), B, V, V, hist_ptr, off_ptr, knobs_d.data_ptr(),
+                          wl.knob_stride, u_d.data_ptr(), out_d.data_ptr(), None, None,
+                          stream.cuda_stream)
 
     def barrier():
         if dist is not None:
@@ -330,7 +391,7 @@ def run_ours(args):
     ms_max = max_over_ranks(dist, ms, dev)
     value = world * B * args.steps / (ms_max / 1e3)
     kernel_ms = ms / args.steps
-    alg_bytes = B * (4 * V + 4 + 4) + 32  # logits, uniform, id, knobs (no history)
+    alg_bytes = wl.alg_bytes  # logits, histories, uniform, id, knobs
     achieved = alg_bytes / (kernel_ms / 1e3) / 1e9
     peak, peak_src = peak_hbm()
     ids_dev = out_d.cpu().numpy()
@@ -342,12 +403,16 @@ def run_ours(args):
         h_u = torch.from_numpy(u_host).pin_memory()
         h_ids = torch.empty(B, dtype=torch.int32).pin_memory()
         h_knobs = torch.from_numpy(knobs.view(np.uint8).copy()).pin_memory()
+        h_hist = torch.from_numpy(wl.hist_h).pin_memory() if wl.hist_h is not None else None
+        h_off = torch.from_numpy(wl.off_h).pin_memory() if wl.off_h is not None else None
         L = bm.lib()
         c = bm.ctypes.c_void_p
 
         def call():
-            bm.check(L.bm_sample_batch_host(ctx.handle, c(h_logits.data_ptr()), B, V, V, None,
-                                            None, c(h_knobs.data_ptr()), 0,
+            bm.check(L.bm_sample_batch_host(ctx.handle, c(h_logits.data_ptr()), B, V, V,
+                                            c(h_hist.data_ptr()) if h_hist is not None else None,
+                                            c(h_off.data_ptr()) if h_off is not None else None,
+                                            c(h_knobs.data_ptr()), wl.knob_stride,
                                             c(h_u.data_ptr()), c(h_ids.data_ptr()), None,
                                             None))
         n_e2e = max(3, min(args.steps, 20))
@@ -367,7 +432,7 @@ def run_ours(args):
         if not np.array_equal(h_ids.numpy(), ids_dev):
             raise SystemExit("e2e ids differ from the device-resident run")
         e2e = {"value": world * B * n_e2e / (e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": B * V * 4 + B * 4 + 32, "d2h_bytes_per_step": B * 4,
+               "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": B * 4,
                "steps": n_e2e, "ms_per_step": e_ms / n_e2e}
 
     # ---- CPU baseline on a bounded sample (rank 0, N=1 only) ----------------
@@ -377,10 +442,10 @@ def run_ours(args):
         n = min(B, args.cpu_rows)
         threads = host_threads()
         h = logits[:n].cpu().numpy()
-        ids_cpu, dt, kind = cpu_leg(h, u_host[:n], threads)
+        rb = wl.batch(h, n)
+        ids_cpu, dt, kind = cpu_leg(rb, u_host[:n], threads)
         cpu = {"value": n / dt, "unit": UNIT, "cores": threads, "kind": kind,
-               "sample": f"first {n} rows of the workload (all four row kinds), "
-                         f"row-parallel pthreads"}
+               "sample": f"first {n} rows of the workload, row-parallel pthreads"}
         same = int((ids_cpu == ids_dev[:n]).sum())
         parity = {"rows": n, "identical_ids": same}
         if same < n:
@@ -389,7 +454,6 @@ def run_ours(args):
             sys.path[:0] = [os.path.join(ROOT, "tests")]
             import oracle
             import parity as parity_rule
-            rb = oracle_batch(h)
             _, _, res = oracle.sample_batch(rb, u_host[:n], threads=threads)
             rep = parity_rule.compare(ids_dev[:n], None, ids_cpu, None, res)
             parity.update({"exempt_mismatch": rep["exempt_mismatch"], "bad": rep["bad"],
@@ -406,7 +470,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": workload_config(B, V),
+        "data": "synthetic", "config": wl.desc,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes_per_launch": alg_bytes, "peak_source": peak_src,
@@ -429,6 +493,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c3",
+                    help="c3 is the benchmark; the others report the other configs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

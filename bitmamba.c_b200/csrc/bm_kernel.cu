@@ -50,6 +50,7 @@ constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
 constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
 constexpr int LISTCAP = 2048;                          // window list cap (entries)
 constexpr int MASKW = 4;                               // membership words per thread
+constexpr int WIDE_CAP = 256;                          // wide draw window: element cap
 constexpr int KREG = 2;                                // top_k path: slots per thread
 constexpr int KOVF = KCAP - KREG * NT;                 // top_k path: overflow entries
 constexpr int BPT = NB / NT;                            // estimate buckets per thread
@@ -86,6 +87,7 @@ struct __align__(16) Vars {
     double mc, ec, mk, ek, md;
     int bc, bk, bd0, bd1, cc, ck, cd, tail_cnt;
     int bc_hi, bd_hi, next_row, pad5;
+    int wd_lo, wd_lo_c, wd_hi, wd_hi_c;  // draw range buckets, counts above / through
 };
 
 struct Layout {
@@ -722,143 +724,230 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
     uint32_t *kh = reinterpret_cast<uint32_t *>(c.scr);                            // 8 x 128
     unsigned long long *kc = reinterpret_cast<unsigned long long *>(c.scr + 4096);  // KCAP
     const float bscale = __fdiv_rn(127.0f, 20.0f);  // src/model.c:184
-    // The candidates are listed by a second pass after the cut (about k plus
-    // the cut bucket's population); listing everything above the min_p
-    // threshold during the histogram pass costs more than that pass.
-    constexpr bool collect = false;
-
-    for (int i = threadIdx.x; i < 8 * HB; i += NT) kh[i] = 0;
-    if (threadIdx.x == 0) v->kcnt = 0;
-    __syncthreads();
-    uint32_t *myh = kh + (warp & 7) * HB;
-    unsigned long long lo8 = 0, hi8 = 0;  // per-thread counts of buckets 0..15
-    // candidates: every thread keeps its first KREG in its own list slots
-    // (index q * NT + tid), further ones go to the shared overflow part
-    // through an atomic (v->kcnt counts them)
-    int cnt = 0;
-    auto put = [&](unsigned long long ent) {
-        if (cnt < KREG) {
-            kc[cnt * NT + threadIdx.x] = ent;
-        } else {
-            const int pos = atomicAdd(&v->kcnt, 1);
-            if (pos < KOVF) kc[KREG * NT + pos] = ent;
-        }
-        ++cnt;
-    };
-    // histogram of (max - l) over l >= thr (src/model.c:185-195); the last
-    // bucket never decides the cut, so it is not counted
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        const float4 x = r4[s];
-        const float t[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
-            if (l >= thr) {
-                int b = x86_cvtt(__fmul_rn(__fsub_rn(mx, l), bscale));
-                b = min(max(b, 0), HB - 1);
-                // buckets 0..15 (where the cut of a top_k <= 256 nearly always
-                // lies, and where flat rows pile up) in 8-bit register fields
-                if (b < 8) lo8 += 1ull << (8 * b);
-                else if (b < 16) hi8 += 1ull << (8 * (b - 8));
-                else if (b < HB - 1) atomicAdd(&myh[b], 1u);
-                if (collect)
-                    put(((unsigned long long)(unsigned)(4 * s + q - sh) << 32) | __float_as_uint(l));
-            }
-        }
-    }
-    {
-        // widen the 8-bit fields to 16 bits (a warp holds at most 32 * 100
-        // per bucket), sum over the warp, add 16 counts to the histogram
-        const unsigned long long M = 0x00ff00ff00ff00ffull;
-        unsigned long long f[4] = {lo8 & M, (lo8 >> 8) & M, hi8 & M, (hi8 >> 8) & M};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) f[j] = warp_sum(f[j]);
-        if (lane < 16) {
-            const int j = lane >> 3, q = lane & 7;  // bucket = 8j + q
-            const unsigned long long fw = f[2 * j + (q & 1)];
-            const unsigned cnt16 = (unsigned)((fw >> (16 * (q >> 1))) & 0xffffu);
-            if (cnt16) atomicAdd(&kh[lane], cnt16);
-        }
-    }
-    __syncthreads();
+    constexpr bool collect = false;  // the streaming branch lists after the cut
+    float ethr;
     // cut bucket: first bucket whose running count reaches k (src/model.c:199-207)
-    if (warp == 0) {
-        uint32_t cq[4];
-        uint32_t ls = 0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t s = 0;
-            for (int cp = 0; cp < 8; ++cp) s += kh[cp * HB + 4 * lane + q];
-            cq[q] = s;
-            ls += s;
+    auto cut_of = [&]() {
+        if (warp == 0) {
+            uint32_t cq[4];
+            uint32_t ls = 0;
+    #pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t s = 0;
+                for (int cp = 0; cp < 8; ++cp) s += kh[cp * HB + 4 * lane + q];
+                cq[q] = s;
+                ls += s;
+            }
+            const uint32_t inc = warp_iscan(ls, lane);
+            uint32_t run = inc - ls;
+            int hit = INT_MAX;
+    #pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                run += cq[q];
+                if (hit == INT_MAX && run >= (uint32_t)k) hit = 4 * lane + q;
+            }
+            hit = warp_imin(hit);
+            if (lane == 0) v->kcut = (hit == INT_MAX) ? HB - 1 : hit;
         }
-        const uint32_t inc = warp_iscan(ls, lane);
-        uint32_t run = inc - ls;
-        int hit = INT_MAX;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            run += cq[q];
-            if (hit == INT_MAX && run >= (uint32_t)k) hit = 4 * lane + q;
-        }
-        hit = warp_imin(hit);
-        if (lane == 0) v->kcut = (hit == INT_MAX) ? HB - 1 : hit;
-    }
-    __syncthreads();
-    const int cut = v->kcut;
-    const float bthr = __fsub_rn(mx, __fdiv_rn((float)(cut + 1), bscale));  // src/model.c:210-211
-    const float ethr = bthr > thr ? bthr : thr;                          // src/model.c:213-214
-    int novf = v->kcnt;
-    if (!(collect && novf <= KOVF)) {
-        // extraction pass (src/model.c:217-224), unordered here
         __syncthreads();
-        if (threadIdx.x == 0) v->kcnt = 0;
-        cnt = 0;
-        __syncthreads();
-        for (int s = threadIdx.x; s < nslots; s += NT) {
+    };
+    // Above a real min_p threshold the candidates are usually few: one pass
+    // marks them (a bit per element, no branch), a gather lists them, and the
+    // histogram, cut and extraction work on that list.
+    bool listed = false;
+    if (v->min_p > 0.0f) {
+        uint32_t *mk = reinterpret_cast<uint32_t *>(kc);  // MASKW words per thread
+        uint32_t w = 0;
+        int i = 0;
+        for (int s = threadIdx.x; s < nslots; s += NT, ++i) {
             const float4 x = r4[s];
-            const float t[4] = {x.x, x.y, x.z, x.w};
+            float t[4] = {x.x, x.y, x.z, x.w};
+            uint32_t b4 = 0;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
-                if (l >= ethr)
-                    put(((unsigned long long)(unsigned)(4 * s + q - sh) << 32) | __float_as_uint(l));
+                b4 |= (l >= thr ? 1u : 0u) << q;
+            }
+            w |= b4 << (4 * (i & 7));
+            if ((i & 7) == 7) { mk[(i >> 3) * NT + threadIdx.x] = w; w = 0; }
+        }
+        if (i & 7) mk[(i >> 3) * NT + threadIdx.x] = w;
+        const int nw = (i + 7) >> 3;
+        uint32_t wv[MASKW];
+        int nb = 0;
+#pragma unroll
+        for (int q = 0; q < MASKW; ++q) {
+            wv[q] = (q < nw) ? mk[q * NT + threadIdx.x] : 0u;
+            nb += __popc(wv[q]);
+        }
+        int tot;
+        int j = block_xscan_i(nb, tot, c.red);  // (its barriers end the mask reads)
+        if (tot <= KCAP) {
+            listed = true;
+            for (int q = 0; q < 8 * HB; q += NT)
+                if (q + (int)threadIdx.x < 8 * HB) kh[q + threadIdx.x] = 0;
+#pragma unroll
+            for (int q = 0; q < MASKW; ++q) {
+                uint32_t m = wv[q];
+                while (m) {
+                    const int bp = __ffs(m) - 1;
+                    m &= m - 1;
+                    const int s = threadIdx.x + (8 * q + (bp >> 2)) * NT;
+                    const int r = min(4 * s + (bp & 3), 4 * nslots - 1);
+                    const float l = SCALE ? __fmul_rn(c.row[r], inv_temp) : c.row[r];
+                    kc[j++] = ((unsigned long long)(unsigned)(r - sh) << 32) | __float_as_uint(l);
+                }
+            }
+            __syncthreads();
+            // histogram of the listed candidates (src/model.c:185-195); the last
+            // bucket never decides the cut, so it is not counted
+            for (int q = threadIdx.x; q < tot; q += NT) {
+                const float l = __uint_as_float((unsigned)(kc[q] & 0xffffffffu));
+                int b = x86_cvtt(__fmul_rn(__fsub_rn(mx, l), bscale));
+                b = min(max(b, 0), HB - 1);
+                if (b < HB - 1) atomicAdd(&kh[b], 1u);
+            }
+            __syncthreads();
+            cut_of();
+            const int cut = v->kcut;
+            const float bthr = __fsub_rn(mx, __fdiv_rn((float)(cut + 1), bscale));  // src/model.c:210-211
+            ethr = bthr > thr ? bthr : thr;                                      // src/model.c:213-214
+            // the extraction set (src/model.c:217-224): the listed candidates
+            // with l >= ethr, compacted
+            constexpr int PQ = KCAP / NT;
+            unsigned long long e[PQ];
+            bool keep[PQ];
+            int mine = 0;
+#pragma unroll
+            for (int q = 0; q < PQ; ++q) {
+                const int jj = threadIdx.x + q * NT;
+                e[q] = (jj < tot) ? kc[jj] : 0ull;
+                keep[q] = jj < tot && __uint_as_float((unsigned)(e[q] & 0xffffffffu)) >= ethr;
+                mine += keep[q] ? 1 : 0;
+            }
+            int n2;
+            int o = block_xscan_i(mine, n2, c.red);
+#pragma unroll
+            for (int q = 0; q < PQ; ++q)
+                if (keep[q]) kc[o++] = e[q];
+            if (threadIdx.x == 0) v->kcnt = n2;
+            __syncthreads();
+        } else {
+            __syncthreads();
+        }
+    }
+    if (!listed) {
+        for (int i = threadIdx.x; i < 8 * HB; i += NT) kh[i] = 0;
+        if (threadIdx.x == 0) v->kcnt = 0;
+        __syncthreads();
+        uint32_t *myh = kh + (warp & 7) * HB;
+        unsigned long long lo8 = 0, hi8 = 0;  // per-thread counts of buckets 0..15
+        // candidates: every thread keeps its first KREG in its own list slots
+        // (index q * NT + tid), further ones go to the shared overflow part
+        // through an atomic (v->kcnt counts them)
+        int cnt = 0;
+        auto put = [&](unsigned long long ent) {
+            if (cnt < KREG) {
+                kc[cnt * NT + threadIdx.x] = ent;
+            } else {
+                const int pos = atomicAdd(&v->kcnt, 1);
+                if (pos < KOVF) kc[KREG * NT + pos] = ent;
+            }
+            ++cnt;
+        };
+        // histogram of (max - l) over l >= thr (src/model.c:185-195); the last
+        // bucket never decides the cut, so it is not counted
+        for (int s = threadIdx.x; s < nslots; s += NT) {
+            const float4 x = r4[s];
+            const float t[4] = {x.x, x.y, x.z, x.w};
+    #pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
+                if (l >= thr) {
+                    int b = x86_cvtt(__fmul_rn(__fsub_rn(mx, l), bscale));
+                    b = min(max(b, 0), HB - 1);
+                    // buckets 0..15 (where the cut of a top_k <= 256 nearly always
+                    // lies, and where flat rows pile up) in 8-bit register fields
+                    if (b < 8) lo8 += 1ull << (8 * b);
+                    else if (b < 16) hi8 += 1ull << (8 * (b - 8));
+                    else if (b < HB - 1) atomicAdd(&myh[b], 1u);
+                    if (collect)
+                        put(((unsigned long long)(unsigned)(4 * s + q - sh) << 32) | __float_as_uint(l));
+                }
+            }
+        }
+        {
+            // widen the 8-bit fields to 16 bits (a warp holds at most 32 * 100
+            // per bucket), sum over the warp, add 16 counts to the histogram
+            const unsigned long long M = 0x00ff00ff00ff00ffull;
+            unsigned long long f[4] = {lo8 & M, (lo8 >> 8) & M, hi8 & M, (hi8 >> 8) & M};
+    #pragma unroll
+            for (int j = 0; j < 4; ++j) f[j] = warp_sum(f[j]);
+            if (lane < 16) {
+                const int j = lane >> 3, q = lane & 7;  // bucket = 8j + q
+                const unsigned long long fw = f[2 * j + (q & 1)];
+                const unsigned cnt16 = (unsigned)((fw >> (16 * (q >> 1))) & 0xffffu);
+                if (cnt16) atomicAdd(&kh[lane], cnt16);
             }
         }
         __syncthreads();
-        novf = v->kcnt;
-    }
-    // the extraction set: the listed candidates with l >= ethr, compacted
-    // (block scan of the per-thread counts; fixed-size register staging)
-    {
-        constexpr int OQ = KOVF / NT;
-        unsigned long long e[KREG + OQ];
-        bool keep[KREG + OQ];
-        const int own = min(cnt, KREG);
-        const bool fits = novf <= KOVF;
-#pragma unroll
-        for (int q = 0; q < KREG; ++q) {
-            e[q] = (q < own) ? kc[q * NT + threadIdx.x] : 0ull;
-            keep[q] = fits && q < own && __uint_as_float((unsigned)(e[q] & 0xffffffffu)) >= ethr;
+        cut_of();
+        const int cut = v->kcut;
+        const float bthr = __fsub_rn(mx, __fdiv_rn((float)(cut + 1), bscale));  // src/model.c:210-211
+        ethr = bthr > thr ? bthr : thr;                                      // src/model.c:213-214
+        int novf = v->kcnt;
+        if (!(collect && novf <= KOVF)) {
+            // extraction pass (src/model.c:217-224), unordered here
+            __syncthreads();
+            if (threadIdx.x == 0) v->kcnt = 0;
+            cnt = 0;
+            __syncthreads();
+            for (int s = threadIdx.x; s < nslots; s += NT) {
+                const float4 x = r4[s];
+                const float t[4] = {x.x, x.y, x.z, x.w};
+    #pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
+                    if (l >= ethr)
+                        put(((unsigned long long)(unsigned)(4 * s + q - sh) << 32) | __float_as_uint(l));
+                }
+            }
+            __syncthreads();
+            novf = v->kcnt;
         }
-#pragma unroll
-        for (int q = 0; q < OQ; ++q) {
-            const int i = threadIdx.x + q * NT;
-            e[KREG + q] = (fits && i < novf) ? kc[KREG * NT + i] : 0ull;
-            keep[KREG + q] = fits && i < novf &&
-                             __uint_as_float((unsigned)(e[KREG + q] & 0xffffffffu)) >= ethr;
+        // the extraction set: the listed candidates with l >= ethr, compacted
+        // (block scan of the per-thread counts; fixed-size register staging)
+        {
+            constexpr int OQ = KOVF / NT;
+            unsigned long long e[KREG + OQ];
+            bool keep[KREG + OQ];
+            const int own = min(cnt, KREG);
+            const bool fits = novf <= KOVF;
+    #pragma unroll
+            for (int q = 0; q < KREG; ++q) {
+                e[q] = (q < own) ? kc[q * NT + threadIdx.x] : 0ull;
+                keep[q] = fits && q < own && __uint_as_float((unsigned)(e[q] & 0xffffffffu)) >= ethr;
+            }
+    #pragma unroll
+            for (int q = 0; q < OQ; ++q) {
+                const int i = threadIdx.x + q * NT;
+                e[KREG + q] = (fits && i < novf) ? kc[KREG * NT + i] : 0ull;
+                keep[KREG + q] = fits && i < novf &&
+                                 __uint_as_float((unsigned)(e[KREG + q] & 0xffffffffu)) >= ethr;
+            }
+            int mine = 0;
+    #pragma unroll
+            for (int q = 0; q < KREG + OQ; ++q) mine += keep[q] ? 1 : 0;
+            int tot;
+            int j = block_xscan_i(mine, tot, c.red);
+            __syncthreads();
+    #pragma unroll
+            for (int q = 0; q < KREG + OQ; ++q)
+                if (keep[q]) kc[j++] = e[q];
+            // more candidates than the list holds: the global-memory path below
+            if (threadIdx.x == 0) v->kcnt = fits ? tot : KCAP + 1;
+            __syncthreads();
         }
-        int mine = 0;
-#pragma unroll
-        for (int q = 0; q < KREG + OQ; ++q) mine += keep[q] ? 1 : 0;
-        int tot;
-        int j = block_xscan_i(mine, tot, c.red);
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < KREG + OQ; ++q)
-            if (keep[q]) kc[j++] = e[q];
-        // more candidates than the list holds: the global-memory path below
-        if (threadIdx.x == 0) v->kcnt = fits ? tot : KCAP + 1;
-        __syncthreads();
     }
     const int n = v->kcnt;
     // the buffer is no longer needed: the rest works on the candidate list
@@ -1435,37 +1524,55 @@ __device__ __noinline__ void replay_top256(Ctx c, bool scale, int n) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float inv_sum = c.v->inv_sum;
     const int V = c.V;
-    if (warp == 0) {
-        int filled = 0;
-        for (int base = 0; base < V; base += 32) {
-            const int id = base + lane;
-            float ev = -0.0f;
-            if (id < V) ev = e_global(c, id, scale);
-            const bool cand = __float_as_int(ev) >= 0;
-            const float p = __fmul_rn(cand ? ev : 0.0f, inv_sum);
-            const unsigned mk = __ballot_sync(FULL, cand);
-            bool rest = cand;
-            if (filled < 256) {
-                const int rk = __popc(mk & ((1u << lane) - 1));
-                const int take = min(__popc(mk), 256 - filled);
-                if (cand && rk < take) { hv[filled + rk] = p; hi[filled + rk] = id; }
-                rest = cand && rk >= take;
-                filled += take;
-                __syncwarp();
-                if (filled < 256) continue;
-                if (take > 0) warp_heapify(hv, hi, 256, lane);
+    // chunks of probabilities computed by every thread from global memory
+    // (-1 for non-candidates), then fed to the heap by warp 0 in id order
+    constexpr int CH = 2048;
+    float *pch = reinterpret_cast<float *>(c.scr + 8192);  // 8 KB
+    int filled = 0;
+    for (int c0 = 0; c0 < V; c0 += CH) {
+        for (int i = threadIdx.x; i < CH; i += NT) {
+            const int id = c0 + i;
+            float pv = -1.0f;
+            if (id < V) {
+                const float ev = e_global(c, id, scale);
+                if (__float_as_int(ev) >= 0) pv = __fmul_rn(ev, inv_sum);
             }
-            const float root = hv[0];
-            unsigned mr = __ballot_sync(FULL, rest && p > root);
-            while (mr) {
-                const int src = __ffs(mr) - 1;
-                const float pb = __shfl_sync(FULL, p, src);
-                const int ib = __shfl_sync(FULL, id, src);
-                if (lane == 0 && pb > hv[0]) { hv[0] = pb; hi[0] = ib; heap_down(hv, hi, 256, 0); }
-                __syncwarp();
-                mr &= mr - 1;
+            pch[i] = pv;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int base = 0; base < CH && c0 + base < V; base += 32) {
+                const int id = c0 + base + lane;
+                const float pv = pch[base + lane];
+                const bool cand = pv >= 0.0f;
+                const float p = cand ? pv : 0.0f;
+                const unsigned mk = __ballot_sync(FULL, cand);
+                bool rest = cand;
+                if (filled < 256) {
+                    const int rk = __popc(mk & ((1u << lane) - 1));
+                    const int take = min(__popc(mk), 256 - filled);
+                    if (cand && rk < take) { hv[filled + rk] = p; hi[filled + rk] = id; }
+                    rest = cand && rk >= take;
+                    filled += take;
+                    __syncwarp();
+                    if (filled < 256) continue;
+                    if (take > 0) warp_heapify(hv, hi, 256, lane);
+                }
+                const float root = hv[0];
+                unsigned mr = __ballot_sync(FULL, rest && p > root);
+                while (mr) {
+                    const int src = __ffs(mr) - 1;
+                    const float pb = __shfl_sync(FULL, p, src);
+                    const int ib = __shfl_sync(FULL, id, src);
+                    if (lane == 0 && pb > hv[0]) { hv[0] = pb; hi[0] = ib; heap_down(hv, hi, 256, 0); }
+                    __syncwarp();
+                    mr &= mr - 1;
+                }
             }
         }
+        __syncthreads();
+    }
+    if (warp == 0) {
         __syncwarp();
         for (int q = lane; q < 256; q += 32) outk[q] = canon_key(hv[q], q);
     }
@@ -1903,7 +2010,9 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     const double mex = block_xscan_d(msum, mt, c.red);
     int ncand;
     const int cex = block_xscan_i(csum, ncand, c.red);
-    if (threadIdx.x == 0) { v->n_cand = ncand; v->bc = NB; v->bk = NB; v->bd0 = NB; }
+    if (threadIdx.x == 0) {
+        v->n_cand = ncand; v->bc = NB; v->bk = NB; v->bd0 = NB; v->wd_lo = NB; v->wd_hi = NB;
+    }
     if (ncand == 0) {  // argmax guard (src/model.c:296-303)
         release_row(c);
         const int id = guard_argmax(c);
@@ -1986,10 +2095,13 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             const double nxt = run + mb[q];
             if (want_cut && cb[q] > 0 && run < fr_c && nxt >= fr_c) {
                 v->bc = bb + q; v->cc = crun; v->mc = (fr_c - run) / mb[q];
+                v->ec = nxt / mt;  // the cut's mass lies in [top_p, ec]
             }
             if (want_k && top_k - 1 >= crun && top_k - 1 < crun + cb[q]) {
                 v->bk = bb + q; v->ck = crun;
                 v->ek = (run + (double)(top_k - crun) * (mb[q] / (double)cb[q])) / mt;
+                v->mk = run / mt;    // the top_k mass lies in [mk, aux0]
+                v->aux0 = nxt / mt;
             }
             run = nxt;
             crun += cb[q];
@@ -2003,6 +2115,12 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         double ns = want_cut ? (double)top_p : 1.0;
         if (want_k && v->bk < NB) ns = fmin(ns, v->ek);
         const double fr_d = (double)v->u * ns * mt;
+        // the range new_sum can take, for a wide window over sparse buckets
+        // (few candidates: the cut's element can carry much of the mass)
+        double lo = want_cut ? (double)top_p : 1.0, hi = (want_cut && v->bc < NB) ? v->ec : 1.0;
+        if (want_k && v->bk < NB) { lo = fmin(lo, v->mk); hi = fmin(hi, v->aux0); }
+        const double fr_lo = (double)v->u * lo * mt * (1.0 - 1e-3);
+        const double fr_hi = (double)v->u * fmin(hi * (1.0 + 1e-3), 1.0 - 1e-9) * mt;
         double run = mex;
         int crun = cex;
 #pragma unroll
@@ -2011,6 +2129,8 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             if (cb[q] > 0 && run <= fr_d && nxt > fr_d) {
                 v->bd0 = bb + q; v->cd = crun; v->md = (fr_d - run) / mb[q];
             }
+            if (run <= fr_lo && nxt > fr_lo) { v->wd_lo = bb + q; v->wd_lo_c = crun; }
+            if (run <= fr_hi && nxt > fr_hi) { v->wd_hi = bb + q; v->wd_hi_c = crun + cb[q]; }
             run = nxt;
             crun += cb[q];
         }
@@ -2028,6 +2148,15 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         if (v->bd0 < NB) {
             if (v->md < 0.5 && v->bd0 > 0) { v->cd -= (int)hc[v->bd0 - 1]; v->bd0 -= 1; }
             else v->bd_hi = min(v->bd0 + 1, NB - 1);
+            // sparse buckets: the window spans the draw's whole range, one
+            // bucket of margin each side, while it holds few elements
+            const int w0 = v->wd_lo, w1 = v->wd_hi;
+            if (w0 < NB && w1 < NB && w0 <= v->bd0 && w1 >= v->bd_hi) {
+                const int a = max(w0 - 1, 0), b = min(w1 + 1, NB - 1);
+                const int ca = v->wd_lo_c - (a < w0 ? (int)hc[a] : 0);
+                const int cb_ = v->wd_hi_c + (b > w1 ? (int)hc[b] : 0);
+                if (cb_ - ca <= WIDE_CAP) { v->bd0 = a; v->bd_hi = b; v->cd = ca; }
+            }
         }
     }
     __syncthreads();
