@@ -4,9 +4,10 @@
  * Drop-in replacement for the sampling tail of jserv/bitmamba.c:
  *   repetition penalty (src/model.c:1268-1305) -> sample_advanced /
  *   filter_and_sample (src/model.c:37-361) -> rng_float (src/utils.c:117-140).
- * The batched entry points run hand-written sm_100a CUDA kernels, one CTA per
- * logits row.  There is no CPU fallback: every sampling entry point fails
- * with BM_ERR_NO_DEVICE / BM_ERR_CUDA when no usable B200 is present.
+ * The batched entry points run a hand-written sm_100a CUDA kernel: one
+ * persistent CTA per SM, one logits row at a time in shared memory.  There is
+ * no CPU fallback: every sampling entry point fails with BM_ERR_NO_DEVICE /
+ * BM_ERR_CUDA when no usable B200 is present.
  *
  * Semantics kept from the reference, row by row:
  *   - penalty applied once per distinct history id in [0, V), skipping the
@@ -20,8 +21,9 @@
  *     full-vocabulary path for other top_k (lazy id-order walk, top-256
  *     partial sort, full sort), then the nucleus cut and the CDF walk against
  *     r = u * (float)new_sum (src/model.c:156-360, 72-118).
- * Token ids equal the reference's; probabilities agree to float rounding
- * (the device expf differs from glibc's by at most 2 ulp).
+ * Token ids equal the reference's except where the draw or the nucleus cut
+ * lies within 1e-5 of a CDF boundary; probabilities agree to a few ulps (the
+ * device exp is within 3 ulp of the correctly rounded value).
  *
  * Thread safety: a bm_ctx_t may be used by one host thread at a time.  The
  * reference-convention calls (bm_sample_row, bm_sample_rows) share one
