@@ -88,6 +88,10 @@ struct __align__(16) Vars {
     int bc, bk, bd0, bd1, cc, ck, cd, tail_cnt;
     int bc_hi, bd_hi, next_row, pad5;
     int wd_lo, wd_lo_c, wd_hi, wd_hi_c;  // draw range buckets, counts above / through
+    const bm_knobs_t *p_knobs;  // launch parameters the row release prefetches from
+    const float *p_uniform;
+    const int64_t *p_hist_off;
+    int64_t p_knob_stride;
 };
 
 struct Layout {
@@ -136,6 +140,15 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "[%3];" ::"r"(sa(dst)),
         "l"(src), "r"(bytes), "r"(sa(b))
         : "memory");
+}
+// 4-byte asynchronous global -> shared copy (the ragged row edges)
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
@@ -589,6 +602,11 @@ __device__ __forceinline__ void release_row(Ctx &c) {
         if (next_row < c.B) {
             if (lane < NCHUNK)
                 issue_chunk(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row, lane);
+            // the next row's knobs, uniform and history offsets into L1
+            const Vars *v = c.v;
+            if (lane == NCHUNK + 1) prefetch_l1(v->p_knobs + (int64_t)next_row * v->p_knob_stride);
+            if (lane == NCHUNK + 2 && v->p_uniform) prefetch_l1(v->p_uniform + next_row);
+            if (lane == NCHUNK + 3 && v->p_hist_off) prefetch_l1(v->p_hist_off + next_row);
             // warm L2 with the row claimed about one round later
             const int pre = next_row + (int)gridDim.x;
             if (lane == NCHUNK && pre < c.B) prefetch_row(c.logits + (int64_t)pre * c.ld, c.V);
@@ -674,10 +692,32 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         r4[s] = x;
         consume(s, x, valid);
     };
-    // plain head slot(s) (all slots when the row is tiny)
-    for (int s = threadIdx.x; s < s0; s += NT) plain(s);
-    // interior, chunk by chunk
     const int nint = s1 - s0;
+    // rows with a bulk-copied interior have at most one ragged head slot and
+    // two tail slots: the last threads load them first and consume them after
+    // the interior, so the global-load latency overlaps the chunk waits
+    int es = -1;
+    unsigned evld = 0;
+    if (nint > 0) {
+        const int ntl = nslots - s1, nedge = s0 + ntl;
+        const int i = (int)threadIdx.x - (NT - nedge);
+        if (i >= 0) {
+            es = (i < s0) ? i : s1 + (i - s0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int e = 4 * es + q - sh;
+                const bool in = e >= 0 && e < V;
+                if (in) cp_async4(c.row + 4 * es + q, c.g + e);
+                else c.row[4 * es + q] = __int_as_float(0x7fc00000);
+                evld |= (unsigned)in << q;
+            }
+            cp_async_commit();
+        }
+    } else {
+        // tiny row: every slot by plain loads
+        for (int s = threadIdx.x; s < nslots; s += NT) plain(s);
+    }
+    // interior, chunk by chunk
     if (nint > 0) {
         for (int ch = 0; ch < NCHUNK; ++ch) {
             const int a = s0 + (ch * nint) / NCHUNK, b = s0 + ((ch + 1) * nint) / NCHUNK;
@@ -691,7 +731,10 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
             for (; s < b; s += NT) consume(s, r4[s], 0xfu);
         }
     }
-    for (int s = max(s1, s0) + (int)threadIdx.x; s < nslots; s += NT) plain(s);
+    if (es >= 0) {
+        cp_async_wait_all();
+        consume(es, r4[es], evld);
+    }
 }
 
 // Argmax over the scaled penalised logits with the guard semantics of
@@ -2375,6 +2418,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     const int tid = threadIdx.x;
 
     if (tid == 0) {
+        v->p_knobs = P.knobs;
+        v->p_uniform = P.uniform;
+        v->p_hist_off = P.hist_off;
+        v->p_knob_stride = P.knob_stride;
         for (int i = 0; i < NCHUNK; ++i) mbar_init(&c.mbar[i], 1);
         fence_mbar_init();
         v->fail = 0;
@@ -2429,11 +2476,18 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             const int h0 = v->h0, h1 = v->h1;
             for (int i = tid; i < L.nbw; i += NT) c.bits[i] = 0u;
             __syncthreads();
-            for (int i = h0 + tid; i < h1; i += NT) {
-                const int id = P.hist[i];
-                if (id >= 0 && id < V && !protected_id(id)) {
-                    const int b = id + sh;
-                    atomicOr(&c.bits[b >> 5], 1u << (b & 31));
+            // four loads in flight per thread before the atomics
+            for (int i = h0 + tid; i < h1; i += 4 * NT) {
+                int ids[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) ids[q] = (i + q * NT < h1) ? __ldg(&P.hist[i + q * NT]) : -1;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int id = ids[q];
+                    if (id >= 0 && id < V && !protected_id(id)) {
+                        const int b = id + sh;
+                        atomicOr(&c.bits[b >> 5], 1u << (b & 31));
+                    }
                 }
             }
             __syncthreads();

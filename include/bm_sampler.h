@@ -162,7 +162,7 @@ int bm_sample_batch(bm_ctx_t *ctx, const float *d_logits, int B, int V,
  * time (different streams, or threads without ordering) race on the row
  * schedule and must not be made; order them on one stream.
  *
- * Limits: V <= bm_max_vocab (50288 on a B200) else BM_ERR_UNSUPPORTED;
+ * Limits: V <= bm_max_vocab (50280 on a B200) else BM_ERR_UNSUPPORTED;
  * B <= 2^30 rows per call else BM_ERR_INVALID_ARG.  There is no context
  * error flag to check: a row whose bounded wait in the kernel expired gets
  * id -1.
