@@ -50,7 +50,6 @@ constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
 constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
 constexpr int LISTCAP = 2048;                          // window list cap (entries)
 constexpr int MASKW = 4;                               // membership words per thread
-constexpr int WIDE_CAP = 256;                          // wide draw window: element cap
 constexpr int KREG = 2;                                // top_k path: slots per thread
 constexpr int KOVF = KCAP - KREG * NT;                 // top_k path: overflow entries
 constexpr int BPT = NB / NT;                            // estimate buckets per thread
@@ -87,7 +86,7 @@ struct __align__(16) Vars {
     double mc, ec, mk, ek, md;
     int bc, bk, bd0, bd1, cc, ck, cd, tail_cnt;
     int bc_hi, bd_hi, next_row, pad5;
-    int wd_lo, wd_lo_c, wd_hi, wd_hi_c;  // draw range buckets, counts above / through
+    double rlo, rhi;  // range of the draw r (normalised mass)
     const bm_knobs_t *p_knobs;  // launch parameters the row release prefetches from
     const float *p_uniform;
     const int64_t *p_hist_off;
@@ -392,6 +391,50 @@ __device__ __forceinline__ int block_xscan_i(int v, int &total, Red r) {
     int winc = warp_iscan(w, lane);
     int woff = __shfl_sync(FULL, winc - w, warp);
     total = __shfl_sync(FULL, winc, 31);
+    __syncthreads();
+    return woff + inc - v;
+}
+
+// exclusive block scan of a double and an int at once (in place); totals out
+__device__ __forceinline__ void block_xscan_di(double &vd, int &vi, double &td, int &ti, Red r) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const double incd = warp_iscan(vd, lane);
+    const int inci = warp_iscan(vi, lane);
+    if (lane == 31) { r.d[warp] = incd; r.i[warp] = inci; }
+    __syncthreads();
+    const double wd = lane < NW ? r.d[lane] : 0.0;
+    const int wi = lane < NW ? r.i[lane] : 0;
+    const double wincd = warp_iscan(wd, lane);
+    const int winci = warp_iscan(wi, lane);
+    const double woffd = __shfl_sync(FULL, wincd - wd, warp);
+    const int woffi = __shfl_sync(FULL, winci - wi, warp);
+    td = __shfl_sync(FULL, wincd, 31);
+    ti = __shfl_sync(FULL, winci, 31);
+    __syncthreads();
+    vd = woffd + incd - vd;
+    vi = woffi + inci - vi;
+}
+
+// exclusive block scan of v (returned, total in `total`) and block sums of
+// three ints s (in place)
+__device__ __forceinline__ int block_xscan_i4(int v, int (&s)[3], int &total, Red r) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int inc = warp_iscan(v, lane);
+    int ws[3];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) ws[t] = warp_sum(s[t]);
+    if (lane == 31) {
+        r.i[warp] = inc;
+#pragma unroll
+        for (int t = 0; t < 3; ++t) r.i[(t + 1) * NW + warp] = ws[t];
+    }
+    __syncthreads();
+    const int w = lane < NW ? r.i[lane] : 0;
+    const int winc = warp_iscan(w, lane);
+    const int woff = __shfl_sync(FULL, winc - w, warp);
+    total = __shfl_sync(FULL, winc, 31);
+#pragma unroll
+    for (int t = 0; t < 3; ++t) s[t] = warp_sum(lane < NW ? r.i[(t + 1) * NW + lane] : 0);
     __syncthreads();
     return woff + inc - v;
 }
@@ -1658,128 +1701,112 @@ __device__ __forceinline__ float2 kf_pair(float2 d, float2 iw2, float2 mg2, floa
     return __ffma2_rn(d, iw2, mg2);
 }
 
-// Pass 1 of the sorted path: bucket counts (one shared atomic per candidate;
-// the clamped last bucket is counted in a register).  CLEAN rows (every logit
-// finite and a candidate) skip the candidate test: junk lanes have keys
-// beyond the last bucket.
-template <bool SCALE, bool CLAMP, bool CLEAN>
-__device__ __forceinline__ void hist_pass(Ctx &c, float inv_w, float dmax) {
+// Pass 1 of the sorted path: per bucket the e-mass of its candidates, one
+// 32-bit shared atomic per candidate (plus a count atomic when CNT: only rows
+// whose top_k position is needed).  A member with d = b*w + t (|t| <= w/2;
+// t = fma(-b, w, d), exact to one rounding) has e = exp(-d) = E_b * exp(-t),
+// E_b = exp(-b*w).  The pass adds G = round(2^16 exp(-t)) (the cubic Taylor
+// polynomial: |t| < 0.01, error below 4e-10; G in [64880, 66200], so a
+// bucket's sum stays below 2^32 for any V <= 64880), so that
+//   mass_b = E_b * 2^-16 * sum_b
+// is the members' e-sum to within 2^-17 relative per member (rounding, not
+// bias: below 4e-6 of the row's total mass in the worst case, ~1e-9 typical).
+// CLEAN rows skip the candidate test (junk lanes have keys beyond the last
+// bucket); CLAMP rows file every d > dmax at dmax (e < e^-40 there).  Returns
+// this thread's candidate count (non-CLEAN rows).
+template <bool SCALE, bool CLAMP, bool CLEAN, bool CNT>
+__device__ __forceinline__ int hist_pass(Ctx &c, float inv_w, float w, float dmax) {
     Vars *v = c.v;
     const int nslots = v->nslots;
     const float mx = v->mx, thr = v->thr;
     const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    uint32_t *hc = reinterpret_cast<uint32_t *>(c.scr);
-    uint32_t *hsh = hc - MAGIC_I;
+    uint32_t *hsh = reinterpret_cast<uint32_t *>(c.scr) - MAGIC_I;
     const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
     const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
+    const float2 nmg2 = make_float2(-MAGIC, -MAGIC), nw2 = make_float2(-w, -w);
     const float2 mx2 = make_float2(mx, mx);
+    // 2^16 exp(-t) = 2^16 - 2^16 t + 2^15 t^2 - (2^16/6) t^3, rounded to an
+    // integer by the bias 2^23 (bits 0x4B000000 + G)
+    const float2 c3 = make_float2(-0x1p16f / 6.0f, -0x1p16f / 6.0f);
+    const float2 c2 = make_float2(0x1p15f, 0x1p15f), c1 = make_float2(-0x1p16f, -0x1p16f);
+    const float2 g0 = make_float2(0x1p23f + 0x1p16f, 0x1p23f + 0x1p16f);
     const int KT = MAGIC_I + NB - 1;
-    int tail = 0;
-    for (int s = threadIdx.x; s < nslots; s += NT) {
-        const float4 x = r4[s];
-        float2 a = make_float2(x.x, x.y), b = make_float2(x.z, x.w);
-        if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
-        float2 ka, kb;
-        if (CLEAN) {
-            ka = __ffma2_rn(__fadd2_rn(mx2, make_float2(-a.x, -a.y)), iw2, mg2);
-            kb = __ffma2_rn(__fadd2_rn(mx2, make_float2(-b.x, -b.y)), iw2, mg2);
-        } else {
-            ka = kf_pair<CLAMP>(d_pair(a, mx, thr), iw2, mg2, dmax);
-            kb = kf_pair<CLAMP>(d_pair(b, mx, thr), iw2, mg2, dmax);
-        }
-        const int kk[4] = {__float_as_int(ka.x), __float_as_int(ka.y), __float_as_int(kb.x),
-                           __float_as_int(kb.y)};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            if (kk[q] > KT) continue;  // non-candidate or junk lane
-            if (CLAMP && kk[q] == KT) ++tail;
-            else atomicAdd(&hsh[kk[q]], 1u);
-        }
-    }
-    if (CLAMP && tail) atomicAdd(&hc[NB - 1], (unsigned)tail);
-}
-
-// 1 when kf < t, else 0, as sat(kf * -2^100 + t * 2^100) (FMA pipe; kf and t
-// are integers + MAGIC, so the product difference is exact); ts = t * 2^100.
-__device__ __forceinline__ float step_lt(float kf, float ts) {
-    float r;
-    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(kf), "f"(-0x1p100f), "f"(ts));
-    return r;
-}
-
-// Pass 2 of the sorted path: exp and its fp64 sum, per window the e-mass of
-// the candidates above it (key < lo_t), and a membership bit per element of
-// the union of the windows.  Two 16-byte slots per thread and
-// trip; fp32 partial sums (16 values per lane and component) go to fp64 every
-// 4 trips.
-template <bool SCALE, bool CLAMP, bool CLEAN, int NTG>
-__device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, const float *tl,
-                                              const float *th, double *mass, double &S) {
-    Vars *v = c.v;
-    const int nslots = v->nslots;
-    const float mx = v->mx, thr = v->thr;
-    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
-    const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
-    const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
-    const float2 mx2 = make_float2(mx, mx);
-    const int lane = threadIdx.x & 31;
-    float tls[NTG > 0 ? NTG : 1], ths[NTG > 0 ? NTG : 1];
-#pragma unroll
-    for (int t = 0; t < NTG; ++t) { tls[t] = tl[t] * 0x1p100f; ths[t] = th[t] * 0x1p100f; }
-    double acc = 0.0;
-    double dm[NTG];
-    float2 fm[NTG];
-#pragma unroll
-    for (int t = 0; t < NTG; ++t) { dm[t] = 0.0; fm[t] = make_float2(0.f, 0.f); }
-    float2 fs = make_float2(0.f, 0.f);
-    // d = max - l of a pair (DNC for non-candidates unless CLEAN)
+    int ncand = 0;
     auto dpair = [&](float2 l) -> float2 {
         if (SCALE) l = __fmul2_rn(l, it2);
         if (CLEAN) return __fadd2_rn(mx2, make_float2(-l.x, -l.y));
-        return d_pair(l, mx, thr);
+        float2 d = d_pair(l, mx, thr);
+        if (CLAMP)
+            d = make_float2(d.x == DNC ? DNC : fminf(d.x, dmax), d.y == DNC ? DNC : fminf(d.y, dmax));
+        return d;
     };
-    auto kpair = [&](float2 d) -> float2 {
-        if (CLEAN) return __ffma2_rn(d, iw2, mg2);
-        return kf_pair<CLAMP>(d, iw2, mg2, dmax);
-    };
-    // e = exp(-d): the exp_pair arithmetic on x = -d with the sign folded in
-    auto epair = [&](float2 d) -> float2 {
-        const float2 nL1 = make_float2(-1.4426950216293335f, -1.4426950216293335f);
-        const float2 nL2 = make_float2(-1.925963033500011e-08f, -1.925963033500011e-08f);
-        const float2 LN2 = make_float2(0.6931471824645996f, 0.6931471824645996f);
-        const float2 y = __fmul2_rn(d, nL1);
-        float2 cc = __ffma2_rn(d, nL1, make_float2(-y.x, -y.y));
-        cc = __ffma2_rn(d, nL2, cc);
-        const float2 e = make_float2(ex2_approx(y.x), ex2_approx(y.y));
-        return __ffma2_rn(__fmul2_rn(e, cc), LN2, e);
-    };
-    // one slot: sums, masses above each window, membership count of the slot
-    auto slot = [&](float4 x, float (&inb)[4]) {
+    for (int s = threadIdx.x; s < nslots; s += NT) {
+        const float4 x = r4[s];
         const float2 da = dpair(make_float2(x.x, x.y)), db = dpair(make_float2(x.z, x.w));
-        const float2 ea = epair(da), eb = epair(db);
-        const float2 ka = kpair(da), kb = kpair(db);
-        fs = __fadd2_rn(fs, ea);
-        fs = __fadd2_rn(fs, eb);
+        const float2 ka = __ffma2_rn(da, iw2, mg2), kb = __ffma2_rn(db, iw2, mg2);
+        const float2 ta = __ffma2_rn(__fadd2_rn(ka, nmg2), nw2, da);
+        const float2 tb = __ffma2_rn(__fadd2_rn(kb, nmg2), nw2, db);
+        const float2 ga = __ffma2_rn(ta, __ffma2_rn(ta, __ffma2_rn(ta, c3, c2), c1), g0);
+        const float2 gb = __ffma2_rn(tb, __ffma2_rn(tb, __ffma2_rn(tb, c3, c2), c1), g0);
+        const int kk[4] = {__float_as_int(ka.x), __float_as_int(ka.y), __float_as_int(kb.x),
+                           __float_as_int(kb.y)};
+        const uint32_t gg[4] = {__float_as_uint(ga.x), __float_as_uint(ga.y), __float_as_uint(gb.x),
+                                __float_as_uint(gb.y)};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) inb[q] = 0.f;
-#pragma unroll
-        for (int t = 0; t < NTG; ++t) {
-            const float2 ua = make_float2(step_lt(ka.x, tls[t]), step_lt(ka.y, tls[t]));
-            const float2 ub = make_float2(step_lt(kb.x, tls[t]), step_lt(kb.y, tls[t]));
-            fm[t] = __ffma2_rn(ea, ua, fm[t]);
-            fm[t] = __ffma2_rn(eb, ub, fm[t]);
-            inb[0] += step_lt(ka.x, ths[t]) - ua.x;
-            inb[1] += step_lt(ka.y, ths[t]) - ua.y;
-            inb[2] += step_lt(kb.x, ths[t]) - ub.x;
-            inb[3] += step_lt(kb.y, ths[t]) - ub.y;
+        for (int q = 0; q < 4; ++q) {
+            if (kk[q] > KT) continue;  // non-candidate or junk lane
+            atomicAdd(&hsh[kk[q]], gg[q] & 0x7fffffu);
+            if (CNT) atomicAdd(&hsh[kk[q] + NB], 1u);
+            if (!CLEAN) ++ncand;
         }
+    }
+    return ncand;
+}
+
+// Pass 2 of the sorted path: one membership bit per element of the union of
+// the windows, each a range of d given as float bits [lo_t, lo_t + span_t]
+// (d >= 0, so its bits order like its value), and per window the count of
+// candidates above it (d below the range).  Two 16-byte slots per thread and
+// trip (slot 0 lanes 0-3, slot 1 lanes 4-7 of the trip's byte), a 32-bit word
+// every 4 trips to the thread's column of the mask area (the dead
+// histogram); the elements are gathered after the pass.  No branch or store
+// per element.
+template <bool SCALE, bool CLAMP, bool CLEAN, int NR>
+__device__ __forceinline__ void member_pass(Ctx &c, float dmax, const uint32_t *wlo,
+                                            const uint32_t *wsp, int *above) {
+    Vars *v = c.v;
+    const int nslots = v->nslots;
+    const float mx = v->mx, thr = v->thr;
+    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
+    const float2 it2 = make_float2(v->inv_temp, v->inv_temp);
+    const float2 mx2 = make_float2(mx, mx);
+    const int lane = threadIdx.x & 31;
+    uint32_t lo[NR], sp[NR];
+    int cnt[NR];
+#pragma unroll
+    for (int t = 0; t < NR; ++t) { lo[t] = wlo[t]; sp[t] = wsp[t]; cnt[t] = 0; }
+    auto dpair = [&](float2 l) -> float2 {
+        if (SCALE) l = __fmul2_rn(l, it2);
+        if (CLEAN) return __fadd2_rn(mx2, make_float2(-l.x, -l.y));
+        float2 d = d_pair(l, mx, thr);
+        if (CLAMP)
+            d = make_float2(d.x == DNC ? DNC : fminf(d.x, dmax), d.y == DNC ? DNC : fminf(d.y, dmax));
+        return d;
     };
-    // Window membership: one bit per element, 8 per trip (slot 0 lanes 0-3,
-    // slot 1 lanes 4-7), a 32-bit word every 4 trips to the thread's column
-    // of the mask area (the dead histogram); the elements are gathered after
-    // the pass.  No branch or store per element.
+    auto inw = [&](float d) -> uint32_t {
+        const uint32_t k = __float_as_uint(d);
+        bool in = false;
+#pragma unroll
+        for (int t = 0; t < NR; ++t) {
+            const uint32_t u = k - lo[t];
+            in |= u <= sp[t];
+            cnt[t] += (int)(u >> 31);  // d below the window's range
+        }
+        return in ? 1u : 0u;
+    };
     uint32_t *mw = reinterpret_cast<uint32_t *>(c.scr);
     uint32_t bits = 0;
+    // out-of-range slots: d = +inf-like (never in a window, never counted)
     const float ov_ = CLEAN ? JUNK : __int_as_float(0x7fc00000);
     const float4 OUT = make_float4(ov_, ov_, ov_, ov_);
     int iter = 0;
@@ -1789,43 +1816,20 @@ __device__ __forceinline__ void combined_pass(Ctx &c, float inv_w, float dmax, c
         const int s0 = base + lane, s1 = base + NT + lane;
         const float4 x0 = (s0 < nslots) ? r4[s0] : OUT;
         const float4 x1 = (s1 < nslots) ? r4[s1] : OUT;
-        float in0[4], in1[4];
-        slot(x0, in0);
-        slot(x1, in1);
-        uint32_t tb = 0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            tb |= (in0[q] > 0.5f ? 1u : 0u) << q;
-            tb |= (in1[q] > 0.5f ? 1u : 0u) << (4 + q);
-        }
+        const float2 a0 = dpair(make_float2(x0.x, x0.y)), b0 = dpair(make_float2(x0.z, x0.w));
+        const float2 a1 = dpair(make_float2(x1.x, x1.y)), b1 = dpair(make_float2(x1.z, x1.w));
+        const uint32_t tb = inw(a0.x) | (inw(a0.y) << 1) | (inw(b0.x) << 2) | (inw(b0.y) << 3) |
+                            (inw(a1.x) << 4) | (inw(a1.y) << 5) | (inw(b1.x) << 6) |
+                            (inw(b1.y) << 7);
         bits |= tb << (8 * (iter & 3));
         if ((iter & 3) == 3) {
             mw[(iter >> 2) * NT + threadIdx.x] = bits;
             bits = 0;
-            acc += (double)(fs.x + fs.y);
-            fs = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int t = 0; t < NTG; ++t) {
-                dm[t] += (double)(fm[t].x + fm[t].y);
-                fm[t] = make_float2(0.f, 0.f);
-            }
         }
     }
     if (iter & 3) mw[(iter >> 2) * NT + threadIdx.x] = bits;
-    acc += (double)(fs.x + fs.y);
 #pragma unroll
-    for (int t = 0; t < NTG; ++t) dm[t] += (double)(fm[t].x + fm[t].y);
-    double m0 = NTG > 0 ? dm[0] : 0.0, m1 = NTG > 1 ? dm[1] : 0.0;
-    int z0 = 0, z1 = 0;
-    block_sum4(acc, m0, z0, z1, c.red);
-    S = acc;
-    if (NTG > 0) mass[0] = m0;
-    if (NTG > 1) {
-        double m2 = NTG > 2 ? dm[2] : 0.0;
-        block_sum4(m1, m2, z0, z1, c.red);
-        mass[1] = m1;
-        if (NTG > 2) mass[2] = m2;
-    }
+    for (int t = 0; t < NR; ++t) above[t] = cnt[t];
 }
 
 // exp pass of the id-order path: e stored in place (-0 for non-candidates),
@@ -1858,43 +1862,48 @@ __device__ __forceinline__ double exp_store_pass(Ctx &c) {
     return block_sum_d(S, c.red);
 }
 
-// Window list entries after the exact pass, self-contained 64-bit keys:
+// Window list entries after the membership pass, self-contained 64-bit keys:
 //   bits 63..32  ~bits(p)        (probability descending)
-//   bits 31..15  id              (then id ascending: the stable sort's order)
-//   bits 12..2   bucket of d = max - l
-//   bits  1..0   edge + 1        (edge: -1 / +1 within rounding of the lower /
-//                                 upper bucket edge, else 0)
-static_assert(NB == 2048, "list keys hold an 11-bit bucket");
-__device__ __forceinline__ unsigned long long list_key(float p, int id, int bkt, int edge) {
-    return ((unsigned long long)(~__float_as_uint(p)) << 32) |
-           (((unsigned)id << 15) | ((unsigned)bkt << 2) | (unsigned)(edge + 1));
+//   bits 31..16  id              (then id ascending: the stable sort's order)
+//   bits  8..0   per target t (0 cut, 1 top_k, 2 draw), bits 3t..3t+2:
+//                in the target's d range / in its band above the target's
+//                buckets / in its band below them
+__device__ __forceinline__ unsigned long long list_key(float p, int id, uint32_t flags) {
+    return ((unsigned long long)(~__float_as_uint(p)) << 32) | (((unsigned)id << 16) | flags);
 }
-__device__ __forceinline__ int lk_id(unsigned long long k) { return (int)((unsigned)k >> 15); }
-__device__ __forceinline__ int lk_bkt(unsigned long long k) {
-    return (int)(((unsigned)k >> 2) & 2047u);
-}
-__device__ __forceinline__ int lk_edge(unsigned long long k) { return (int)((unsigned)k & 3u) - 1; }
+__device__ __forceinline__ int lk_id(unsigned long long k) { return (int)((unsigned)k >> 16); }
 
-// Exclusive block scan of three doubles and three ints (scratch `wd`, `wi`:
-// 3 * NW each).
-__device__ __forceinline__ void block_xscan3(double (&m)[3], int (&n)[3], double *wd, int *wi) {
+// Exclusive block scan of three doubles m and three ints n, and block sums of
+// three doubles a (in place; scratch `wd`: 6 * NW doubles, `wi`: 3 * NW ints).
+__device__ __forceinline__ void block_xscan3a(double (&m)[3], int (&n)[3], double (&a)[3],
+                                              double *wd, int *wi) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    double im[3];
+    double im[3], sa[3];
     int in[3];
 #pragma unroll
-    for (int t = 0; t < 3; ++t) { im[t] = warp_iscan(m[t], lane); in[t] = warp_iscan(n[t], lane); }
+    for (int t = 0; t < 3; ++t) {
+        im[t] = warp_iscan(m[t], lane);
+        in[t] = warp_iscan(n[t], lane);
+        sa[t] = warp_sum(a[t]);
+    }
     if (lane == 31) {
 #pragma unroll
-        for (int t = 0; t < 3; ++t) { wd[3 * warp + t] = im[t]; wi[3 * warp + t] = in[t]; }
+        for (int t = 0; t < 3; ++t) {
+            wd[3 * warp + t] = im[t]; wi[3 * warp + t] = in[t]; wd[3 * NW + 3 * warp + t] = sa[t];
+        }
     }
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < 3; ++t) {
-        double bm = 0.0;
+        double bm = 0.0, ba = 0.0;
         int bn = 0;
-        for (int w = 0; w < warp; ++w) { bm += wd[3 * w + t]; bn += wi[3 * w + t]; }
+        for (int w = 0; w < NW; ++w) {
+            if (w < warp) { bm += wd[3 * w + t]; bn += wi[3 * w + t]; }
+            ba += wd[3 * NW + 3 * w + t];
+        }
         m[t] = bm + (im[t] - m[t]);
         n[t] = bn + (in[t] - n[t]);
+        a[t] = ba;
     }
     __syncthreads();
 }
@@ -1912,14 +1921,14 @@ struct Cand {
 };
 
 // The first entry of this thread's run [j0, j1) of the sorted list that lies
-// in window [lo, hi] and where the running mass from m0 crosses T (GE / GT)
-// or whose position from cnt0 equals m (POS); (pre_m, pre_n) is the window's
-// exclusive prefix in front of the run.  j = INT_MAX when none.  Runs of two
-// threads can both claim a crossing within fp64 rounding of T: the lowest
-// list index wins (run_publish).
-__device__ __forceinline__ Cand run_find(const unsigned long long *list, int j0, int j1, int lo,
-                                         int hi, double m0, int cnt0, double pre_m, int pre_n,
-                                         int mode, double T, int m) {
+// in target t's d range and where the running mass from m0 crosses T (GE /
+// GT) or whose position from cnt0 equals m (POS); (pre_m, pre_n) is the
+// range's exclusive prefix in front of the run.  j = INT_MAX when none.  Runs
+// of two threads can both claim a crossing within fp64 rounding of T: the
+// lowest list index wins (run_publish).
+__device__ __forceinline__ Cand run_find(const unsigned long long *list, int j0, int j1, int t,
+                                         double m0, int cnt0, double pre_m, int pre_n, int mode,
+                                         double T, int m) {
     Cand r;
     r.j = INT_MAX;
     r.pos = 0;
@@ -1928,8 +1937,7 @@ __device__ __forceinline__ Cand run_find(const unsigned long long *list, int j0,
     int pos = cnt0 + pre_n;
     for (int j = j0; j < j1; ++j) {
         const unsigned long long k = list[j];
-        const int b = lk_bkt(k);
-        if (b < lo || b > hi) continue;
+        if (!(((uint32_t)k >> (3 * t)) & 1u)) continue;
         const double prev = cs;
         cs += (double)key_p(k);
         const bool hit = (mode == T_MASS_GE) ? ((pos == 0 || prev < T) && cs >= T)
@@ -1942,14 +1950,14 @@ __device__ __forceinline__ Cand run_find(const unsigned long long *list, int j0,
 }
 
 __device__ __forceinline__ void run_publish(const unsigned long long *list, int nl, const Cand &h,
-                                            int lo, int hi, Hit *out) {
+                                            int t, Hit *out) {
     const unsigned long long k = list[h.j];
-    const int j = h.j, b = lk_bkt(k), e = lk_edge(k);
+    const int j = h.j;
     const float p = key_p(k);
     const bool tie = (j > 0 && key_p(list[j - 1]) == p) || (j + 1 < nl && key_p(list[j + 1]) == p);
-    // an element within rounding of the window's outer edges can share its
-    // probability with one across the edge
-    const bool outer = (b == lo && e < 0) || (b == hi && e > 0);
+    // a crossing in the band outside the target's buckets: the estimate
+    // missed; the exact fallback decides
+    const bool outer = (((uint32_t)k >> (3 * t)) & 6u) != 0;
     out->cs = h.cs;
     out->p = p;
     out->id = lk_id(k);
@@ -2011,7 +2019,8 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     if (!(dmax > 1e-30f)) dmax = 1.0f;
     const float inv_w = __fdiv_rn((float)NB - 1.5f, dmax);
     const float w = __fdiv_rn(1.0f, inv_w);
-    for (int i = threadIdx.x; i < NB; i += NT) hc[i] = 0;
+    const bool cntv = top_k > 0;  // bucket counts needed (the top_k position)
+    for (int i = threadIdx.x; i < (cntv ? 2 : 1) * NB; i += NT) hc[i] = 0;
     if (threadIdx.x == 0) v->ln0 = 0;
     __syncthreads();
     // CLEAN variants only without clamping (junk lanes must stay beyond the
@@ -2032,29 +2041,44 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         }
         __syncthreads();
     }
-    if (clamp) hist_pass<SCALE, true, false>(c, inv_w, dmax);
-    else if (clean) hist_pass<SCALE, false, true>(c, inv_w, dmax);
-    else hist_pass<SCALE, false, false>(c, inv_w, dmax);
+    int my_nc;
+    if (clamp) {
+        my_nc = cntv ? hist_pass<SCALE, true, false, true>(c, inv_w, w, dmax)
+                     : hist_pass<SCALE, true, false, false>(c, inv_w, w, dmax);
+    } else if (clean) {
+        my_nc = cntv ? hist_pass<SCALE, false, true, true>(c, inv_w, w, dmax)
+                     : hist_pass<SCALE, false, true, false>(c, inv_w, w, dmax);
+    } else {
+        my_nc = cntv ? hist_pass<SCALE, false, false, true>(c, inv_w, w, dmax)
+                     : hist_pass<SCALE, false, false, false>(c, inv_w, w, dmax);
+    }
     __syncthreads();
-    // bucket scan: counts exactly, masses estimated from bucket centres
+    // bucket scan: e-masses (and counts when cntv)
     const int bb = BPT * threadIdx.x;
     int cb[BPT];
     double mb[BPT];
     int csum = 0;
     double msum = 0.0;
+    {
+        double E = exp(-(double)bb * (double)w) * 0x1p-16;  // E_b of the first bucket, scaled
+        const double qd = exp(-(double)w);
 #pragma unroll
-    for (int q = 0; q < BPT; ++q) {
-        cb[q] = (int)hc[bb + q];
-        mb[q] = (double)cb[q] * (double)exp_one(-(float)(bb + q) * w);
-        csum += cb[q];
-        msum += mb[q];
+        for (int q = 0; q < BPT; ++q) {
+            cb[q] = cntv ? (int)hc[NB + bb + q] : 0;
+            mb[q] = E * (double)hc[bb + q];
+            E *= qd;
+            csum += cb[q];
+            msum += mb[q];
+        }
     }
     double mt;
-    const double mex = block_xscan_d(msum, mt, c.red);
     int ncand;
-    const int cex = block_xscan_i(csum, ncand, c.red);
+    double mex = msum;
+    int cex = cntv ? csum : my_nc;
+    block_xscan_di(mex, cex, mt, ncand, c.red);
+    if (clean && !cntv) ncand = c.V;  // every logit finite and a candidate
     if (threadIdx.x == 0) {
-        v->n_cand = ncand; v->bc = NB; v->bk = NB; v->bd0 = NB; v->wd_lo = NB; v->wd_hi = NB;
+        v->n_cand = ncand; v->bc = NB; v->bc_hi = NB; v->bk = NB; v->bd0 = NB; v->bd_hi = NB;
     }
     if (ncand == 0) {  // argmax guard (src/model.c:296-303)
         release_row(c);
@@ -2123,157 +2147,168 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
 
     // ---- sorted order: nucleus cut, top_k truncation, draw -----------------
-    // Windows: the bucket each target falls in by the estimate.  Exact masses
-    // above each window come from the combined pass (inv_sum * e-mass: within
-    // ~1e-10 of the reference's sums of rounded probabilities), exact counts
-    // from the histogram; the walks inside a window use exact probabilities.
+    // Windows: the buckets each target can fall in, from the exact bucket
+    // masses (normalised by the reference's inv_sum they are within 8e-6 of
+    // the reference's cumulative sums of rounded probabilities, hence the EPS
+    // margins) and counts (top_k).  Each window becomes a range of d with a
+    // band of 1.2e-6 (+5e-7 relative) beyond its bucket edges: two candidates
+    // with one probability lie within 5e-7 of each other in d, so every
+    // candidate tied with one inside the buckets is inside the range.  The
+    // walks run over each range's elements in exact (p desc, id asc) order
+    // from the mass and count of the candidates below the range's d.
     const bool want_cut = top_p < 1.0f;
     const bool want_k = top_k > 0 && top_k < ncand;
+    const double S = mt;
+    const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
+    const double ip = (double)inv_sum;
+    constexpr double EPS = 8e-6;
+    int lastb = -1;  // last non-empty bucket
     {
-        const double fr_c = (double)top_p * mt;  // estimated e-mass fractions
+        const double tlo = fmax((double)top_p - EPS, 0.0), thi = (double)top_p + EPS;
         double run = mex;
         int crun = cex;
 #pragma unroll
         for (int q = 0; q < BPT; ++q) {
             const double nxt = run + mb[q];
-            if (want_cut && cb[q] > 0 && run < fr_c && nxt >= fr_c) {
-                v->bc = bb + q; v->cc = crun; v->mc = (fr_c - run) / mb[q];
-                v->ec = nxt / mt;  // the cut's mass lies in [top_p, ec]
-            }
-            if (want_k && top_k - 1 >= crun && top_k - 1 < crun + cb[q]) {
-                v->bk = bb + q; v->ck = crun;
-                v->ek = (run + (double)(top_k - crun) * (mb[q] / (double)cb[q])) / mt;
-                v->mk = run / mt;    // the top_k mass lies in [mk, aux0]
-                v->aux0 = nxt / mt;
+            if (mb[q] > 0.0) {
+                const int b = bb + q;
+                const double pr = run * ip, pn = nxt * ip;
+                lastb = b;
+                if (want_cut && (pr < tlo || pr == 0.0) && pn >= tlo) { v->bc = b; v->mc = run; }
+                if (want_cut && pr < thi && pn >= thi) { v->bc_hi = b; v->ec = pn; }
+                if (want_k && top_k - 1 >= crun && top_k - 1 < crun + cb[q]) {
+                    v->bk = b; v->mk = run; v->aux0 = pr; v->ek = pn;
+                }
             }
             run = nxt;
             crun += cb[q];
         }
     }
-    __syncthreads();
-    {
-        // predicted new_sum: the reference stops at the first cumulative
-        // probability >= top_p, i.e. within one probability of top_p; the
-        // top_k estimate interpolates inside its bucket
-        double ns = want_cut ? (double)top_p : 1.0;
-        if (want_k && v->bk < NB) ns = fmin(ns, v->ek);
-        const double fr_d = (double)v->u * ns * mt;
-        // the range new_sum can take, for a wide window over sparse buckets
-        // (few candidates: the cut's element can carry much of the mass)
-        double lo = want_cut ? (double)top_p : 1.0, hi = (want_cut && v->bc < NB) ? v->ec : 1.0;
-        if (want_k && v->bk < NB) { lo = fmin(lo, v->mk); hi = fmin(hi, v->aux0); }
-        const double fr_lo = (double)v->u * lo * mt * (1.0 - 1e-3);
-        const double fr_hi = (double)v->u * fmin(hi * (1.0 + 1e-3), 1.0 - 1e-9) * mt;
-        double run = mex;
-        int crun = cex;
-#pragma unroll
-        for (int q = 0; q < BPT; ++q) {
-            const double nxt = run + mb[q];
-            if (cb[q] > 0 && run <= fr_d && nxt > fr_d) {
-                v->bd0 = bb + q; v->cd = crun; v->md = (fr_d - run) / mb[q];
-            }
-            if (run <= fr_lo && nxt > fr_lo) { v->wd_lo = bb + q; v->wd_lo_c = crun; }
-            if (run <= fr_hi && nxt > fr_hi) { v->wd_hi = bb + q; v->wd_hi_c = crun + cb[q]; }
-            run = nxt;
-            crun += cb[q];
-        }
-    }
-    __syncthreads();
+    lastb = block_max_i(lastb, c.red);  // (its barriers publish the stores above)
     if (threadIdx.x == 0) {
-        // mass targets get a two-bucket window: the estimated bucket and the
-        // neighbour on the side of the estimated position
-        v->bc_hi = v->bc;
-        if (want_cut && v->bc < NB) {
-            if (v->mc < 0.5 && v->bc > 0) { v->cc -= (int)hc[v->bc - 1]; v->bc -= 1; }
-            else v->bc_hi = min(v->bc + 1, NB - 1);
-        }
-        v->bd_hi = v->bd0;
-        if (v->bd0 < NB) {
-            if (v->md < 0.5 && v->bd0 > 0) { v->cd -= (int)hc[v->bd0 - 1]; v->bd0 -= 1; }
-            else v->bd_hi = min(v->bd0 + 1, NB - 1);
-            // sparse buckets: the window spans the draw's whole range, one
-            // bucket of margin each side, while it holds few elements
-            const int w0 = v->wd_lo, w1 = v->wd_hi;
-            if (w0 < NB && w1 < NB && w0 <= v->bd0 && w1 >= v->bd_hi) {
-                const int a = max(w0 - 1, 0), b = min(w1 + 1, NB - 1);
-                const int ca = v->wd_lo_c - (a < w0 ? (int)hc[a] : 0);
-                const int cb_ = v->wd_hi_c + (b > w1 ? (int)hc[b] : 0);
-                if (cb_ - ca <= WIDE_CAP) { v->bd0 = a; v->bd_hi = b; v->cd = ca; }
+        v->inv_sum = inv_sum;
+        v->S = S;
+        const double tot = S * ip;
+        if (want_cut && v->bc < NB && v->bc_hi == NB) { v->bc_hi = lastb; v->ec = tot; }
+        // range of new_sum (the cumulative mass where the walk stops), then of
+        // r = u * (float)new_sum
+        double lo = tot, hi = tot;
+        if (want_cut && v->bc < NB) { lo = (double)top_p; hi = v->ec; }
+        if (want_k && v->bk < NB) { lo = fmin(lo, v->aux0); hi = fmin(hi, v->ek); }
+        v->rlo = fmax((double)v->u * lo * (1.0 - 1e-6) - EPS, 0.0);
+        v->rhi = (double)v->u * hi * (1.0 + 1e-6) + EPS;
+    }
+    __syncthreads();
+    {
+        const double rlo = v->rlo, rhi = v->rhi;
+        double run = mex;
+#pragma unroll
+        for (int q = 0; q < BPT; ++q) {
+            const double nxt = run + mb[q];
+            if (mb[q] > 0.0) {
+                const double pr = run * ip, pn = nxt * ip;
+                if (pr <= rlo && pn > rlo) { v->bd0 = bb + q; v->md = run; }
+                if (pr <= rhi && pn > rhi) v->bd_hi = bb + q;
             }
+            run = nxt;
         }
     }
+    __syncthreads();
+    if (threadIdx.x == 0 && v->bd0 < NB && v->bd_hi == NB) v->bd_hi = lastb;
     __syncthreads();
     const int bc = want_cut ? v->bc : NB, bk = want_k ? v->bk : NB, bd = v->bd0;
-    const int bc1 = v->bc_hi, bd1 = v->bd_hi;
-    // distinct active windows first: slot_* = index of the target's window
-    // (straight-line code: the small arrays stay in registers)
-    float tl[3] = {MAGIC, MAGIC, MAGIC}, th[3] = {MAGIC, MAGIC, MAGIC};
-    int ntg = 0, slot_c = -1, slot_k = -1, slot_d = -1;
-    auto add_window = [&](int lo_b, int hi_b) -> int {
-        const float lo = MAGIC + (float)lo_b, hi = MAGIC + (float)(hi_b + 1);
-        if (ntg > 0 && tl[0] == lo && th[0] == hi) return 0;
-        if (ntg > 1 && tl[1] == lo && th[1] == hi) return 1;
-        if (ntg == 0) { tl[0] = lo; th[0] = hi; }
-        else if (ntg == 1) { tl[1] = lo; th[1] = hi; }
-        else { tl[2] = lo; th[2] = hi; }
-        return ntg++;
-    };
-    if (bc < NB) slot_c = add_window(bc, bc1);
-    if (bk < NB) slot_k = add_window(bk, bk);
-    if (bd < NB) slot_d = add_window(bd, bd1);
-    double mass[3] = {0.0, 0.0, 0.0};
-    double S = 0.0;
-    if (clamp) {
-        if (ntg <= 1) combined_pass<SCALE, true, false, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, true, false, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, true, false, 3>(c, inv_w, dmax, tl, th, mass, S);
-    } else if (clean) {
-        if (ntg <= 1) combined_pass<SCALE, false, true, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, false, true, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, false, true, 3>(c, inv_w, dmax, tl, th, mass, S);
-    } else {
-        if (ntg <= 1) combined_pass<SCALE, false, false, 1>(c, inv_w, dmax, tl, th, mass, S);
-        else if (ntg == 2) combined_pass<SCALE, false, false, 2>(c, inv_w, dmax, tl, th, mass, S);
-        else combined_pass<SCALE, false, false, 3>(c, inv_w, dmax, tl, th, mass, S);
+    const int tlo_b[3] = {bc, bk, bd}, thi_b[3] = {v->bc_hi, bk, v->bd_hi};
+    // d ranges of the targets (float bits; inactive: empty)
+    uint32_t ta[3], tsp[3];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        ta[t] = 0xffffffffu;
+        tsp[t] = 0u;
+        if (tlo_b[t] < NB) {
+            const double dl = ((double)tlo_b[t] - 0.5) / (double)inv_w;
+            const double dh = ((double)thi_b[t] + 0.5) / (double)inv_w;
+            const uint32_t a = (tlo_b[t] == 0) ? 0u
+                                               : __float_as_uint(fmaxf(0.0f, __double2float_rd(
+                                                     dl * (1.0 - 5e-7) - 1.2e-6)));
+            const uint32_t b = (thi_b[t] >= NB - 1)
+                                   ? __float_as_uint(DNC) - 1u
+                                   : min(__float_as_uint(__double2float_ru(dh * (1.0 + 5e-7) + 1.2e-6)),
+                                         __float_as_uint(DNC) - 1u);
+            ta[t] = a;
+            tsp[t] = b - a;
+        }
     }
-    auto mass_of = [&](int sl) {
-        return sl == 0 ? mass[0] : sl == 1 ? mass[1] : sl == 2 ? mass[2] : 0.0;
-    };
-    const double mass_c = mass_of(slot_c), mass_k = mass_of(slot_k), mass_d = mass_of(slot_d);
-    const float inv_sum = __fdiv_rn(1.0f, __double2float_rn(S));  // src/model.c:311
-    if (threadIdx.x == 0) { v->inv_sum = inv_sum; v->S = S; }
-    // exact probability, bucket and edge flag of a listed element as its key
+    // distinct ranges for the pass; rng[t] = the range of target t
+    uint32_t wl[3] = {0u, 0u, 0u}, ws[3] = {0u, 0u, 0u};
+    int rng[3] = {-1, -1, -1};
+    int ntg = 0;
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        if (tlo_b[t] >= NB) continue;
+        int f = -1;
+        if (ntg > 0 && wl[0] == ta[t] && ws[0] == tsp[t]) f = 0;
+        else if (ntg > 1 && wl[1] == ta[t] && ws[1] == tsp[t]) f = 1;
+        if (f < 0) {
+            if (ntg == 0) { wl[0] = ta[t]; ws[0] = tsp[t]; }
+            else if (ntg == 1) { wl[1] = ta[t]; ws[1] = tsp[t]; }
+            else { wl[2] = ta[t]; ws[2] = tsp[t]; }
+            f = ntg++;
+        }
+        rng[t] = f;
+    }
+    int abv[3] = {0, 0, 0};
+    if (clamp) {
+        if (ntg == 1) member_pass<SCALE, true, false, 1>(c, dmax, wl, ws, abv);
+        else if (ntg == 2) member_pass<SCALE, true, false, 2>(c, dmax, wl, ws, abv);
+        else if (ntg == 3) member_pass<SCALE, true, false, 3>(c, dmax, wl, ws, abv);
+    } else if (clean) {
+        if (ntg == 1) member_pass<SCALE, false, true, 1>(c, dmax, wl, ws, abv);
+        else if (ntg == 2) member_pass<SCALE, false, true, 2>(c, dmax, wl, ws, abv);
+        else if (ntg == 3) member_pass<SCALE, false, true, 3>(c, dmax, wl, ws, abv);
+    } else {
+        if (ntg == 1) member_pass<SCALE, false, false, 1>(c, dmax, wl, ws, abv);
+        else if (ntg == 2) member_pass<SCALE, false, false, 2>(c, dmax, wl, ws, abv);
+        else if (ntg == 3) member_pass<SCALE, false, false, 3>(c, dmax, wl, ws, abv);
+    }
+    // exact probability and window flags of a listed element as its key
     auto to_key = [&](int id, float l) -> unsigned long long {
         const float pe = __fmul_rn(exp_one(__fsub_rn(l, mx)), inv_sum);
         float d = __fsub_rn(mx, l);
         if (clamp) d = fminf(d, dmax);
-        const float kf = __fmaf_rn(d, inv_w, MAGIC);
-        const int bk_ = __float_as_int(kf) - MAGIC_I;
-        // within 2e-3 of a bucket edge, a logit a few ulps away (possibly the
-        // same probability) may sit in the neighbouring bucket
-        const float fr = __fmaf_rn(d, inv_w, -(float)bk_);
-        const int eg = (fr > 0.5f - 2e-3f) ? 1 : (fr < -(0.5f - 2e-3f)) ? -1 : 0;
-        return list_key(pe, id, bk_, eg);
+        const int kb = __float_as_int(__fmaf_rn(d, inv_w, MAGIC)) - MAGIC_I;
+        const uint32_t db = __float_as_uint(d);
+        uint32_t f = 0;
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            if (db - ta[t] <= tsp[t]) {
+                f |= 1u << (3 * t);
+                if (kb < tlo_b[t]) f |= 2u << (3 * t);
+                if (kb > thi_b[t]) f |= 4u << (3 * t);
+            }
+        }
+        return list_key(pe, id, f);
     };
-    // gather the window elements marked by the exact pass into keys: block
-    // scan of the per-thread bit counts, then every thread writes its own
+    // gather the window elements marked by the membership pass into keys:
+    // block scan of the per-thread bit counts, then every thread writes its own
     int tot;
     {
         const uint32_t *mw = reinterpret_cast<const uint32_t *>(c.scr);
         const int wbase = threadIdx.x & ~31, lane = threadIdx.x & 31;
         const int ntrips = (nslots - wbase + 2 * NT - 1) / (2 * NT);  // this warp's trips
-        uint32_t w[MASKW];
+        uint32_t wm[MASKW];
         int nb = 0;
 #pragma unroll
         for (int q = 0; q < MASKW; ++q) {
-            w[q] = (4 * q < ntrips) ? mw[q * NT + threadIdx.x] : 0u;
-            nb += __popc(w[q]);
+            wm[q] = (ntg > 0 && 4 * q < ntrips) ? mw[q * NT + threadIdx.x] : 0u;
+            nb += __popc(wm[q]);
         }
-        int j = block_xscan_i(nb, tot, c.red);  // (its barriers end the mask reads)
+        // the block scan of the bit counts also sums the per-range counts of
+        // candidates above the ranges
+        int j = block_xscan_i4(nb, abv, tot, c.red);  // (its barriers end the mask reads)
         const float it = v->inv_temp;
 #pragma unroll
         for (int q = 0; q < MASKW; ++q) {
-            uint32_t m = w[q];
+            uint32_t m = wm[q];
             while (m) {
                 const int bpos = __ffs(m) - 1;
                 m &= m - 1;
@@ -2302,39 +2337,51 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
     if (threadIdx.x < 3) { hits[threadIdx.x].flags = 0; hits[threadIdx.x].jmin = INT_MAX; }
 
-    const double ip = (double)inv_sum;
-    // per-thread runs of the sorted list and each window's prefix in front
+    // per-thread runs of the sorted list; per target the exclusive prefix in
+    // front of the run and the total mass of the band elements above the
+    // target's buckets
     const int RQ = (nl + NT - 1) / NT;
     const int j0 = list_ok ? min(nl, (int)threadIdx.x * RQ) : 0;
     const int j1 = list_ok ? min(nl, j0 + RQ) : 0;
-    const int wlo[3] = {bc, bk, bd}, whi[3] = {bc1, bk, bd1};
-    double pm[3] = {0.0, 0.0, 0.0};
+    double pm[3] = {0.0, 0.0, 0.0}, pa[3] = {0.0, 0.0, 0.0};
     int pn[3] = {0, 0, 0};
     for (int j = j0; j < j1; ++j) {
         const unsigned long long k = list[j];
-        const int b = lk_bkt(k);
+        const uint32_t f = (uint32_t)k;
         const double p = (double)key_p(k);
 #pragma unroll
-        for (int t = 0; t < 3; ++t)
-            if (b >= wlo[t] && b <= whi[t]) { pm[t] += p; ++pn[t]; }
+        for (int t = 0; t < 3; ++t) {
+            if ((f >> (3 * t)) & 1u) { pm[t] += p; ++pn[t]; }
+            if ((f >> (3 * t)) & 2u) pa[t] += p;
+        }
     }
-    block_xscan3(pm, pn, reinterpret_cast<double *>(c.scr + LISTCAP * 8),
-                 reinterpret_cast<int *>(c.scr + LISTCAP * 8 + 3 * NW * 8));
+    block_xscan3a(pm, pn, pa, reinterpret_cast<double *>(c.scr + LISTCAP * 8),
+                  reinterpret_cast<int *>(c.scr + LISTCAP * 8 + 6 * NW * 8));
+    // mass and count of the candidates below each target's d range
+    double m0[3];
+    int c0[3];
+    {
+        const double mh[3] = {v->mc, v->mk, v->md};
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            m0[t] = mh[t] * ip - pa[t];
+            c0[t] = (rng[t] == 0) ? abv[0] : (rng[t] == 1) ? abv[1] : (rng[t] == 2) ? abv[2] : 0;
+        }
+    }
 
     // nucleus cut and top_k position: the owners of the crossings publish them
-    const double m0c = mass_c * ip, m0k = mass_k * ip, m0d = mass_d * ip;
-    const bool try_c = want_cut && list_ok && bc < NB && !(m0c >= (double)top_p && v->cc > 0);
-    const bool try_k = want_k && list_ok && bk < NB && !(top_k - 1 < v->ck);
+    const bool try_c = want_cut && list_ok && bc < NB && !(m0[0] >= (double)top_p && c0[0] > 0);
+    const bool try_k = want_k && list_ok && bk < NB && !(top_k - 1 < c0[1]);
     Cand hc_ = {INT_MAX, 0, 0.0}, hk_ = {INT_MAX, 0, 0.0};
     if (try_c)
-        hc_ = run_find(list, j0, j1, bc, bc1, m0c, v->cc, pm[0], pn[0], T_MASS_GE, (double)top_p, 0);
+        hc_ = run_find(list, j0, j1, 0, m0[0], c0[0], pm[0], pn[0], T_MASS_GE, (double)top_p, 0);
     if (try_k)
-        hk_ = run_find(list, j0, j1, bk, bk, m0k, v->ck, pm[1], pn[1], T_POS, 0.0, top_k - 1);
+        hk_ = run_find(list, j0, j1, 1, m0[1], c0[1], pm[1], pn[1], T_POS, 0.0, top_k - 1);
     if (hc_.j != INT_MAX) atomicMin(&hits[0].jmin, hc_.j);
     if (hk_.j != INT_MAX) atomicMin(&hits[1].jmin, hk_.j);
     __syncthreads();
-    if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) run_publish(list, nl, hc_, bc, bc1, &hits[0]);
-    if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) run_publish(list, nl, hk_, bk, bk, &hits[1]);
+    if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) run_publish(list, nl, hc_, 0, &hits[0]);
+    if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) run_publish(list, nl, hk_, 1, &hits[1]);
     __syncthreads();
 
     int n = ncand;
@@ -2346,7 +2393,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     if (want_cut) {
         Sel cut;
         if (!(try_c && hit_sel(hits[0], cut))) {
-            if (bc < NB) pwin_of(bc - 4, bc1 + 4, w, inv_sum, pw_lo, pw_hi);
+            if (bc < NB) pwin_of(bc - 4, v->bc_hi + 4, w, inv_sum, pw_lo, pw_hi);
             cut = select_slow(c, SCALE, T_MASS_GE, (double)top_p, 0, pw_lo, pw_hi);
         }
         if (cut.found) {
@@ -2370,17 +2417,17 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     const float r = __fmul_rn(v->u, __double2float_rn(new_sum));
     Sel d;
     {
-        const bool try_d = list_ok && bd < NB && !(m0d > (double)r && v->cd > 0);
+        const bool try_d = list_ok && bd < NB && !(m0[2] > (double)r && c0[2] > 0);
         Cand hd_ = {INT_MAX, 0, 0.0};
         if (try_d)
-            hd_ = run_find(list, j0, j1, bd, bd1, m0d, v->cd, pm[2], pn[2], T_MASS_GT, (double)r, 0);
+            hd_ = run_find(list, j0, j1, 2, m0[2], c0[2], pm[2], pn[2], T_MASS_GT, (double)r, 0);
         if (hd_.j != INT_MAX) atomicMin(&hits[2].jmin, hd_.j);
         __syncthreads();
-        if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) run_publish(list, nl, hd_, bd, bd1, &hits[2]);
+        if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) run_publish(list, nl, hd_, 2, &hits[2]);
         __syncthreads();
         if (!(try_d && hit_sel(hits[2], d))) {
             pw_lo = 0.0f; pw_hi = PINF;
-            if (bd < NB) pwin_of(bd - 4, bd1 + 4, w, inv_sum, pw_lo, pw_hi);
+            if (bd < NB) pwin_of(bd - 4, v->bd_hi + 4, w, inv_sum, pw_lo, pw_hi);
             d = select_slow(c, SCALE, T_MASS_GT, (double)r, 0, pw_lo, pw_hi);
         }
     }
