@@ -87,6 +87,9 @@ struct __align__(16) Vars {
     int bc, bk, bd0, bd1, cc, ck, cd, tail_cnt;
     int bc_hi, bd_hi, next_row, pad5;
     double rlo, rhi;  // range of the draw r (normalised mass)
+    double adj[3];    // per target: mass of the band elements above its buckets
+    double lbm[3];    // per target: mass of the listed elements below its d range
+    int lbc[3], pad6; // per target: their count
     const bm_knobs_t *p_knobs;  // launch parameters the row release prefetches from
     const float *p_uniform;
     const int64_t *p_hist_off;
@@ -1865,9 +1868,9 @@ __device__ __forceinline__ double exp_store_pass(Ctx &c) {
 // Window list entries after the membership pass, self-contained 64-bit keys:
 //   bits 63..32  ~bits(p)        (probability descending)
 //   bits 31..16  id              (then id ascending: the stable sort's order)
-//   bits  8..0   per target t (0 cut, 1 top_k, 2 draw), bits 3t..3t+2:
+//   bits 11..0   per target t (0 cut, 1 top_k, 2 draw), bits 4t..4t+3:
 //                in the target's d range / in its band above the target's
-//                buckets / in its band below them
+//                buckets / in its band below them / below the range's d
 __device__ __forceinline__ unsigned long long list_key(float p, int id, uint32_t flags) {
     return ((unsigned long long)(~__float_as_uint(p)) << 32) | (((unsigned)id << 16) | flags);
 }
@@ -1937,7 +1940,7 @@ __device__ __forceinline__ Cand run_find(const unsigned long long *list, int j0,
     int pos = cnt0 + pre_n;
     for (int j = j0; j < j1; ++j) {
         const unsigned long long k = list[j];
-        if (!(((uint32_t)k >> (3 * t)) & 1u)) continue;
+        if (!(((uint32_t)k >> (4 * t)) & 1u)) continue;
         const double prev = cs;
         cs += (double)key_p(k);
         const bool hit = (mode == T_MASS_GE) ? ((pos == 0 || prev < T) && cs >= T)
@@ -1957,7 +1960,7 @@ __device__ __forceinline__ void run_publish(const unsigned long long *list, int 
     const bool tie = (j > 0 && key_p(list[j - 1]) == p) || (j + 1 < nl && key_p(list[j + 1]) == p);
     // a crossing in the band outside the target's buckets: the estimate
     // missed; the exact fallback decides
-    const bool outer = (((uint32_t)k >> (3 * t)) & 6u) != 0;
+    const bool outer = (((uint32_t)k >> (4 * t)) & 6u) != 0;
     out->cs = h.cs;
     out->p = p;
     out->id = lk_id(k);
@@ -2188,6 +2191,9 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     if (threadIdx.x == 0) {
         v->inv_sum = inv_sum;
         v->S = S;
+        v->adj[0] = v->adj[1] = v->adj[2] = 0.0;
+        v->lbm[0] = v->lbm[1] = v->lbm[2] = 0.0;
+        v->lbc[0] = v->lbc[1] = v->lbc[2] = 0;
         const double tot = S * ip;
         if (want_cut && v->bc < NB && v->bc_hi == NB) { v->bc_hi = lastb; v->ec = tot; }
         // range of new_sum (the cumulative mass where the walk stops), then of
@@ -2281,9 +2287,11 @@ __device__ __forceinline__ void full_path(Ctx &c) {
 #pragma unroll
         for (int t = 0; t < 3; ++t) {
             if (db - ta[t] <= tsp[t]) {
-                f |= 1u << (3 * t);
-                if (kb < tlo_b[t]) f |= 2u << (3 * t);
-                if (kb > thi_b[t]) f |= 4u << (3 * t);
+                f |= 1u << (4 * t);
+                if (kb < tlo_b[t]) f |= 2u << (4 * t);
+                if (kb > thi_b[t]) f |= 4u << (4 * t);
+            } else if (tlo_b[t] < NB && db < ta[t]) {
+                f |= 8u << (4 * t);
             }
         }
         return list_key(pe, id, f);
@@ -2329,34 +2337,87 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     __syncthreads();
     const bool list_ok = tot <= LISTCAP;
     const int nl = list_ok ? tot : 0;
-    // canonical sort
+    // Order statistics of the list.  Up to NT entries (the common case): no
+    // sort; each entry's rank and per-target exclusive prefix (mass, count)
+    // in canonical order are counted over the whole list by G threads per
+    // entry (comparisons of self-contained keys), so every entry is a run of
+    // one.  Longer lists: block sort, then runs of ceil(nl / NT) entries.
     Hit *hits = reinterpret_cast<Hit *>(c.scr + LISTCAP * 8 + 1024);
-    if (list_ok) {
-        if (nl <= NT) sort_reg(list, nl);
-        else sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
-    }
     if (threadIdx.x < 3) { hits[threadIdx.x].flags = 0; hits[threadIdx.x].jmin = INT_MAX; }
-
-    // per-thread runs of the sorted list; per target the exclusive prefix in
-    // front of the run and the total mass of the band elements above the
-    // target's buckets
-    const int RQ = (nl + NT - 1) / NT;
-    const int j0 = list_ok ? min(nl, (int)threadIdx.x * RQ) : 0;
-    const int j1 = list_ok ? min(nl, j0 + RQ) : 0;
+    const bool small = list_ok && nl <= NT;
     double pm[3] = {0.0, 0.0, 0.0}, pa[3] = {0.0, 0.0, 0.0};
     int pn[3] = {0, 0, 0};
-    for (int j = j0; j < j1; ++j) {
-        const unsigned long long k = list[j];
-        const uint32_t f = (uint32_t)k;
-        const double p = (double)key_p(k);
+    int j0 = 0, j1 = 0;
+    unsigned long long ki = ~0ull;  // small lists: this thread's entry
+    int rank = 0, tie = 0, own = 0;
+    if (small) {
+        // per pair: rank, tie and the mass of all entries in front; a
+        // target's prefix is that minus the entries below its range (all in
+        // front of any entry of the range: lower d, no tie across the band)
+        const int lg = (nl <= NT / 4) ? 2 : (nl <= NT / 2) ? 1 : 0;  // G = 1 << lg
+        const int i = (int)threadIdx.x >> lg, sub = (int)threadIdx.x & ((1 << lg) - 1);
+        own = (sub == 0 && i < nl);
+        ki = (i < nl) ? list[i] : ~0ull;
+        const float pi = key_p(ki);
+        {
+            // per target: band mass above the buckets (adj), mass and count
+            // of the entries below the range (warp sums, one atomic a warp)
+            const uint32_t fi = own ? (uint32_t)ki : 0u;
+            const int lane = threadIdx.x & 31;
+#pragma unroll
+            for (int t = 0; t < 3; ++t) {
+                const double ab = ((fi >> (4 * t)) & 2u) ? (double)pi : 0.0;
+                const double be = ((fi >> (4 * t)) & 8u) ? (double)pi : 0.0;
+                const unsigned bc_ = __ballot_sync(FULL, (fi >> (4 * t)) & 8u);
+                const double sab = warp_sum(ab), sbe = warp_sum(be);
+                if (lane == 0) {
+                    if (sab != 0.0) atomicAdd(&v->adj[t], sab);
+                    if (sbe != 0.0) atomicAdd(&v->lbm[t], sbe);
+                    if (bc_) atomicAdd(&v->lbc[t], __popc(bc_));
+                }
+            }
+        }
+        const int per = (nl + (1 << lg) - 1) >> lg;
+        const int jb = min(nl, sub * per), je = min(nl, jb + per);
+        double pall = 0.0;
+        for (int j = jb; j < je; ++j) {
+            const unsigned long long kj = list[j];
+            const bool lt = kj < ki;
+            const float pj = key_p(kj);
+            rank += lt;
+            tie |= (pj == pi) && (j != i);
+            pall += lt ? (double)pj : 0.0;
+        }
+        for (int o = 1; o < (1 << lg); o <<= 1) {
+            rank += __shfl_xor_sync(FULL, rank, o);
+            tie |= __shfl_xor_sync(FULL, tie, o);
+            pall += __shfl_xor_sync(FULL, pall, o);
+        }
+        __syncthreads();  // per-target sums complete
 #pragma unroll
         for (int t = 0; t < 3; ++t) {
-            if ((f >> (3 * t)) & 1u) { pm[t] += p; ++pn[t]; }
-            if ((f >> (3 * t)) & 2u) pa[t] += p;
+            pa[t] = v->adj[t];
+            pm[t] = pall - v->lbm[t];
+            pn[t] = rank - v->lbc[t];
         }
+    } else if (list_ok) {
+        sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
+        const int RQ = (nl + NT - 1) / NT;
+        j0 = min(nl, (int)threadIdx.x * RQ);
+        j1 = min(nl, j0 + RQ);
+        for (int j = j0; j < j1; ++j) {
+            const unsigned long long k = list[j];
+            const uint32_t f = (uint32_t)k;
+            const double p = (double)key_p(k);
+#pragma unroll
+            for (int t = 0; t < 3; ++t) {
+                if ((f >> (4 * t)) & 1u) { pm[t] += p; ++pn[t]; }
+                if ((f >> (4 * t)) & 2u) pa[t] += p;
+            }
+        }
+        block_xscan3a(pm, pn, pa, reinterpret_cast<double *>(c.scr + LISTCAP * 8),
+                      reinterpret_cast<int *>(c.scr + LISTCAP * 8 + 6 * NW * 8));
     }
-    block_xscan3a(pm, pn, pa, reinterpret_cast<double *>(c.scr + LISTCAP * 8),
-                  reinterpret_cast<int *>(c.scr + LISTCAP * 8 + 6 * NW * 8));
     // mass and count of the candidates below each target's d range
     double m0[3];
     int c0[3];
@@ -2368,20 +2429,49 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             c0[t] = (rng[t] == 0) ? abv[0] : (rng[t] == 1) ? abv[1] : (rng[t] == 2) ? abv[2] : 0;
         }
     }
+    // the crossing of target t in this thread's run (small lists: its entry,
+    // j = the entry's rank), and its publication by the lowest claimant
+    // (the per-target values are passed by value: an array indexed by a
+    // runtime target would leave registers for local memory)
+    auto find = [&](int t, double m0t, int c0t, double pmt, int pnt, int mode, double T,
+                    int m) -> Cand {
+        if (!small) return run_find(list, j0, j1, t, m0t, c0t, pmt, pnt, mode, T, m);
+        Cand r = {INT_MAX, 0, 0.0};
+        if (own && (((uint32_t)ki >> (4 * t)) & 1u)) {
+            const double prev = m0t + pmt;
+            const double cs = prev + (double)key_p(ki);
+            const int pos = c0t + pnt;
+            const bool hit = (mode == T_MASS_GE) ? ((pos == 0 || prev < T) && cs >= T)
+                             : (mode == T_MASS_GT) ? ((pos == 0 || prev <= T) && cs > T)
+                                                   : (pos == m);
+            if (hit) { r.j = rank; r.pos = pos; r.cs = cs; }
+        }
+        return r;
+    };
+    auto publish = [&](const Cand &h, int t) {
+        if (!small) { run_publish(list, nl, h, t, &hits[t]); return; }
+        Hit *o = &hits[t];
+        o->cs = h.cs;
+        o->p = key_p(ki);
+        o->id = lk_id(ki);
+        o->pos = h.pos;
+        const bool outer = (((uint32_t)ki >> (4 * t)) & 6u) != 0;
+        o->flags = 1 | (outer ? 2 : 0) | (tie ? 4 : 0);
+    };
 
     // nucleus cut and top_k position: the owners of the crossings publish them
     const bool try_c = want_cut && list_ok && bc < NB && !(m0[0] >= (double)top_p && c0[0] > 0);
     const bool try_k = want_k && list_ok && bk < NB && !(top_k - 1 < c0[1]);
     Cand hc_ = {INT_MAX, 0, 0.0}, hk_ = {INT_MAX, 0, 0.0};
     if (try_c)
-        hc_ = run_find(list, j0, j1, 0, m0[0], c0[0], pm[0], pn[0], T_MASS_GE, (double)top_p, 0);
+        hc_ = find(0, m0[0], c0[0], pm[0], pn[0], T_MASS_GE, (double)top_p, 0);
     if (try_k)
-        hk_ = run_find(list, j0, j1, 1, m0[1], c0[1], pm[1], pn[1], T_POS, 0.0, top_k - 1);
+        hk_ = find(1, m0[1], c0[1], pm[1], pn[1], T_POS, 0.0, top_k - 1);
     if (hc_.j != INT_MAX) atomicMin(&hits[0].jmin, hc_.j);
     if (hk_.j != INT_MAX) atomicMin(&hits[1].jmin, hk_.j);
     __syncthreads();
-    if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) run_publish(list, nl, hc_, 0, &hits[0]);
-    if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) run_publish(list, nl, hk_, 1, &hits[1]);
+    if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) publish(hc_, 0);
+    if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) publish(hk_, 1);
     __syncthreads();
 
     int n = ncand;
@@ -2420,10 +2510,10 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         const bool try_d = list_ok && bd < NB && !(m0[2] > (double)r && c0[2] > 0);
         Cand hd_ = {INT_MAX, 0, 0.0};
         if (try_d)
-            hd_ = run_find(list, j0, j1, 2, m0[2], c0[2], pm[2], pn[2], T_MASS_GT, (double)r, 0);
+            hd_ = find(2, m0[2], c0[2], pm[2], pn[2], T_MASS_GT, (double)r, 0);
         if (hd_.j != INT_MAX) atomicMin(&hits[2].jmin, hd_.j);
         __syncthreads();
-        if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) run_publish(list, nl, hd_, 2, &hits[2]);
+        if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) publish(hd_, 2);
         __syncthreads();
         if (!(try_d && hit_sel(hits[2], d))) {
             pw_lo = 0.0f; pw_hi = PINF;
