@@ -71,29 +71,28 @@ __device__ __forceinline__ bool protected_id(int id) {
 }
 
 struct __align__(16) Vars {
-    float mx, thr, xmin, inv_temp;
-    float temp, penalty, min_p, top_p;
-    float log_min_p, u, inv_sum, w;
-    int top_k, greedy, pen, k;
-    int sh, nslots, s_int0, s_int1;
-    int h0, h1, released, fail;
-    int kcut, kcnt, n_cand, own;
-    int bh0, bh1, bh2, clean;
-    int ln0, ln1, ln2, ln3;
-    int sel_found, sel_j, res_id, n_final;
-    float res_p, pad1, pad2, pad3;
     double S, cs, aux0, aux1;
     double mc, ec, mk, ek, md;
-    int bc, bk, bd0, bd1, cc, ck, cd, tail_cnt;
-    int bc_hi, bd_hi, next_row, pad5;
     double rlo, rhi;  // range of the draw r (normalised mass)
     double adj[3];    // per target: mass of the band elements above its buckets
-    double lbm[3];    // per target: mass of the listed elements below its d range
-    int lbc[3], pad6; // per target: their count
+    double lbm[3];    // per target: mass of the listed elements in front of its range
     const bm_knobs_t *p_knobs;  // launch parameters the row release prefetches from
     const float *p_uniform;
     const int64_t *p_hist_off;
     int64_t p_knob_stride;
+    float mx, thr, xmin, inv_temp;
+    float temp, penalty, min_p, top_p;
+    float log_min_p, u, inv_sum, res_p;
+    int top_k, greedy, pen, k;
+    int sh, nslots, s_int0, s_int1;
+    int h0, h1, released, fail;
+    int kcut, kcnt, n_cand, own;
+    int clean, ln0, ln2, ln3;
+    int sel_found, sel_j, res_id, n_final;
+    int bc, bk, bd0, bc_hi, bd_hi, next_row, lastb;
+    int frk[3];              // per target: rank of its range's first listed element
+    uint32_t ta[3], tsp[3];  // per target: d range as float bits (start, span)
+    int tlo[3], thi[3];      // per target: bucket range
 };
 
 struct Layout {
@@ -2024,7 +2023,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     const float w = __fdiv_rn(1.0f, inv_w);
     const bool cntv = top_k > 0;  // bucket counts needed (the top_k position)
     for (int i = threadIdx.x; i < (cntv ? 2 : 1) * NB; i += NT) hc[i] = 0;
-    if (threadIdx.x == 0) v->ln0 = 0;
+    if (threadIdx.x == 0) { v->ln0 = 0; v->lastb = -1; }
     __syncthreads();
     // CLEAN variants only without clamping (junk lanes must stay beyond the
     // last bucket)
@@ -2063,8 +2062,15 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     int csum = 0;
     double msum = 0.0;
     {
-        double E = exp(-(double)bb * (double)w) * 0x1p-16;  // E_b of the first bucket, scaled
-        const double qd = exp(-(double)w);
+        // E_b = exp(-b*w) of the first bucket (2^-16 scaled) and exp(-w), to
+        // ~2e-7: 2^-x as 2^-n * ex2(-f) with x = n + f from an exact product
+        auto e2neg = [](double x) -> double {
+            const double n = floor(x);
+            return ldexp((double)ex2_approx((float)(n - x)), -(int)n);
+        };
+        const double L2E = 1.4426950408889634;
+        double E = e2neg((double)bb * (double)w * L2E) * 0x1p-16;
+        const double qd = e2neg((double)w * L2E);
 #pragma unroll
         for (int q = 0; q < BPT; ++q) {
             cb[q] = cntv ? (int)hc[NB + bb + q] : 0;
@@ -2187,13 +2193,14 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             crun += cb[q];
         }
     }
-    lastb = block_max_i(lastb, c.red);  // (its barriers publish the stores above)
+    if (lastb >= 0) atomicMax(&v->lastb, lastb);
+    __syncthreads();
     if (threadIdx.x == 0) {
+        lastb = v->lastb;
         v->inv_sum = inv_sum;
         v->S = S;
         v->adj[0] = v->adj[1] = v->adj[2] = 0.0;
-        v->lbm[0] = v->lbm[1] = v->lbm[2] = 0.0;
-        v->lbc[0] = v->lbc[1] = v->lbc[2] = 0;
+        v->frk[0] = v->frk[1] = v->frk[2] = INT_MAX;
         const double tot = S * ip;
         if (want_cut && v->bc < NB && v->bc_hi == NB) { v->bc_hi = lastb; v->ec = tot; }
         // range of new_sum (the cumulative mass where the walk stops), then of
@@ -2220,30 +2227,33 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0 && v->bd0 < NB && v->bd_hi == NB) v->bd_hi = lastb;
-    __syncthreads();
-    const int bc = want_cut ? v->bc : NB, bk = want_k ? v->bk : NB, bd = v->bd0;
-    const int tlo_b[3] = {bc, bk, bd}, thi_b[3] = {v->bc_hi, bk, v->bd_hi};
-    // d ranges of the targets (float bits; inactive: empty)
-    uint32_t ta[3], tsp[3];
-#pragma unroll
-    for (int t = 0; t < 3; ++t) {
-        ta[t] = 0xffffffffu;
-        tsp[t] = 0u;
-        if (tlo_b[t] < NB) {
-            const double dl = ((double)tlo_b[t] - 0.5) / (double)inv_w;
-            const double dh = ((double)thi_b[t] + 0.5) / (double)inv_w;
-            const uint32_t a = (tlo_b[t] == 0) ? 0u
-                                               : __float_as_uint(fmaxf(0.0f, __double2float_rd(
-                                                     dl * (1.0 - 5e-7) - 1.2e-6)));
-            const uint32_t b = (thi_b[t] >= NB - 1)
+    if (threadIdx.x < 3) {
+        // d range of target t as float bits (inactive: empty), one thread each
+        const int t = threadIdx.x;
+        if (t == 2 && v->bd0 < NB && v->bd_hi == NB) v->bd_hi = v->lastb;
+        const int lo_b = (t == 0) ? (want_cut ? v->bc : NB) : (t == 1) ? (want_k ? v->bk : NB) : v->bd0;
+        const int hi_b = (t == 0) ? v->bc_hi : (t == 1) ? lo_b : v->bd_hi;
+        uint32_t a = 0xffffffffu, sp = 0u;
+        if (lo_b < NB) {
+            const double rw = 1.0 / (double)inv_w;
+            const double dl = ((double)lo_b - 0.5) * rw, dh = ((double)hi_b + 0.5) * rw;
+            a = (lo_b == 0) ? 0u
+                            : __float_as_uint(fmaxf(0.0f, __double2float_rd(dl * (1.0 - 5e-7) - 1.2e-6)));
+            const uint32_t b = (hi_b >= NB - 1)
                                    ? __float_as_uint(DNC) - 1u
                                    : min(__float_as_uint(__double2float_ru(dh * (1.0 + 5e-7) + 1.2e-6)),
                                          __float_as_uint(DNC) - 1u);
-            ta[t] = a;
-            tsp[t] = b - a;
+            sp = b - a;
         }
+        v->ta[t] = a;
+        v->tsp[t] = sp;
+        v->tlo[t] = lo_b;
+        v->thi[t] = hi_b;
     }
+    __syncthreads();
+    const int bc = want_cut ? v->bc : NB, bk = want_k ? v->bk : NB, bd = v->bd0;
+    const int tlo_b[3] = {v->tlo[0], v->tlo[1], v->tlo[2]}, thi_b[3] = {v->thi[0], v->thi[1], v->thi[2]};
+    const uint32_t ta[3] = {v->ta[0], v->ta[1], v->ta[2]}, tsp[3] = {v->tsp[0], v->tsp[1], v->tsp[2]};
     // distinct ranges for the pass; rng[t] = the range of target t
     uint32_t wl[3] = {0u, 0u, 0u}, ws[3] = {0u, 0u, 0u};
     int rng[3] = {-1, -1, -1};
@@ -2349,56 +2359,45 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     int pn[3] = {0, 0, 0};
     int j0 = 0, j1 = 0;
     unsigned long long ki = ~0ull;  // small lists: this thread's entry
-    int rank = 0, tie = 0, own = 0;
+    int rank = 0, own = 0;
     if (small) {
-        // per pair: rank, tie and the mass of all entries in front; a
-        // target's prefix is that minus the entries below its range (all in
-        // front of any entry of the range: lower d, no tie across the band)
+        // per pair: the rank and the mass of all entries in front.  A
+        // target's range is contiguous in canonical order (no tie crosses its
+        // band), so the prefix at an entry of the range is that mass minus
+        // the mass in front of the range's first entry.
         const int lg = (nl <= NT / 4) ? 2 : (nl <= NT / 2) ? 1 : 0;  // G = 1 << lg
         const int i = (int)threadIdx.x >> lg, sub = (int)threadIdx.x & ((1 << lg) - 1);
         own = (sub == 0 && i < nl);
         ki = (i < nl) ? list[i] : ~0ull;
-        const float pi = key_p(ki);
-        {
-            // per target: band mass above the buckets (adj), mass and count
-            // of the entries below the range (warp sums, one atomic a warp)
-            const uint32_t fi = own ? (uint32_t)ki : 0u;
-            const int lane = threadIdx.x & 31;
-#pragma unroll
-            for (int t = 0; t < 3; ++t) {
-                const double ab = ((fi >> (4 * t)) & 2u) ? (double)pi : 0.0;
-                const double be = ((fi >> (4 * t)) & 8u) ? (double)pi : 0.0;
-                const unsigned bc_ = __ballot_sync(FULL, (fi >> (4 * t)) & 8u);
-                const double sab = warp_sum(ab), sbe = warp_sum(be);
-                if (lane == 0) {
-                    if (sab != 0.0) atomicAdd(&v->adj[t], sab);
-                    if (sbe != 0.0) atomicAdd(&v->lbm[t], sbe);
-                    if (bc_) atomicAdd(&v->lbc[t], __popc(bc_));
-                }
-            }
-        }
         const int per = (nl + (1 << lg) - 1) >> lg;
         const int jb = min(nl, sub * per), je = min(nl, jb + per);
         double pall = 0.0;
         for (int j = jb; j < je; ++j) {
             const unsigned long long kj = list[j];
             const bool lt = kj < ki;
-            const float pj = key_p(kj);
             rank += lt;
-            tie |= (pj == pi) && (j != i);
-            pall += lt ? (double)pj : 0.0;
+            pall += lt ? (double)key_p(kj) : 0.0;
         }
         for (int o = 1; o < (1 << lg); o <<= 1) {
             rank += __shfl_xor_sync(FULL, rank, o);
-            tie |= __shfl_xor_sync(FULL, tie, o);
             pall += __shfl_xor_sync(FULL, pall, o);
         }
-        __syncthreads();  // per-target sums complete
+        const uint32_t fi = own ? (uint32_t)ki : 0u;
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            if ((fi >> (4 * t)) & 1u) atomicMin(&v->frk[t], rank);
+            if ((fi >> (4 * t)) & 2u) atomicAdd(&v->adj[t], (double)key_p(ki));  // (rare)
+        }
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < 3; ++t)
+            if (((fi >> (4 * t)) & 1u) && rank == v->frk[t]) v->lbm[t] = pall;
+        __syncthreads();
 #pragma unroll
         for (int t = 0; t < 3; ++t) {
             pa[t] = v->adj[t];
             pm[t] = pall - v->lbm[t];
-            pn[t] = rank - v->lbc[t];
+            pn[t] = rank - v->frk[t];
         }
     } else if (list_ok) {
         sort_keys(list, nl, reinterpret_cast<int *>(c.scr + LISTCAP * 8), LISTCAP);
@@ -2456,7 +2455,19 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         o->id = lk_id(ki);
         o->pos = h.pos;
         const bool outer = (((uint32_t)ki >> (4 * t)) & 6u) != 0;
-        o->flags = 1 | (outer ? 2 : 0) | (tie ? 4 : 0);
+        o->flags = 1 | (outer ? 2 : 0);
+    };
+    // small lists: a published crossing's tie flag (another entry with the
+    // same probability), one comparison per entry
+    auto mark_ties = [&](int t_a, int t_b) {
+        if (!small) return;
+        if (own) {
+            const float pi = key_p(ki);
+            const int id = lk_id(ki);
+            if ((hits[t_a].flags & 1) && hits[t_a].p == pi && hits[t_a].id != id) atomicOr(&hits[t_a].flags, 4);
+            if ((hits[t_b].flags & 1) && hits[t_b].p == pi && hits[t_b].id != id) atomicOr(&hits[t_b].flags, 4);
+        }
+        __syncthreads();
     };
 
     // nucleus cut and top_k position: the owners of the crossings publish them
@@ -2473,6 +2484,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) publish(hc_, 0);
     if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) publish(hk_, 1);
     __syncthreads();
+    mark_ties(0, 1);
 
     int n = ncand;
     double new_sum = S * ip;  // total probability mass (fallback when no cut)
@@ -2515,6 +2527,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         __syncthreads();
         if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) publish(hd_, 2);
         __syncthreads();
+        mark_ties(2, 2);
         if (!(try_d && hit_sel(hits[2], d))) {
             pw_lo = 0.0f; pw_hi = PINF;
             if (bd < NB) pwin_of(bd - 4, v->bd_hi + 4, w, inv_sum, pw_lo, pw_hi);
