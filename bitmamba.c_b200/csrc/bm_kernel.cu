@@ -49,7 +49,7 @@ constexpr float DCAP = 40.0f;                          // bucket range cap
 constexpr float MAGIC = 12582912.0f;                   // 1.5 * 2^23
 constexpr int MAGIC_I = 0x4B400000;                    // bits of MAGIC
 constexpr int LISTCAP = 2048;                          // window list cap (entries)
-constexpr int MASKW = 4;                               // membership words per thread
+constexpr int MASKW = 4;                               // top_k path: mask words per thread
 constexpr int KREG = 2;                                // top_k path: slots per thread
 constexpr int KOVF = KCAP - KREG * NT;                 // top_k path: overflow entries
 constexpr int BPT = NB / NT;                            // estimate buckets per thread
@@ -189,6 +189,17 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+// three-input max / min (sm_100): NaN inputs are ignored like fmaxf / fminf
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
 
 // --------------------------------------------------------- small helpers --
@@ -699,8 +710,20 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
     gi = INT_MAX;
     // `valid`: lanes that hold elements (junk lanes of the ragged head / tail
     // slots hold NaN and take no part in the reductions)
+    float2 chk2 = make_float2(0.0f, 0.0f);
+    const float2 it2 = make_float2(inv_temp, inv_temp), z2 = make_float2(0.0f, 0.0f);
     auto consume = [&](int s, float4 x, unsigned valid) {
         float t[4] = {x.x, x.y, x.z, x.w};
+        if (!PEN && !GREEDY && valid == 0xfu) {
+            // whole slot: two three-input max / min, two packed checks
+            float2 a = make_float2(t[0], t[1]), b = make_float2(t[2], t[3]);
+            if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
+            mx = max3f(mx, max3f(a.x, a.y, b.x), b.y);
+            xmin = min3f(xmin, min3f(a.x, a.y, b.x), b.y);
+            chk2 = __ffma2_rn(a, z2, chk2);
+            chk2 = __ffma2_rn(b, z2, chk2);
+            return;
+        }
         if (PEN) {
             const unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
             if (nib) {
@@ -780,6 +803,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         cp_async_wait_all();
         consume(es, r4[es], evld);
     }
+    chk = __fadd_rn(chk, __fadd_rn(chk2.x, chk2.y));
 }
 
 // Argmax over the scaled penalised logits with the guard semantics of
@@ -1742,7 +1766,7 @@ __device__ __forceinline__ int hist_pass(Ctx &c, float inv_w, float w, float dma
             d = make_float2(d.x == DNC ? DNC : fminf(d.x, dmax), d.y == DNC ? DNC : fminf(d.y, dmax));
         return d;
     };
-    for (int s = threadIdx.x; s < nslots; s += NT) {
+    auto slot = [&](int s, bool check) {
         const float4 x = r4[s];
         const float2 da = dpair(make_float2(x.x, x.y)), db = dpair(make_float2(x.z, x.w));
         const float2 ka = __ffma2_rn(da, iw2, mg2), kb = __ffma2_rn(db, iw2, mg2);
@@ -1756,24 +1780,32 @@ __device__ __forceinline__ int hist_pass(Ctx &c, float inv_w, float w, float dma
                                 __float_as_uint(gb.y)};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            if (kk[q] > KT) continue;  // non-candidate or junk lane
+            if (check && kk[q] > KT) continue;  // non-candidate or junk lane
             atomicAdd(&hsh[kk[q]], gg[q] & 0x7fffffu);
             if (CNT) atomicAdd(&hsh[kk[q] + NB], 1u);
             if (!CLEAN) ++ncand;
         }
+    };
+    if (CLEAN) {
+        // interior slots hold candidates only; the ragged head / tail slots
+        // (junk lanes: keys beyond the last bucket) take the key test
+        const int s0 = v->s_int0, s1 = max(v->s_int1, s0), nh = s0, nt = nslots - s1;
+        for (int s = s0 + threadIdx.x; s < s1; s += NT) slot(s, false);
+        for (int i = threadIdx.x; i < nh + nt; i += NT) slot(i < nh ? i : s1 + (i - nh), true);
+    } else {
+        for (int s = threadIdx.x; s < nslots; s += NT) slot(s, true);
     }
     return ncand;
 }
 
-// Pass 2 of the sorted path: one membership bit per element of the union of
-// the windows, each a range of d given as float bits [lo_t, lo_t + span_t]
-// (d >= 0, so its bits order like its value), and per window the count of
-// candidates above it (d below the range).  Two 16-byte slots per thread and
-// trip (slot 0 lanes 0-3, slot 1 lanes 4-7 of the trip's byte), a 32-bit word
-// every 4 trips to the thread's column of the mask area (the dead
-// histogram); the elements are gathered after the pass.  No branch or store
-// per element.
-template <bool SCALE, bool CLAMP, bool CLEAN, int NR>
+// Pass 2 of the sorted path: one flag per 16-byte slot holding an element of
+// the union of the windows, each a range of d given as float bits
+// [lo_t, lo_t + span_t] (d >= 0, so its bits order like its value), and
+// (COUNT) per window the number of candidates above it (d below the range).
+// Two slots per thread and trip, the flags of up to 16 trips in one 32-bit
+// word per thread (the dead histogram); the gather re-tests the flagged
+// slots' elements.  No branch or store per element.
+template <bool SCALE, bool CLAMP, bool CLEAN, int NR, bool COUNT>
 __device__ __forceinline__ void member_pass(Ctx &c, float dmax, const uint32_t *wlo,
                                             const uint32_t *wsp, int *above) {
     Vars *v = c.v;
@@ -1795,20 +1827,22 @@ __device__ __forceinline__ void member_pass(Ctx &c, float dmax, const uint32_t *
             d = make_float2(d.x == DNC ? DNC : fminf(d.x, dmax), d.y == DNC ? DNC : fminf(d.y, dmax));
         return d;
     };
-    auto inw = [&](float d) -> uint32_t {
-        const uint32_t k = __float_as_uint(d);
+    auto slot_in = [&](float4 x) -> uint32_t {
+        const float2 a = dpair(make_float2(x.x, x.y)), b = dpair(make_float2(x.z, x.w));
+        const uint32_t k0 = __float_as_uint(a.x), k1 = __float_as_uint(a.y);
+        const uint32_t k2 = __float_as_uint(b.x), k3 = __float_as_uint(b.y);
         bool in = false;
 #pragma unroll
         for (int t = 0; t < NR; ++t) {
-            const uint32_t u = k - lo[t];
-            in |= u <= sp[t];
-            cnt[t] += (int)(u >> 31);  // d below the window's range
+            const uint32_t u0 = k0 - lo[t], u1 = k1 - lo[t], u2 = k2 - lo[t], u3 = k3 - lo[t];
+            in |= min(min(u0, u1), min(u2, u3)) <= sp[t];
+            if (COUNT) cnt[t] += (int)((u0 >> 31) + (u1 >> 31) + (u2 >> 31) + (u3 >> 31));
         }
         return in ? 1u : 0u;
     };
     uint32_t *mw = reinterpret_cast<uint32_t *>(c.scr);
     uint32_t bits = 0;
-    // out-of-range slots: d = +inf-like (never in a window, never counted)
+    // out-of-range slots: d beyond every range, never counted
     const float ov_ = CLEAN ? JUNK : __int_as_float(0x7fc00000);
     const float4 OUT = make_float4(ov_, ov_, ov_, ov_);
     int iter = 0;
@@ -1818,20 +1852,28 @@ __device__ __forceinline__ void member_pass(Ctx &c, float dmax, const uint32_t *
         const int s0 = base + lane, s1 = base + NT + lane;
         const float4 x0 = (s0 < nslots) ? r4[s0] : OUT;
         const float4 x1 = (s1 < nslots) ? r4[s1] : OUT;
-        const float2 a0 = dpair(make_float2(x0.x, x0.y)), b0 = dpair(make_float2(x0.z, x0.w));
-        const float2 a1 = dpair(make_float2(x1.x, x1.y)), b1 = dpair(make_float2(x1.z, x1.w));
-        const uint32_t tb = inw(a0.x) | (inw(a0.y) << 1) | (inw(b0.x) << 2) | (inw(b0.y) << 3) |
-                            (inw(a1.x) << 4) | (inw(a1.y) << 5) | (inw(b1.x) << 6) |
-                            (inw(b1.y) << 7);
-        bits |= tb << (8 * (iter & 3));
-        if ((iter & 3) == 3) {
-            mw[(iter >> 2) * NT + threadIdx.x] = bits;
-            bits = 0;
-        }
+        bits |= (slot_in(x0) | (slot_in(x1) << 1)) << (2 * iter);
     }
-    if (iter & 3) mw[(iter >> 2) * NT + threadIdx.x] = bits;
+    mw[threadIdx.x] = bits;
 #pragma unroll
-    for (int t = 0; t < NR; ++t) above[t] = cnt[t];
+    for (int t = 0; t < NR; ++t) above[t] = COUNT ? cnt[t] : 0;
+}
+
+// Candidates with d below float bits `a` (d as the passes compute it), over
+// global memory: the exact count of candidates above a window when the
+// membership pass did not count (rare).
+__device__ __noinline__ int count_below_g(Ctx c, bool scale, bool clamp, float dmax, uint32_t a) {
+    c.attach();
+    const float mx = c.v->mx, thr = c.v->thr;
+    int n = 0;
+    for (int e = threadIdx.x; e < c.V; e += NT) {
+        const float l = logit_g(c, e, scale);
+        if (!(l >= thr)) continue;
+        float d = __fsub_rn(mx, l);
+        if (clamp) d = fminf(d, dmax);
+        n += __float_as_uint(d) < a;
+    }
+    return block_sum_i(n, c.red);
 }
 
 // exp pass of the id-order path: e stored in place (-0 for non-candidates),
@@ -1874,6 +1916,20 @@ __device__ __forceinline__ unsigned long long list_key(float p, int id, uint32_t
     return ((unsigned long long)(~__float_as_uint(p)) << 32) | (((unsigned)id << 16) | flags);
 }
 __device__ __forceinline__ int lk_id(unsigned long long k) { return (int)((unsigned)k >> 16); }
+struct __align__(16) Ent {
+    unsigned long long k;
+    double p;
+};
+__device__ __forceinline__ Ent make_ent(unsigned long long k) {
+    Ent e;
+    e.k = k;
+    e.p = (double)key_p(k);
+    return e;
+}
+// small lists live past the membership mask words (read into registers by the
+// gather before any entry is written) and below the sort's rank area
+constexpr int ENT_OFF = 8192;
+static_assert(ENT_OFF + NT * 16 <= LISTCAP * 8, "entry area inside the list area");
 
 // Exclusive block scan of three doubles m and three ints n, and block sums of
 // three doubles a (in place; scratch `wd`: 6 * NW doubles, `wi`: 3 * NW ints).
@@ -2273,19 +2329,31 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         rng[t] = f;
     }
     int abv[3] = {0, 0, 0};
+    // counts of the candidates above each window: needed for positions (the
+    // top_k target, stats) and for the cut's position unless its mass bound
+    // already puts it at 256 or beyond (checked exactly after the gather)
+    const bool cntp = cntv || (c.stats != nullptr) || (want_cut && bc > 0 && bc < NB && v->mc < 1024.0);
+#define BM_MEMBER(CL, CN, N)                                                           \
+    (cntp ? member_pass<SCALE, CL, CN, N, true>(c, dmax, wl, ws, abv)                  \
+          : member_pass<SCALE, CL, CN, N, false>(c, dmax, wl, ws, abv))
     if (clamp) {
-        if (ntg == 1) member_pass<SCALE, true, false, 1>(c, dmax, wl, ws, abv);
-        else if (ntg == 2) member_pass<SCALE, true, false, 2>(c, dmax, wl, ws, abv);
-        else if (ntg == 3) member_pass<SCALE, true, false, 3>(c, dmax, wl, ws, abv);
+        if (ntg == 1) member_pass<SCALE, true, false, 1, true>(c, dmax, wl, ws, abv);
+        else if (ntg == 2) member_pass<SCALE, true, false, 2, true>(c, dmax, wl, ws, abv);
+        else if (ntg == 3) member_pass<SCALE, true, false, 3, true>(c, dmax, wl, ws, abv);
     } else if (clean) {
-        if (ntg == 1) member_pass<SCALE, false, true, 1>(c, dmax, wl, ws, abv);
-        else if (ntg == 2) member_pass<SCALE, false, true, 2>(c, dmax, wl, ws, abv);
-        else if (ntg == 3) member_pass<SCALE, false, true, 3>(c, dmax, wl, ws, abv);
+        if (ntg == 1) BM_MEMBER(false, true, 1);
+        else if (ntg == 2) BM_MEMBER(false, true, 2);
+        else if (ntg == 3) BM_MEMBER(false, true, 3);
     } else {
-        if (ntg == 1) member_pass<SCALE, false, false, 1>(c, dmax, wl, ws, abv);
-        else if (ntg == 2) member_pass<SCALE, false, false, 2>(c, dmax, wl, ws, abv);
-        else if (ntg == 3) member_pass<SCALE, false, false, 3>(c, dmax, wl, ws, abv);
+        if (ntg == 1) BM_MEMBER(false, false, 1);
+        else if (ntg == 2) BM_MEMBER(false, false, 2);
+        else if (ntg == 3) BM_MEMBER(false, false, 3);
     }
+#undef BM_MEMBER
+    const bool counted = cntp || clamp;
+    // entries of lists of up to NT elements: the key and its probability as a
+    // double, side by side (one 16-byte load per pair in the rank loop)
+    Ent *ent = reinterpret_cast<Ent *>(c.scr + ENT_OFF);
     // exact probability and window flags of a listed element as its key
     auto to_key = [&](int id, float l) -> unsigned long long {
         const float pe = __fmul_rn(exp_one(__fsub_rn(l, mx)), inv_sum);
@@ -2306,37 +2374,65 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         }
         return list_key(pe, id, f);
     };
-    // gather the window elements marked by the membership pass into keys:
-    // block scan of the per-thread bit counts, then every thread writes its own
+    // gather the window elements of the flagged slots into keys: count them,
+    // block scan of the counts, then every thread writes its own
     int tot;
     {
         const uint32_t *mw = reinterpret_cast<const uint32_t *>(c.scr);
         const int wbase = threadIdx.x & ~31, lane = threadIdx.x & 31;
-        const int ntrips = (nslots - wbase + 2 * NT - 1) / (2 * NT);  // this warp's trips
-        uint32_t wm[MASKW];
-        int nb = 0;
-#pragma unroll
-        for (int q = 0; q < MASKW; ++q) {
-            wm[q] = (ntg > 0 && 4 * q < ntrips) ? mw[q * NT + threadIdx.x] : 0u;
-            nb += __popc(wm[q]);
-        }
-        // the block scan of the bit counts also sums the per-range counts of
-        // candidates above the ranges
-        int j = block_xscan_i4(nb, abv, tot, c.red);  // (its barriers end the mask reads)
+        const uint32_t fl = (ntg > 0) ? mw[threadIdx.x] : 0u;
         const float it = v->inv_temp;
+        // element q of slot `sl` in a window: its value (scaled) or NaN
+        auto member = [&](int sl, int q) -> float {
+            const int e = 4 * sl + q - sh;
+            if (sl >= nslots || e < 0 || e >= c.V) return __int_as_float(0x7fc00000);
+            const float l = SCALE ? __fmul_rn(c.row[4 * sl + q], it) : c.row[4 * sl + q];
+            if (!(l >= thr)) return __int_as_float(0x7fc00000);
+            float d = __fsub_rn(mx, l);
+            if (clamp) d = fminf(d, dmax);
+            const uint32_t db = __float_as_uint(d);
+            bool in = false;
 #pragma unroll
-        for (int q = 0; q < MASKW; ++q) {
-            uint32_t m = wm[q];
-            while (m) {
-                const int bpos = __ffs(m) - 1;
-                m &= m - 1;
-                const int trip = 4 * q + (bpos >> 3), k = bpos & 7;
-                const int sl = wbase + trip * 2 * NT + (k < 4 ? 0 : NT) + lane;
-                // marked lanes lie in slots < nslots; the clamp only keeps a
-                // read inside the row buffer whatever the bits say
-                const int r = min(4 * sl + (k & 3), 4 * nslots - 1);
-                const float l = SCALE ? __fmul_rn(c.row[r], it) : c.row[r];
-                if (j < LISTCAP) list[j] = to_key(r - sh, l);
+            for (int t = 0; t < 3; ++t) in |= (db - ta[t] <= tsp[t]);
+            return in ? l : __int_as_float(0x7fc00000);
+        };
+        auto slot_of = [&](int bpos) { return wbase + (bpos >> 1) * 2 * NT + (bpos & 1) * NT + lane; };
+        // member lanes of the first 8 flagged slots, 4 bits each (later
+        // slots are re-tested in the write loop)
+        uint32_t mm = 0;
+        int nb = 0, k = 0;
+        for (uint32_t m = fl; m; m &= m - 1, ++k) {
+            const int sl = slot_of(__ffs(m) - 1);
+            uint32_t m4 = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float l = member(sl, q);
+                m4 |= (l == l) ? (1u << q) : 0u;
+            }
+            nb += __popc(m4);
+            if (k < 8) mm |= m4 << (4 * k);
+        }
+        // the block scan of the member counts also sums the per-range counts
+        // of candidates above the ranges
+        int j = block_xscan_i4(nb, abv, tot, c.red);  // (its barriers end the flag reads)
+        k = 0;
+        for (uint32_t m = fl; m; m &= m - 1, ++k) {
+            const int sl = slot_of(__ffs(m) - 1);
+            uint32_t m4 = (mm >> (4 * k)) & 15u;
+            if (k >= 8) {
+                m4 = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float l = member(sl, q);
+                    m4 |= (l == l) ? (1u << q) : 0u;
+                }
+            }
+            for (; m4; m4 &= m4 - 1) {
+                const int q = __ffs(m4) - 1;
+                const float l = SCALE ? __fmul_rn(c.row[4 * sl + q], it) : c.row[4 * sl + q];
+                const unsigned long long key = to_key(4 * sl + q - sh, l);
+                if (tot <= NT) ent[j] = make_ent(key);
+                else if (j < LISTCAP) list[j] = key;
                 ++j;
             }
         }
@@ -2368,15 +2464,15 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         const int lg = (nl <= NT / 4) ? 2 : (nl <= NT / 2) ? 1 : 0;  // G = 1 << lg
         const int i = (int)threadIdx.x >> lg, sub = (int)threadIdx.x & ((1 << lg) - 1);
         own = (sub == 0 && i < nl);
-        ki = (i < nl) ? list[i] : ~0ull;
+        ki = (i < nl) ? ent[i].k : ~0ull;
         const int per = (nl + (1 << lg) - 1) >> lg;
         const int jb = min(nl, sub * per), je = min(nl, jb + per);
         double pall = 0.0;
         for (int j = jb; j < je; ++j) {
-            const unsigned long long kj = list[j];
-            const bool lt = kj < ki;
+            const Ent e = ent[j];
+            const bool lt = e.k < ki;
             rank += lt;
-            pall += lt ? (double)key_p(kj) : 0.0;
+            pall += lt ? e.p : 0.0;
         }
         for (int o = 1; o < (1 << lg); o <<= 1) {
             rank += __shfl_xor_sync(FULL, rank, o);
@@ -2426,6 +2522,9 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         for (int t = 0; t < 3; ++t) {
             m0[t] = mh[t] * ip - pa[t];
             c0[t] = (rng[t] == 0) ? abv[0] : (rng[t] == 1) ? abv[1] : (rng[t] == 2) ? abv[2] : 0;
+            // uncounted: nothing lies below a range that starts at d = 0;
+            // otherwise a large placeholder (the cut's bound is checked below)
+            if (!counted) c0[t] = (tlo_b[t] == 0) ? 0 : (1 << 28);
         }
     }
     // the crossing of target t in this thread's run (small lists: its entry,
@@ -2470,6 +2569,11 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         __syncthreads();
     };
 
+    if (!counted && want_cut && bc > 0 && bc < NB && !(v->mc - pa[0] / ip >= 256.5)) {
+        // the placeholder stands for at least 256 candidates above the cut's
+        // range only while their e-mass (each e <= 1) reaches 256: count
+        c0[0] = count_below_g(c, SCALE, clamp, dmax, ta[0]);
+    }
     // nucleus cut and top_k position: the owners of the crossings publish them
     const bool try_c = want_cut && list_ok && bc < NB && !(m0[0] >= (double)top_p && c0[0] > 0);
     const bool try_k = want_k && list_ok && bk < NB && !(top_k - 1 < c0[1]);
@@ -2536,7 +2640,10 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
     int id;
     float pp;
-    if (d.found && d.pos < n) { id = d.id; pp = d.p; }
+    // the draw's crossing lies in the nucleus when it is at or before the
+    // nucleus' last element in canonical order (p desc, id asc)
+    const bool in_nucleus = !tail.found || d.p > tail.p || (d.p == tail.p && d.id <= tail.id);
+    if (d.found && in_nucleus) { id = d.id; pp = d.p; }
     else { id = tail.id; pp = tail.p; d.tie = tail.tie; }
     if (partial && d.tie) {
         // the reference's heap layout decides the order among equal
