@@ -1790,7 +1790,12 @@ __device__ __forceinline__ int hist_pass(Ctx &c, float inv_w, float w, float dma
         // interior slots hold candidates only; the ragged head / tail slots
         // (junk lanes: keys beyond the last bucket) take the key test
         const int s0 = v->s_int0, s1 = max(v->s_int1, s0), nh = s0, nt = nslots - s1;
-        for (int s = s0 + threadIdx.x; s < s1; s += NT) slot(s, false);
+        int s = s0 + threadIdx.x;
+        for (; s + NT < s1; s += 2 * NT) {  // two slots in flight
+            slot(s, false);
+            slot(s + NT, false);
+        }
+        if (s < s1) slot(s, false);
         for (int i = threadIdx.x; i < nh + nt; i += NT) slot(i < nh ? i : s1 + (i - nh), true);
     } else {
         for (int s = threadIdx.x; s < nslots; s += NT) slot(s, true);
@@ -2481,7 +2486,9 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         const uint32_t fi = own ? (uint32_t)ki : 0u;
 #pragma unroll
         for (int t = 0; t < 3; ++t) {
-            if ((fi >> (4 * t)) & 1u) atomicMin(&v->frk[t], rank);
+            // lowest rank of the range: a warp minimum, one atomic a warp
+            const int rmin = __reduce_min_sync(FULL, ((fi >> (4 * t)) & 1u) ? rank : INT_MAX);
+            if ((threadIdx.x & 31) == 0 && rmin != INT_MAX) atomicMin(&v->frk[t], rmin);
             if ((fi >> (4 * t)) & 2u) atomicAdd(&v->adj[t], (double)key_p(ki));  // (rare)
         }
         __syncthreads();
@@ -2569,7 +2576,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         __syncthreads();
     };
 
-    if (!counted && want_cut && bc > 0 && bc < NB && !(v->mc - pa[0] / ip >= 256.5)) {
+    if (!counted && want_cut && bc > 0 && bc < NB && !(v->mc - pa[0] * S * 1.001 >= 256.5)) {
         // the placeholder stands for at least 256 candidates above the cut's
         // range only while their e-mass (each e <= 1) reaches 256: count
         c0[0] = count_below_g(c, SCALE, clamp, dmax, ta[0]);
