@@ -90,6 +90,8 @@ struct __align__(16) Vars {
     int clean, ln0, ln2, ln3;
     int sel_found, sel_j, res_id, n_final;
     int bc, bk, bd0, bc_hi, bd_hi, next_row, lastb;
+    int amax;       // index of the maximum (lowest among equal maxima)
+    uint32_t h0b;   // fixed-point mass sum of bucket 0
     int frk[3];              // per target: rank of its range's first listed element
     uint32_t ta[3], tsp[3];  // per target: d range as float bits (start, span)
     int tlo[3], thi[3];      // per target: bucket range
@@ -718,7 +720,9 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
             // whole slot: two three-input max / min, two packed checks
             float2 a = make_float2(t[0], t[1]), b = make_float2(t[2], t[3]);
             if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
-            mx = max3f(mx, max3f(a.x, a.y, b.x), b.y);
+            // (gi: the slot of this thread's maximum)
+            const float m4 = fmaxf(max3f(a.x, a.y, b.x), b.y);
+            if (m4 > mx) { mx = m4; gi = s; }
             xmin = min3f(xmin, min3f(a.x, a.y, b.x), b.y);
             chk2 = __ffma2_rn(a, z2, chk2);
             chk2 = __ffma2_rn(b, z2, chk2);
@@ -740,6 +744,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
                 if (t[q] > gv) { gv = t[q]; gi = 4 * s + q - sh; }
             } else {
                 const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
+                if (l > mx) gi = s;
                 mx = fmaxf(mx, l);
                 xmin = fminf(xmin, l);
                 chk = __fmaf_rn(l, 0.0f, chk);
@@ -2130,6 +2135,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             return ldexp((double)ex2_approx((float)(n - x)), -(int)n);
         };
         const double L2E = 1.4426950408889634;
+        if (threadIdx.x == 0) v->h0b = hc[0];
         double E = e2neg((double)bb * (double)w * L2E) * 0x1p-16;
         const double qd = e2neg((double)w * L2E);
 #pragma unroll
@@ -2256,6 +2262,16 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     }
     if (lastb >= 0) atomicMax(&v->lastb, lastb);
     __syncthreads();
+    if (want_cut && !want_k && v->bc == 0 && v->bc_hi == 0 && v->h0b < 2u * 64880u &&
+        v->amax != INT_MAX) {
+        // bucket 0 holds one element (each adds at least 64880), the maximum
+        // (e = 1, p = inv_sum), and its probability alone reaches top_p: the
+        // nucleus is that element (n = 1; src/model.c:84-118, 327-356), the
+        // draw r = u * p < p picks it (u = 1: the last element, the same)
+        release_row(c);
+        write_result(c, v->amax, inv_sum, (ncand > 256) ? 6 : 7, ncand, 1, 1);
+        return;
+    }
     if (threadIdx.x == 0) {
         lastb = v->lastb;
         v->inv_sum = inv_sum;
@@ -2717,6 +2733,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             v->s_int0 = (i0 + sh) >> 2;
             v->s_int1 = v->s_int0 + (n4 >> 2);
             v->released = 0;
+            v->amax = INT_MAX;
             const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
             v->temp = kn.temp;
             v->penalty = kn.penalty;
@@ -2789,7 +2806,21 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             release_row(c);
             write_result(c, gi == INT_MAX ? 0 : gi, 1.0f, 1, 0, 0, 0);
         } else {
+            const float lmx = mx;
             block_maxmin_chk(mx, xmin, chk, c.red);
+            if (lmx == mx && gi != INT_MAX) {
+                // this thread saw the maximum in slot gi: its index
+                const float4 x = reinterpret_cast<const float4 *>(c.row)[gi];
+                const float xv[4] = {x.x, x.y, x.z, x.w};
+                int idx = INT_MAX;
+#pragma unroll
+                for (int q = 3; q >= 0; --q) {
+                    const int e = 4 * gi + q - sh;
+                    const float l = scale ? __fmul_rn(xv[q], v->inv_temp) : xv[q];
+                    if (e >= 0 && e < V && l == mx) idx = e;
+                }
+                if (idx != INT_MAX) atomicMin(&v->amax, idx);
+            }
             if (tid == 0) {
                 v->mx = mx;
                 v->xmin = xmin;
