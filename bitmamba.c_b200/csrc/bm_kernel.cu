@@ -1736,9 +1736,10 @@ __device__ __forceinline__ float2 kf_pair(float2 d, float2 iw2, float2 mg2, floa
 // 32-bit shared atomic per candidate (plus a count atomic when CNT: only rows
 // whose top_k position is needed).  A member with d = b*w + t (|t| <= w/2;
 // t = fma(-b, w, d), exact to one rounding) has e = exp(-d) = E_b * exp(-t),
-// E_b = exp(-b*w).  The pass adds G = round(2^16 exp(-t)) (the cubic Taylor
-// polynomial: |t| < 0.01, error below 4e-10; G in [64880, 66200], so a
-// bucket's sum stays below 2^32 for any V <= 64880), so that
+// E_b = exp(-b*w).  The pass adds G = round(2^16 exp(-t)) (the quadratic
+// Taylor polynomial: |t| < 0.01, error below 1.7e-7 relative, odd in t; G in
+// [64880, 66200], so a bucket's sum stays below 2^32 for any V <= 64880), so
+// that
 //   mass_b = E_b * 2^-16 * sum_b
 // is the members' e-sum to within 2^-17 relative per member (rounding, not
 // bias: below 4e-6 of the row's total mass in the worst case, ~1e-9 typical).
@@ -1756,9 +1757,8 @@ __device__ __forceinline__ int hist_pass(Ctx &c, float inv_w, float w, float dma
     const float2 iw2 = make_float2(inv_w, inv_w), mg2 = make_float2(MAGIC, MAGIC);
     const float2 nmg2 = make_float2(-MAGIC, -MAGIC), nw2 = make_float2(-w, -w);
     const float2 mx2 = make_float2(mx, mx);
-    // 2^16 exp(-t) = 2^16 - 2^16 t + 2^15 t^2 - (2^16/6) t^3, rounded to an
-    // integer by the bias 2^23 (bits 0x4B000000 + G)
-    const float2 c3 = make_float2(-0x1p16f / 6.0f, -0x1p16f / 6.0f);
+    // 2^16 exp(-t) ~ 2^16 - 2^16 t + 2^15 t^2, rounded to an integer by the
+    // bias 2^23 (bits 0x4B000000 + G)
     const float2 c2 = make_float2(0x1p15f, 0x1p15f), c1 = make_float2(-0x1p16f, -0x1p16f);
     const float2 g0 = make_float2(0x1p23f + 0x1p16f, 0x1p23f + 0x1p16f);
     const int KT = MAGIC_I + NB - 1;
@@ -1777,8 +1777,8 @@ __device__ __forceinline__ int hist_pass(Ctx &c, float inv_w, float w, float dma
         const float2 ka = __ffma2_rn(da, iw2, mg2), kb = __ffma2_rn(db, iw2, mg2);
         const float2 ta = __ffma2_rn(__fadd2_rn(ka, nmg2), nw2, da);
         const float2 tb = __ffma2_rn(__fadd2_rn(kb, nmg2), nw2, db);
-        const float2 ga = __ffma2_rn(ta, __ffma2_rn(ta, __ffma2_rn(ta, c3, c2), c1), g0);
-        const float2 gb = __ffma2_rn(tb, __ffma2_rn(tb, __ffma2_rn(tb, c3, c2), c1), g0);
+        const float2 ga = __ffma2_rn(ta, __ffma2_rn(ta, c2, c1), g0);
+        const float2 gb = __ffma2_rn(tb, __ffma2_rn(tb, c2, c1), g0);
         const int kk[4] = {__float_as_int(ka.x), __float_as_int(ka.y), __float_as_int(kb.x),
                            __float_as_int(kb.y)};
         const uint32_t gg[4] = {__float_as_uint(ga.x), __float_as_uint(ga.y), __float_as_uint(gb.x),
@@ -2459,9 +2459,9 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         }
     }
     // release: the row buffer is no longer read on the common path (the list
-    // holds the window elements; the rare fallbacks read global memory)
+    // holds the window elements, visible after its barrier; the rare
+    // fallbacks read global memory)
     release_row(c);
-    __syncthreads();
     const bool list_ok = tot <= LISTCAP;
     const int nl = list_ok ? tot : 0;
     // Order statistics of the list.  Up to NT entries (the common case): no
@@ -2580,9 +2580,10 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         o->flags = 1 | (outer ? 2 : 0);
     };
     // small lists: a published crossing's tie flag (another entry with the
-    // same probability), one comparison per entry
-    auto mark_ties = [&](int t_a, int t_b) {
-        if (!small) return;
+    // same probability), one comparison per entry; only the top-256 heap
+    // path (a nucleus of fewer than 256) reads it
+    auto mark_ties = [&](int t_a, int t_b, bool need) {
+        if (!small || !need) return;
         if (own) {
             const float pi = key_p(ki);
             const int id = lk_id(ki);
@@ -2611,7 +2612,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     if (hc_.j != INT_MAX && hc_.j == hits[0].jmin) publish(hc_, 0);
     if (hk_.j != INT_MAX && hk_.j == hits[1].jmin) publish(hk_, 1);
     __syncthreads();
-    mark_ties(0, 1);
+    mark_ties(0, 1, (hits[0].flags & 1) && hits[0].pos < 256 && ncand > 256);
 
     int n = ncand;
     double new_sum = S * ip;  // total probability mass (fallback when no cut)
@@ -2654,7 +2655,7 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         __syncthreads();
         if (hd_.j != INT_MAX && hd_.j == hits[2].jmin) publish(hd_, 2);
         __syncthreads();
-        mark_ties(2, 2);
+        mark_ties(2, 2, partial);
         if (!(try_d && hit_sel(hits[2], d))) {
             pw_lo = 0.0f; pw_hi = PINF;
             if (bd < NB) pwin_of(bd - 4, v->bd_hi + 4, w, inv_sum, pw_lo, pw_hi);
