@@ -1,0 +1,331 @@
+// Final RMSNorm + bf16 lm_head GEMM on the sm_100a tensor cores, the producer
+// of the sampler's logits (the optional fused variant of the sampling path).
+//
+//   rmsnorm   a[r, :] = bf16(x[r, :] * rms_r * w), the normalisation of
+//             jserv/bitmamba.c src/kernel.c:72-91 (scalar_rms_norm: four
+//             strided fp32 accumulators, 1 / sqrtf(sum / size + 1e-6f)),
+//             bit for bit, then rounded to bf16 for the tensor cores.
+//   gemm      logits[r, n] = sum_k a[r, k] * W[n, k]: one CTA per 128 x 256
+//             output tile; a TMA producer thread streams 128 x 64 (a) and
+//             256 x 64 (W) bf16 tiles with 128-byte swizzle through a 4-stage
+//             shared-memory ring (no multicast), one thread issues
+//             tcgen05.mma (kind::f16, M=128, N=256, K=16) into a 256-column
+//             fp32 accumulator in tensor memory and frees each stage with
+//             tcgen05.commit; the four warps then read their 32 accumulator
+//             lanes with tcgen05.ld and store fp32 logits.  CTAs run along M
+//             first, so the 64-row groups that share a W tile run together
+//             and W streams from HBM once.
+//
+// The reference computes its lm_head as a ternary BitLinear (src/model.c:
+// 1239-1262); this bf16 variant has no counterpart there and is checked
+// against a CPU GEMM of the same bf16 operands.  Every wait is bounded.
+#include "bm_lmhead.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+namespace bml {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, NTH = 128;
+constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t TMEM_COLS = BN;  // fp32 accumulator: one column per n
+constexpr size_t GEMM_SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
+
+__device__ __forceinline__ uint32_t sa(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(n));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(sa(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
+    if (mbar_try(b, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    for (unsigned it = 0; it < (1u << 30); ++it) {
+        if (mbar_try(b, parity)) return true;
+        if (gtimer() - t0 > WAIT_NS) return false;
+    }
+    return false;
+}
+// 2-D tiled TMA load (no multicast): box at (x = k, y = row) into smem
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+        "{%2, %3}], [%4];" ::"r"(sa(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(sa(bar))
+        : "memory");
+}
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1, layout 2.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     sa(bar))
+                 : "memory");
+}
+// 32 consecutive fp32 accumulator columns of this thread's lane
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(NTH, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                float *out, int M, int N, int K, int64_t ldo, int *err) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the 128-byte swizzle pattern repeats every 1024 bytes: tiles start on
+    // a 1024-byte boundary
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                          ~static_cast<uintptr_t>(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *accf = empty + STAGES;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 1);
+    int *fail = reinterpret_cast<int *>(tslot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int KT = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accf, 1);
+        *fail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         sa(tslot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tslot;
+
+    if (threadIdx.x == 0) {
+        // producer: stage s is free once the MMAs that read it completed
+        for (int kt = 0; kt < KT; ++kt) {
+            const int s = kt % STAGES;
+            if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
+                atomicOr(fail, 1);
+                break;
+            }
+            unsigned char *st = smem + (size_t)s * STAGE_BYTES;
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(st, &tmA, kt * BK, m0, &full[s]);
+            tma_load_2d(st + A_BYTES, &tmB, kt * BK, n0, &full[s]);
+        }
+    } else if (threadIdx.x == 32) {
+        // MMA issuer: bf16 x bf16 -> fp32, A and B K-major, M=128, N=256
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                               ((uint32_t)(BM >> 4) << 24);
+        for (int kt = 0; kt < KT; ++kt) {
+            const int s = kt % STAGES;
+            if (!mbar_wait(&full[s], (kt / STAGES) & 1)) {
+                atomicOr(fail, 1);
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a0 = sa(smem + (size_t)s * STAGE_BYTES), b0 = a0 + A_BYTES;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+                umma_f16(tmem, sdesc(a0 + k * 32), sdesc(b0 + k * 32), idesc,
+                         (kt > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+        }
+        umma_commit(accf);  // arrives once every MMA issued above has completed
+    }
+    __syncwarp();
+    // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31
+    const bool ok = mbar_wait(accf, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int row = m0 + warp * 32 + lane;
+    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        const int col0 = n0 + c * 32;
+        if (ok && row < M && col0 < N) {
+            float *o = out + (int64_t)row * ldo + col0;
+            if (vec && col0 + 32 <= N) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(o + j) =
+                        make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                    __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < N) o[j] = __uint_as_float(r[j]);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    if (threadIdx.x == 0 && (!ok || *fail)) atomicOr(err, 4);
+}
+
+// One warp per row: the row is staged in shared memory, lanes 0-3 keep the
+// reference's four strided accumulators (multiply, then add: the library is
+// built without contraction), lane 0 adds them left to right with the tail.
+constexpr int RN_WARPS = 8;
+constexpr int RN_MAXD = 4096;  // floats staged per warp
+
+__global__ void __launch_bounds__(RN_WARPS * 32)
+    rmsnorm_kernel(const float *x, int B, int D, const float *w, __nv_bfloat16 *a) {
+    extern __shared__ float rn_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *buf = rn_smem + (size_t)warp * D;
+    for (int r = blockIdx.x * RN_WARPS + warp; r < B; r += gridDim.x * RN_WARPS) {
+        const float *xr = x + (int64_t)r * D;
+        for (int i = lane; i < D; i += 32) buf[i] = xr[i];
+        __syncwarp();
+        float s = 0.0f;
+        const int D4 = (D / 4) * 4;
+        if (lane < 4)
+            for (int i = lane; i < D4; i += 4) s = __fadd_rn(s, __fmul_rn(buf[i], buf[i]));
+        const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
+                    s3 = __shfl_sync(0xffffffffu, s, 3);
+        float rms = 0.0f;
+        if (lane == 0) {
+            float sum = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);
+            for (int i = D4; i < D; ++i) sum = __fadd_rn(sum, __fmul_rn(buf[i], buf[i]));
+            rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), 1e-6f)));
+        }
+        rms = __shfl_sync(0xffffffffu, rms, 0);
+        __nv_bfloat16 *ar = a + (int64_t)r * D;
+        for (int i = lane; i < D; i += 32)
+            ar[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(buf[i], rms), w[i]));
+        __syncwarp();
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_mu;
+
+cudaError_t get_encode() {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_encode) return cudaSuccess;
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return cudaSuccess;
+}
+
+// rows x K bf16 row-major, box BK x box_rows, 128-byte swizzle, zero fill
+cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int K, int box_rows) {
+    const cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+                                gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t prepare() {
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)GEMM_SMEM);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(RN_WARPS * RN_MAXD * sizeof(float)));
+}
+
+cudaError_t rmsnorm_bf16(const float *x, int B, int D, const float *w, uint16_t *a,
+                         cudaStream_t s) {
+    if (B <= 0) return cudaSuccess;
+    if (D <= 0 || D > RN_MAXD) return cudaErrorInvalidValue;
+    int grid = (B + RN_WARPS - 1) / RN_WARPS;
+    if (grid > 148 * 8) grid = 148 * 8;
+    rmsnorm_kernel<<<grid, RN_WARPS * 32, (size_t)RN_WARPS * D * sizeof(float), s>>>(
+        x, B, D, w, reinterpret_cast<__nv_bfloat16 *>(a));
+    return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16(const uint16_t *a, const uint16_t *W, int M, int N, int K, float *out,
+                      int64_t ldo, int *err, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (K <= 0 || K % 8 || (reinterpret_cast<uintptr_t>(a) & 15) ||
+        (reinterpret_cast<uintptr_t>(W) & 15) || ldo < N)
+        return cudaErrorInvalidValue;
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    CUtensorMap ma, mb;
+    if ((e = make_map(&ma, a, M, K, BM)) != cudaSuccess) return e;
+    if ((e = make_map(&mb, W, N, K, BN)) != cudaSuccess) return e;
+    const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+    if (grid.y > 65535) return cudaErrorInvalidValue;
+    gemm_kernel<<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, err);
+    return cudaGetLastError();
+}
+
+}  // namespace bml

@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "bm_kernel.cuh"
+#include "bm_lmhead.cuh"
 #include "bm_sampler.h"
 
 struct bm_ctx {
@@ -36,6 +37,12 @@ struct bm_ctx {
     float *d_prob;
     bm_row_stats_t *d_stats;
     size_t cap_rows;
+    // lm_head: normalised bf16 hidden states and the logits of the fused call
+    uint16_t *d_a;
+    size_t cap_a;
+    float *d_lm;
+    size_t cap_lm;
+    int lm_ready;
 };
 
 namespace {
@@ -216,6 +223,8 @@ void bm_ctx_destroy(bm_ctx_t *c) {
     cudaFree(c->d_id);
     cudaFree(c->d_prob);
     cudaFree(c->d_stats);
+    cudaFree(c->d_a);
+    cudaFree(c->d_lm);
     if (c->stream) cudaStreamDestroy(c->stream);
     free(c);
 }
@@ -267,6 +276,54 @@ int bm_sample_batch(bm_ctx_t *c, const float *d_logits, int B, int V, int64_t ld
     int grid = B < c->sms ? B : c->sms;
     CK(bmk::launch(p, grid, s));
     return BM_OK;
+}
+
+int bm_lmhead_logits(bm_ctx_t *c, const float *d_hidden, int B, int d_model,
+                     const float *d_norm_w, const uint16_t *d_W, int V, float *d_logits,
+                     int64_t ld, void *stream) {
+    if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    if (B < 0 || V < 1 || ld < V)
+        return fail(BM_ERR_INVALID_ARG, "B = %d, V = %d, ld = %lld", B, V, (long long)ld);
+    if (B == 0) return BM_OK;
+    if (!d_hidden || !d_norm_w || !d_W || !d_logits)
+        return fail(BM_ERR_INVALID_ARG, "hidden, norm weight, W and logits must be non-NULL");
+    if (d_model <= 0 || d_model % 8 || d_model > 4096)
+        return fail(BM_ERR_UNSUPPORTED, "d_model = %d (needs a multiple of 8, <= 4096)", d_model);
+    if ((reinterpret_cast<uintptr_t>(d_W) & 15) || (reinterpret_cast<uintptr_t>(d_hidden) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_logits) & 3))
+        return fail(BM_ERR_INVALID_ARG, "W / hidden not 16-byte or logits not 4-byte aligned");
+    if ((V + 255) / 256 > 65535) return fail(BM_ERR_UNSUPPORTED, "V = %d too large", V);
+    CK(cudaSetDevice(c->device));
+    if (!c->lm_ready) {
+        CK(bml::prepare());
+        c->lm_ready = 1;
+    }
+    int rc = grow(&c->d_a, &c->cap_a, (size_t)B * d_model);
+    if (rc != BM_OK) return rc;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    CK(bml::rmsnorm_bf16(d_hidden, B, d_model, d_norm_w, c->d_a, s));
+    CK(bml::gemm_bf16(c->d_a, d_W, B, V, d_model, d_logits, ld, c->d_err, s));
+    return BM_OK;
+}
+
+int bm_lmhead_sample_batch(bm_ctx_t *c, const float *d_hidden, int B, int d_model,
+                           const float *d_norm_w, const uint16_t *d_W, int V,
+                           const int32_t *d_hist, const int64_t *d_hist_off,
+                           const bm_knobs_t *d_knobs, int64_t knob_stride, const float *d_uniform,
+                           int32_t *d_out_id, float *d_out_prob, bm_row_stats_t *d_stats,
+                           void *stream) {
+    if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    // the sampler's checks first (a logits pointer stands in for the buffer)
+    const int64_t ld = ((int64_t)V + 3) / 4 * 4;  // 16-byte rows for the GEMM's stores
+    int rc = check_batch_args(c, d_hidden, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
+                              d_uniform, d_out_id);
+    if (rc != BM_OK || B == 0) return rc;
+    CK(cudaSetDevice(c->device));
+    if ((rc = grow(&c->d_lm, &c->cap_lm, (size_t)B * (size_t)ld)) != BM_OK) return rc;
+    rc = bm_lmhead_logits(c, d_hidden, B, d_model, d_norm_w, d_W, V, c->d_lm, ld, stream);
+    if (rc != BM_OK) return rc;
+    return bm_sample_batch(c, c->d_lm, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
+                           d_uniform, d_out_id, d_out_prob, d_stats, stream);
 }
 
 int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,

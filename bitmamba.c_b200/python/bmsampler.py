@@ -67,6 +67,11 @@ def lib():
         L.bm_sample_batch_host.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int64, _P, _P, _P, ctypes.c_int64, _P,
                                            _P, _P, _P]
+        L.bm_lmhead_logits.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
+                                       ctypes.c_int, _P, ctypes.c_int64, _P]
+        L.bm_lmhead_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
+                                             ctypes.c_int, _P, _P, _P, ctypes.c_int64, _P, _P,
+                                             _P, _P, _P]
         L.bm_rng_seed.argtypes = [ctypes.c_uint64]
         L.bm_rng_seed.restype = None
         L.bm_rng_next.restype = ctypes.c_uint64
@@ -152,6 +157,27 @@ class Context:
                                     c(out_prob_ptr) if out_prob_ptr else None,
                                     c(stats_ptr) if stats_ptr else None,
                                     c(stream) if stream else None))
+
+    def lmhead_logits(self, hidden_ptr, B, d_model, norm_w_ptr, w_ptr, V, logits_ptr, ld,
+                      stream=None):
+        """bm_lmhead_logits on raw device pointers (ints): RMSNorm + bf16 GEMM."""
+        c = ctypes.c_void_p
+        check(lib().bm_lmhead_logits(self._c, c(hidden_ptr), B, d_model, c(norm_w_ptr),
+                                     c(w_ptr), V, c(logits_ptr), ld,
+                                     c(stream) if stream else None))
+
+    def lmhead_sample(self, hidden_ptr, B, d_model, norm_w_ptr, w_ptr, V, hist_ptr, off_ptr,
+                      knobs_ptr, knob_stride, u_ptr, out_id_ptr, out_prob_ptr=None,
+                      stats_ptr=None, stream=None):
+        """bm_lmhead_sample_batch on raw device pointers (ints)."""
+        c = ctypes.c_void_p
+        check(lib().bm_lmhead_sample_batch(self._c, c(hidden_ptr), B, d_model, c(norm_w_ptr),
+                                           c(w_ptr), V, c(hist_ptr) if hist_ptr else None,
+                                           c(off_ptr) if off_ptr else None, c(knobs_ptr),
+                                           knob_stride, c(u_ptr), c(out_id_ptr),
+                                           c(out_prob_ptr) if out_prob_ptr else None,
+                                           c(stats_ptr) if stats_ptr else None,
+                                           c(stream) if stream else None))
 
     def sample_host(self, logits, hist, hist_off, knobs, uniform, want_prob=True,
                     want_stats=True):

@@ -162,7 +162,7 @@ int bm_sample_batch(bm_ctx_t *ctx, const float *d_logits, int B, int V,
  * time (different streams, or threads without ordering) race on the row
  * schedule and must not be made; order them on one stream.
  *
- * Limits: V <= bm_max_vocab (50280 on a B200) else BM_ERR_UNSUPPORTED;
+ * Limits: V <= bm_max_vocab (50268 on a B200) else BM_ERR_UNSUPPORTED;
  * B <= 2^30 rows per call else BM_ERR_INVALID_ARG.  There is no context
  * error flag to check: a row whose bounded wait in the kernel expired gets
  * id -1.
@@ -173,6 +173,39 @@ int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,
                             const float *d_uniform, int32_t *d_out_id,
                             float *d_out_prob, bm_row_stats_t *d_stats,
                             void *stream);
+
+/* ---- final RMSNorm + bf16 lm_head feeding the sampler ---------------------- */
+
+/*
+ * logits[r, n] = sum_k bf16(rmsnorm(hidden[r, :]))[k] * W[n, k] for B rows of
+ * d_model hidden states (fp32, row-major) and a V x d_model bf16 lm_head (raw
+ * bf16 bits, row-major), accumulated in fp32 on the tensor cores, into
+ * d_logits (fp32, row pitch ld >= V).  rmsnorm is the reference's
+ * scalar_rms_norm (src/kernel.c:72-91: x * (1 / sqrtf(sum_sq / d + 1e-6f)) * w,
+ * the sum of squares in four strided fp32 accumulators), bit for bit, rounded
+ * to bf16 for the tensor cores.  The reference's own lm_head is a ternary
+ * BitLinear (src/model.c:1239-1262); this bf16 projection has no counterpart
+ * there.  d_model % 8 == 0, d_model <= 4096; hidden, W 16-byte aligned.
+ * Stream-ordered; errors of the kernels show in bm_ctx_check.
+ */
+int bm_lmhead_logits(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
+                     const float *d_norm_w, const uint16_t *d_W, int V,
+                     float *d_logits, int64_t ld, void *stream);
+
+/*
+ * bm_lmhead_logits into a context-owned logits buffer, then bm_sample_batch
+ * on it: the fused decode step from the final hidden state to the next
+ * token (the sampler's arguments as in bm_sample_batch).  No counterpart in
+ * the reference (see bm_lmhead_logits); the sampling part replaces the tail
+ * of model_forward_step (src/model.c:1268-1307).
+ */
+int bm_lmhead_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
+                           const float *d_norm_w, const uint16_t *d_W, int V,
+                           const int32_t *d_hist, const int64_t *d_hist_off,
+                           const bm_knobs_t *d_knobs, int64_t knob_stride,
+                           const float *d_uniform, int32_t *d_out_id,
+                           float *d_out_prob, bm_row_stats_t *d_stats,
+                           void *stream);
 
 /* ---- batched sampling, host buffers ---------------------------------------- */
 

@@ -15,6 +15,10 @@ The five workloads mirror the sampler configurations the benchmark names:
   c4  N(0, 2^2) logits with per-row knobs (temp U[0,1.5] with 10% exactly
       0, top_k in {0,1,40,200}, top_p U[.5,1], min_p U[0,.2], penalty
       U[1,1.5]) and uniform histories of length U[0,2048]
+  c5  the fused lm_head inputs: hidden states N(0,1) [B x d], RMSNorm
+      weight 1 + N(0, 0.02), lm_head W [V x d] N(0, 0.02) as bf16, default
+      knobs, 256-id Zipf(1.1) histories (make_c5; its logits come from the
+      GEMM)
 No public dataset is involved; these stand in for real decode logits.
 """
 from __future__ import annotations
@@ -233,3 +237,29 @@ def rng_uniforms(seed: int, n: int) -> np.ndarray:
         v = (s * 0x2545F4914F6CDD1D) & m
         out[i] = np.float32(float(v >> 11)) * np.float32(1.0 / 9007199254740992.0)
     return out
+
+
+class LmBatch:
+    """Inputs of the fused lm_head + sampler (config c5)."""
+
+    def __init__(self, hidden, norm_w, w_bits, hist, hist_off, knobs):
+        self.hidden, self.norm_w, self.w_bits = hidden, norm_w, w_bits
+        self.hist, self.hist_off = hist, hist_off
+        self.temp, self.penalty, self.min_p, self.top_p, self.top_k = knobs
+
+
+def make_c5(seed: int, B: int, V: int = VOCAB, d: int = 2048, H: int = 256) -> LmBatch:
+    """c5: hidden N(0,1), norm weight 1+N(0,.02), W N(0,.02) rounded to bf16
+    (nearest even), default knobs, 256-id Zipf(1.1) histories."""
+    hidden = normal(seed, 5001, B * d).astype(np.float32).reshape(B, d)
+    norm_w = (1.0 + 0.02 * normal(seed, 5002, d)).astype(np.float32)
+    w = (0.02 * normal(seed, 5003, V * d)).astype(np.float32)
+    u = w.view(np.uint32).astype(np.uint64)
+    w_bits = ((u + np.uint64(0x7FFF) + ((u >> np.uint64(16)) & np.uint64(1))) >>
+              np.uint64(16)).astype(np.uint16).reshape(V, d)
+    hist, off = _csr([ids_zipf(seed, 5100 + r, H, V) for r in range(B)])
+    k = DEFAULT_KNOBS
+    kn = (np.full(B, k["temp"], np.float32), np.full(B, k["penalty"], np.float32),
+          np.full(B, k["min_p"], np.float32), np.full(B, k["top_p"], np.float32),
+          np.full(B, k["top_k"], np.int32))
+    return LmBatch(hidden, norm_w, w_bits, hist, off, kn)
