@@ -482,6 +482,166 @@ def run_ours(args):
     return 0
 
 
+def run_lmhead(args):
+    """Config c5: the fused decode step (final RMSNorm + bf16 lm_head GEMM on
+    the tensor cores + the sampler on its logits) for B rows per GPU of
+    d_model=2048 hidden states, V=50257, default knobs, 256-id Zipf histories.
+    Reports rows/s of the whole step and the GEMM's tensor roofline."""
+    import torch
+    import bmsampler as bm
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (no CPU fallback)")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    sys.path[:0] = [os.path.join(ROOT, "tests", "golden")]
+    import synth
+    B, V, d = args.B, args.V, args.d_model
+    dev = torch.device("cuda", local)
+    ctx = bm.Context(local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321 + rank)
+    hidden = torch.randn(B, d, generator=g, device=dev, dtype=torch.float32)
+    norm_w = 1.0 + 0.02 * torch.randn(d, generator=g, device=dev, dtype=torch.float32)
+    W = (0.02 * torch.randn(V, d, generator=g, device=dev, dtype=torch.float32)).to(
+        torch.bfloat16).view(torch.int16).contiguous()
+    hists = [synth.ids_zipf(77 + rank, 6000 + r, 256, V) for r in range(B)]
+    hist_h = np.concatenate(hists).astype(np.int32)
+    off_h = np.arange(0, 256 * (B + 1), 256, dtype=np.int64)
+    k = synth.DEFAULT_KNOBS
+    knobs = bm.knobs_array(k["temp"], k["penalty"], k["min_p"], k["top_p"], k["top_k"])
+    knobs_d = torch.from_numpy(knobs.view(np.uint8).copy()).to(dev)
+    hist_d = torch.from_numpy(hist_h).to(dev)
+    off_d = torch.from_numpy(off_h).to(dev)
+    start, _ = shard_rows(world * B, world, rank)
+    u_host = ref_uniforms(world * B)[start:start + B]
+    u_d = torch.from_numpy(u_host).to(dev)
+    out_d = torch.empty(B, dtype=torch.int32, device=dev)
+    ld = (V + 3) // 4 * 4
+    logits = torch.empty((B, ld), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)
+
+    def fused():
+        ctx.lmhead_sample(hidden.data_ptr(), B, d, norm_w.data_ptr(), W.data_ptr(), V,
+                          hist_d.data_ptr(), off_d.data_ptr(), knobs_d.data_ptr(), 0,
+                          u_d.data_ptr(), out_d.data_ptr(), None, None, stream.cuda_stream)
+
+    def gemm_only():
+        ctx.lmhead_logits(hidden.data_ptr(), B, d, norm_w.data_ptr(), W.data_ptr(), V,
+                          logits.data_ptr(), ld, stream.cuda_stream)
+
+    def sampler_only():
+        ctx.sample_device(logits.data_ptr(), B, V, ld, hist_d.data_ptr(), off_d.data_ptr(),
+                          knobs_d.data_ptr(), 0, u_d.data_ptr(), out_d.data_ptr(), None, None,
+                          stream.cuda_stream)
+
+    def timed(fn, steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        return max_over_ranks(dist, e0.elapsed_time(e1), dev) / steps
+
+    for fn in (fused, gemm_only, sampler_only):
+        for _ in range(args.warmup):
+            fn()
+    torch.cuda.synchronize(dev)
+    ctx.check()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    t_a = time.time()
+    ms = timed(fused, args.steps)
+    t_b = time.time()
+    clocks.window = (t_a, t_b)
+    gemm_ms = timed(gemm_only, max(3, args.steps // 2))
+    samp_ms = timed(sampler_only, max(3, args.steps // 2))
+    time.sleep(0.25)
+    clocks.stop()
+    ctx.check()
+    flops = 2.0 * B * V * d
+    tflops = flops / (gemm_ms / 1e3) / 1e12
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    ids_dev = out_d.cpu().numpy()
+
+    # CPU leg on a bounded sample: the oracle's RMSNorm + float64 product of
+    # the same bf16 operands and the sampler oracle on the GPU's own logits
+    cpu = parity = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")]
+        import lmhead_oracle as lo
+        import oracle
+        import parity as parity_rule
+        n = min(B, 16)
+        hx = hidden[:n].cpu().numpy()
+        wn = norm_w.cpu().numpy()
+        wb = W.cpu().numpy().view(np.uint16)
+        t0 = time.time()
+        ref_logits = lo.lmhead_logits(lo.rmsnorm_bf16(hx, wn), wb)
+        dt_gemm = time.time() - t0
+        gpu_l = logits[:n, :V].cpu().numpy()
+        max_err = float(np.abs(gpu_l - ref_logits).max())
+        rb = synth.Batch(gpu_l, hist_h[:256 * n], off_h[:n + 1], np.full(n, k["temp"]),
+                         np.full(n, k["penalty"]), np.full(n, k["min_p"]),
+                         np.full(n, k["top_p"]), np.full(n, k["top_k"]))
+        t0 = time.time()
+        rids, _, res = oracle.sample_batch(rb, u_host[:n])
+        dt_samp = time.time() - t0
+        rep = parity_rule.compare(ids_dev[:n], None, rids, None, res)
+        cpu = {"value": n / (dt_gemm + dt_samp), "unit": UNIT, "cores": 1, "kind": "port",
+               "sample": f"first {n} rows: numpy RMSNorm + float64 GEMM of the bf16 operands, "
+                         f"then the sampler oracle"}
+        parity = {"rows": n, "identical_ids": rep["exact"], "bad": rep["bad"],
+                  "max_abs_logit_err_vs_float64": max_err}
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "sampled tokens/s, fused RMSNorm + bf16 lm_head + sampler (c5)",
+        "value": world * B / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 GEMM (fp32 accumulate), f32 sampler",
+        "data": "synthetic",
+        "config": {"workload": "c5 fused lm_head + sampler: hidden N(0,1), RMSNorm weight "
+                               "1+N(0,.02), W [V x d] N(0,.02) bf16, default knobs, 256-id "
+                               "Zipf histories", "B_per_gpu": B, "V": V, "d_model": d,
+                   "l2": "W (206 MB) and the logits (B*V*4 bytes) exceed the 126 MB L2"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": tflops / peak, "traffic": None, "kernel": "gemm_kernel (+rmsnorm)",
+                     "kernel_ms": gemm_ms, "flops_per_launch": flops,
+                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"},
+        "parts_ms": {"rmsnorm_plus_gemm": gemm_ms, "sampler": samp_ms, "fused_step": ms},
+        "cpu_baseline": cpu, "e2e": None, "clocks": clocks.summary(),
+        "gpu_launches": 3 * args.steps, "parity_sample": parity,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -493,13 +653,17 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c3",
-                    help="c3 is the benchmark; the others report the other configs")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c3",
+                    help="c3 is the benchmark; the others report the other configs "
+                         "(c5: the fused lm_head + sampler step)")
+    ap.add_argument("--d-model", type=int, default=2048)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "c5":
+        return run_lmhead(args)
     return run_ours(args)
 
 
