@@ -225,37 +225,48 @@ __global__ void __launch_bounds__(NTH, 1)
     if (threadIdx.x == 0 && (!ok || *fail)) atomicOr(err, 4);
 }
 
-// One warp per row: the row is staged in shared memory, lanes 0-3 keep the
-// reference's four strided accumulators (multiply, then add: the library is
-// built without contraction), lane 0 adds them left to right with the tail.
+// One warp per row: the row is staged in shared memory with 16-byte loads,
+// lanes 0-3 keep the reference's four strided accumulators (multiply, then
+// add: the library is built without contraction), lane 0 adds them left to
+// right with the tail; the norm weight is staged once per block.  D % 4 == 0.
 constexpr int RN_WARPS = 8;
 constexpr int RN_MAXD = 4096;  // floats staged per warp
 
 __global__ void __launch_bounds__(RN_WARPS * 32)
     rmsnorm_kernel(const float *x, int B, int D, const float *w, __nv_bfloat16 *a) {
-    extern __shared__ float rn_smem[];
+    extern __shared__ float4 rn_smem4[];
+    float *wbuf = reinterpret_cast<float *>(rn_smem4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *buf = rn_smem + (size_t)warp * D;
+    float *buf = wbuf + D + (size_t)warp * D;
+    const int D4 = D / 4;
+    for (int i = threadIdx.x; i < D4; i += blockDim.x)
+        reinterpret_cast<float4 *>(wbuf)[i] = reinterpret_cast<const float4 *>(w)[i];
+    __syncthreads();
     for (int r = blockIdx.x * RN_WARPS + warp; r < B; r += gridDim.x * RN_WARPS) {
-        const float *xr = x + (int64_t)r * D;
-        for (int i = lane; i < D; i += 32) buf[i] = xr[i];
+        const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)r * D);
+#pragma unroll 4
+        for (int i = lane; i < D4; i += 32) reinterpret_cast<float4 *>(buf)[i] = xr[i];
         __syncwarp();
         float s = 0.0f;
-        const int D4 = (D / 4) * 4;
-        if (lane < 4)
-            for (int i = lane; i < D4; i += 4) s = __fadd_rn(s, __fmul_rn(buf[i], buf[i]));
+        if (lane < 4) {
+#pragma unroll 8
+            for (int i = lane; i < 4 * D4; i += 4) s = __fadd_rn(s, __fmul_rn(buf[i], buf[i]));
+        }
         const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
                     s3 = __shfl_sync(0xffffffffu, s, 3);
         float rms = 0.0f;
         if (lane == 0) {
-            float sum = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);
-            for (int i = D4; i < D; ++i) sum = __fadd_rn(sum, __fmul_rn(buf[i], buf[i]));
+            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);
             rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), 1e-6f)));
         }
         rms = __shfl_sync(0xffffffffu, rms, 0);
-        __nv_bfloat16 *ar = a + (int64_t)r * D;
-        for (int i = lane; i < D; i += 32)
-            ar[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(buf[i], rms), w[i]));
+        __nv_bfloat162 *ar = reinterpret_cast<__nv_bfloat162 *>(a + (int64_t)r * D);
+#pragma unroll 4
+        for (int i = lane; i < D / 2; i += 32) {
+            const float v0 = __fmul_rn(__fmul_rn(buf[2 * i], rms), wbuf[2 * i]);
+            const float v1 = __fmul_rn(__fmul_rn(buf[2 * i + 1], rms), wbuf[2 * i + 1]);
+            ar[i] = __halves2bfloat162(__float2bfloat16_rn(v0), __float2bfloat16_rn(v1));
+        }
         __syncwarp();
     }
 }
@@ -297,16 +308,18 @@ cudaError_t prepare() {
                              (int)GEMM_SMEM);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(RN_WARPS * RN_MAXD * sizeof(float)));
+                                (int)((RN_WARPS + 1) * RN_MAXD * sizeof(float)));
 }
 
 cudaError_t rmsnorm_bf16(const float *x, int B, int D, const float *w, uint16_t *a,
                          cudaStream_t s) {
     if (B <= 0) return cudaSuccess;
-    if (D <= 0 || D > RN_MAXD) return cudaErrorInvalidValue;
+    if (D <= 0 || D > RN_MAXD || D % 4 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(w) & 15))
+        return cudaErrorInvalidValue;
     int grid = (B + RN_WARPS - 1) / RN_WARPS;
     if (grid > 148 * 8) grid = 148 * 8;
-    rmsnorm_kernel<<<grid, RN_WARPS * 32, (size_t)RN_WARPS * D * sizeof(float), s>>>(
+    rmsnorm_kernel<<<grid, RN_WARPS * 32, (size_t)(RN_WARPS + 1) * D * sizeof(float), s>>>(
         x, B, D, w, reinterpret_cast<__nv_bfloat16 *>(a));
     return cudaGetLastError();
 }

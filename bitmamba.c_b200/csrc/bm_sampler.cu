@@ -290,8 +290,9 @@ int bm_lmhead_logits(bm_ctx_t *c, const float *d_hidden, int B, int d_model,
     if (d_model <= 0 || d_model % 8 || d_model > 4096)
         return fail(BM_ERR_UNSUPPORTED, "d_model = %d (needs a multiple of 8, <= 4096)", d_model);
     if ((reinterpret_cast<uintptr_t>(d_W) & 15) || (reinterpret_cast<uintptr_t>(d_hidden) & 15) ||
-        (reinterpret_cast<uintptr_t>(d_logits) & 3))
-        return fail(BM_ERR_INVALID_ARG, "W / hidden not 16-byte or logits not 4-byte aligned");
+        (reinterpret_cast<uintptr_t>(d_norm_w) & 15) || (reinterpret_cast<uintptr_t>(d_logits) & 3))
+        return fail(BM_ERR_INVALID_ARG,
+                    "W / hidden / norm weight not 16-byte or logits not 4-byte aligned");
     if ((V + 255) / 256 > 65535) return fail(BM_ERR_UNSUPPORTED, "V = %d too large", V);
     CK(cudaSetDevice(c->device));
     if (!c->lm_ready) {

@@ -185,7 +185,8 @@ int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,
  * the sum of squares in four strided fp32 accumulators), bit for bit, rounded
  * to bf16 for the tensor cores.  The reference's own lm_head is a ternary
  * BitLinear (src/model.c:1239-1262); this bf16 projection has no counterpart
- * there.  d_model % 8 == 0, d_model <= 4096; hidden, W 16-byte aligned.
+ * there.  d_model % 8 == 0, d_model <= 4096; hidden, norm weight and W
+ * 16-byte aligned.
  * Stream-ordered; errors of the kernels show in bm_ctx_check.
  */
 int bm_lmhead_logits(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
