@@ -5,16 +5,16 @@
 //             jserv/bitmamba.c src/kernel.c:72-91 (scalar_rms_norm: four
 //             strided fp32 accumulators, 1 / sqrtf(sum / size + 1e-6f)),
 //             bit for bit, then rounded to bf16 for the tensor cores.
-//   gemm      logits[r, n] = sum_k a[r, k] * W[n, k]: one CTA per 128 x 256
-//             output tile; a TMA producer thread streams 128 x 64 (a) and
-//             256 x 64 (W) bf16 tiles with 128-byte swizzle through a 4-stage
-//             shared-memory ring (no multicast), one thread issues
-//             tcgen05.mma (kind::f16, M=128, N=256, K=16) into a 256-column
-//             fp32 accumulator in tensor memory and frees each stage with
-//             tcgen05.commit; the four warps then read their 32 accumulator
-//             lanes with tcgen05.ld and store fp32 logits.  CTAs run along M
-//             first, so the 64-row groups that share a W tile run together
-//             and W streams from HBM once.
+//   gemm      logits[r, n] = sum_k a[r, k] * W[n, k] in 128 x 256 output
+//             tiles on persistent CTAs (one per SM): a TMA producer thread
+//             streams 128 x 64 (a) and 256 x 64 (W) bf16 tiles with 128-byte
+//             swizzle through a 4-stage shared-memory ring (no multicast),
+//             one thread issues tcgen05.mma (kind::f16, M=128, N=256, K=16)
+//             into one of two 256-column fp32 accumulators in tensor memory
+//             and frees each stage with tcgen05.commit; four warps drain the
+//             other accumulator with tcgen05.ld and store fp32 logits while
+//             the next tile's MMAs run.  Tiles go M-index first, so CTAs
+//             running together share W tiles and W streams from HBM once.
 //
 // The reference computes its lm_head as a ternary BitLinear (src/model.c:
 // 1239-1262); this bf16 variant has no counterpart there and is checked
@@ -30,10 +30,11 @@
 namespace bml {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, NTH = 128;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int EPI_WARPS = 4, NTH = 32 * (2 + EPI_WARPS);  // producer, MMA, 4 drain warps
 constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr uint32_t TMEM_COLS = BN;  // fp32 accumulator: one column per n
+constexpr uint32_t TMEM_COLS = 2 * BN;  // two fp32 accumulators, one column per n
 constexpr size_t GEMM_SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
@@ -115,6 +116,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Persistent: CTA c takes tiles c, c + grid, ... (M-tile index fastest, so
+// CTAs running together share W tiles).  Warp 0 lane 0 is the TMA producer,
+// warp 1 lane 0 issues the MMAs, warps 2-5 drain the accumulators.  Two
+// 256-column accumulators in tensor memory let the drain of tile i overlap
+// the MMAs of tile i + 1.
 __global__ void __launch_bounds__(NTH, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 float *out, int M, int N, int K, int64_t ldo, int *err) {
@@ -126,11 +132,13 @@ __global__ void __launch_bounds__(NTH, 1)
                                           ~static_cast<uintptr_t>(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
     uint64_t *empty = full + STAGES;
-    uint64_t *accf = empty + STAGES;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 1);
-    int *fail = reinterpret_cast<int *>(tslot + 1);
+    uint64_t *accf = empty + STAGES;  // [2] accumulator b complete
+    uint64_t *acce = accf + 2;        // [2] accumulator b drained
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acce + 2);
+    int *abort_ = reinterpret_cast<int *>(tslot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int MT = (M + BM - 1) / BM, NTL = (N + BN - 1) / BN;
+    const int tiles = MT * NTL;
     const int KT = (K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -138,8 +146,11 @@ __global__ void __launch_bounds__(NTH, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accf, 1);
-        *fail = 0;
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], EPI_WARPS);
+        }
+        *abort_ = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
@@ -155,74 +166,105 @@ __global__ void __launch_bounds__(NTH, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tslot;
+    auto fail = [&]() { atomicOr(abort_, 1); };
+    auto aborted = [&]() { return *reinterpret_cast<volatile int *>(abort_) != 0; };
 
     if (threadIdx.x == 0) {
         // producer: stage s is free once the MMAs that read it completed
-        for (int kt = 0; kt < KT; ++kt) {
-            const int s = kt % STAGES;
-            if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
-                atomicOr(fail, 1);
-                break;
+        int g = 0;
+        for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x) {
+            const int m0 = (t % MT) * BM, n0 = (t / MT) * BN;
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % STAGES;
+                if (g >= STAGES && !mbar_wait(&empty[s], ((g / STAGES) - 1) & 1)) {
+                    fail();
+                    break;
+                }
+                unsigned char *st = smem + (size_t)s * STAGE_BYTES;
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                tma_load_2d(st, &tmA, kt * BK, m0, &full[s]);
+                tma_load_2d(st + A_BYTES, &tmB, kt * BK, n0, &full[s]);
             }
-            unsigned char *st = smem + (size_t)s * STAGE_BYTES;
-            mbar_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(st, &tmA, kt * BK, m0, &full[s]);
-            tma_load_2d(st + A_BYTES, &tmB, kt * BK, n0, &full[s]);
         }
     } else if (threadIdx.x == 32) {
         // MMA issuer: bf16 x bf16 -> fp32, A and B K-major, M=128, N=256
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                ((uint32_t)(BM >> 4) << 24);
-        for (int kt = 0; kt < KT; ++kt) {
-            const int s = kt % STAGES;
-            if (!mbar_wait(&full[s], (kt / STAGES) & 1)) {
-                atomicOr(fail, 1);
+        int g = 0, i = 0;
+        for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x, ++i) {
+            const int b = i & 1;
+            if (i >= 2 && !mbar_wait(&acce[b], ((i >> 1) - 1) & 1)) {
+                fail();
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a0 = sa(smem + (size_t)s * STAGE_BYTES), b0 = a0 + A_BYTES;
+            const uint32_t acc = tmem + (uint32_t)(b * BN);
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % STAGES;
+                if (!mbar_wait(&full[s], (g / STAGES) & 1)) {
+                    fail();
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a0 = sa(smem + (size_t)s * STAGE_BYTES), b0 = a0 + A_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-                umma_f16(tmem, sdesc(a0 + k * 32), sdesc(b0 + k * 32), idesc,
-                         (kt > 0 || k > 0) ? 1u : 0u);
-            umma_commit(&empty[s]);
+                for (int k = 0; k < BK / 16; ++k)
+                    umma_f16(acc, sdesc(a0 + k * 32), sdesc(b0 + k * 32), idesc,
+                             (kt > 0 || k > 0) ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(&accf[b]);  // arrives once every MMA of this tile completed
         }
-        umma_commit(accf);  // arrives once every MMA issued above has completed
+    } else if (warp >= 2) {
+        // drain: warp w reads accumulator lanes (rows) 32 (w % 4) .. + 31
+        const int q = warp & 3;
+        const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const int b = i & 1;
+            const bool ok = !aborted() && mbar_wait(&accf[b], (i >> 1) & 1);
+            if (!ok) {
+                fail();
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int m0 = (t % MT) * BM, n0 = (t / MT) * BN;
+            const int row = m0 + q * 32 + lane;
+            const uint32_t tb = tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tb + c * 32, r);
+                const int col0 = n0 + c * 32;
+                if (row < M && col0 < N) {
+                    float *o = out + (int64_t)row * ldo + col0;
+                    if (vec && col0 + 32 <= N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4 *>(o + j) =
+                                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < N) o[j] = __uint_as_float(r[j]);
+                    }
+                }
+            }
+            // the accumulator is free for the MMAs of tile i + 2
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(&acce[b])) : "memory");
+        }
     }
     __syncwarp();
-    // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31
-    const bool ok = mbar_wait(accf, 0);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16);
-    const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        const int col0 = n0 + c * 32;
-        if (ok && row < M && col0 < N) {
-            float *o = out + (int64_t)row * ldo + col0;
-            if (vec && col0 + 32 <= N) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4 *>(o + j) =
-                        make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                    __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (col0 + j < N) o[j] = __uint_as_float(r[j]);
-            }
-        }
-    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(TMEM_COLS)
                      : "memory");
-    if (threadIdx.x == 0 && (!ok || *fail)) atomicOr(err, 4);
+    if (threadIdx.x == 0 && *abort_) atomicOr(err, 4);
 }
 
 // One warp per row: the row is staged in shared memory with 16-byte loads,
@@ -335,8 +377,13 @@ cudaError_t gemm_bf16(const uint16_t *a, const uint16_t *W, int M, int N, int K,
     CUtensorMap ma, mb;
     if ((e = make_map(&ma, a, M, K, BM)) != cudaSuccess) return e;
     if ((e = make_map(&mb, W, N, K, BN)) != cudaSuccess) return e;
-    const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
-    if (grid.y > 65535) return cudaErrorInvalidValue;
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    if (tiles > (1LL << 30)) return cudaErrorInvalidValue;
+    const int grid = (int)(tiles < sms ? tiles : sms);
     gemm_kernel<<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, err);
     return cudaGetLastError();
 }
