@@ -1741,8 +1741,9 @@ __device__ __forceinline__ float2 kf_pair(float2 d, float2 iw2, float2 mg2, floa
 // [64880, 66200], so a bucket's sum stays below 2^32 for any V <= 64880), so
 // that
 //   mass_b = E_b * 2^-16 * sum_b
-// is the members' e-sum to within 2^-17 relative per member (rounding, not
-// bias: below 4e-6 of the row's total mass in the worst case, ~1e-9 typical).
+// is the members' e-sum to within 2^-17 = 7.6e-6 relative per member: below
+// 7.6e-6 of the row's total mass in the worst case (equal logits round
+// alike), ~1e-9 when the roundings are independent.
 // CLEAN rows skip the candidate test (junk lanes have keys beyond the last
 // bucket); CLAMP rows file every d > dmax at dmax (e < e^-40 there).  Returns
 // this thread's candidate count (non-CLEAN rows).
