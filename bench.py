@@ -483,10 +483,13 @@ def run_ours(args):
 
 
 def run_lmhead(args):
-    """Config c5: the fused decode step (final RMSNorm + bf16 lm_head GEMM on
-    the tensor cores + the sampler on its logits) for B rows per GPU of
+    """Configs c5 / c6: the fused decode step for B rows per GPU of
     d_model=2048 hidden states, V=50257, default knobs, 256-id Zipf histories.
-    Reports rows/s of the whole step and the GEMM's tensor roofline."""
+    c5: final RMSNorm + bf16 lm_head GEMM on the tensor cores + the sampler.
+    c6: the reference's own producer, final RMSNorm + BitLinear RMSNorm +
+    int8 quantisation + ternary lm_head (int8 tensor cores, exact int32
+    accumulation) + the sampler.  Reports rows/s of the whole step and the
+    GEMM's tensor roofline."""
     import torch
     import bmsampler as bm
 
@@ -505,14 +508,28 @@ def run_lmhead(args):
     sys.path[:0] = [os.path.join(ROOT, "tests", "golden")]
     import synth
     B, V, d = args.B, args.V, args.d_model
+    tern = args.workload == "c6"
     dev = torch.device("cuda", local)
     ctx = bm.Context(local)
     g = torch.Generator(device=dev)
     g.manual_seed(4321 + rank)
     hidden = torch.randn(B, d, generator=g, device=dev, dtype=torch.float32)
     norm_w = 1.0 + 0.02 * torch.randn(d, generator=g, device=dev, dtype=torch.float32)
-    W = (0.02 * torch.randn(V, d, generator=g, device=dev, dtype=torch.float32)).to(
-        torch.bfloat16).view(torch.int16).contiguous()
+    if tern:
+        # c6: the reference's ternary lm_head; 2-bit codes with P(0) = 1/2
+        # (a random code 3 becomes 1), decoded to int8 once (weight setup)
+        lmh_norm = 1.0 + 0.02 * torch.randn(d, generator=g, device=dev, dtype=torch.float32)
+        pk = torch.randint(0, 256, (V, d // 4), generator=g, device=dev, dtype=torch.int32)
+        pk = pk & ~((pk & (pk >> 1) & 0x55) << 1)
+        packed = pk.to(torch.uint8).contiguous()
+        del pk
+        w_scale = 16.0
+        W = torch.empty((V, d), dtype=torch.int8, device=dev)
+        ctx.ternary_unpack(packed.data_ptr(), V, d, W.data_ptr())
+        torch.cuda.synchronize(dev)
+    else:
+        W = (0.02 * torch.randn(V, d, generator=g, device=dev, dtype=torch.float32)).to(
+            torch.bfloat16).view(torch.int16).contiguous()
     hists = [synth.ids_zipf(77 + rank, 6000 + r, 256, V) for r in range(B)]
     hist_h = np.concatenate(hists).astype(np.int32)
     off_h = np.arange(0, 256 * (B + 1), 256, dtype=np.int64)
@@ -531,13 +548,24 @@ def run_lmhead(args):
     torch.cuda.synchronize(dev)
 
     def fused():
-        ctx.lmhead_sample(hidden.data_ptr(), B, d, norm_w.data_ptr(), W.data_ptr(), V,
-                          hist_d.data_ptr(), off_d.data_ptr(), knobs_d.data_ptr(), 0,
-                          u_d.data_ptr(), out_d.data_ptr(), None, None, stream.cuda_stream)
+        if tern:
+            ctx.ternary_sample(hidden.data_ptr(), B, d, norm_w.data_ptr(), lmh_norm.data_ptr(),
+                               W.data_ptr(), w_scale, V, hist_d.data_ptr(), off_d.data_ptr(),
+                               knobs_d.data_ptr(), 0, u_d.data_ptr(), out_d.data_ptr(), None,
+                               None, stream.cuda_stream)
+        else:
+            ctx.lmhead_sample(hidden.data_ptr(), B, d, norm_w.data_ptr(), W.data_ptr(), V,
+                              hist_d.data_ptr(), off_d.data_ptr(), knobs_d.data_ptr(), 0,
+                              u_d.data_ptr(), out_d.data_ptr(), None, None, stream.cuda_stream)
 
     def gemm_only():
-        ctx.lmhead_logits(hidden.data_ptr(), B, d, norm_w.data_ptr(), W.data_ptr(), V,
-                          logits.data_ptr(), ld, stream.cuda_stream)
+        if tern:
+            ctx.ternary_logits(hidden.data_ptr(), B, d, norm_w.data_ptr(), lmh_norm.data_ptr(),
+                               W.data_ptr(), w_scale, V, logits.data_ptr(), ld,
+                               stream.cuda_stream)
+        else:
+            ctx.lmhead_logits(hidden.data_ptr(), B, d, norm_w.data_ptr(), W.data_ptr(), V,
+                              logits.data_ptr(), ld, stream.cuda_stream)
 
     def sampler_only():
         ctx.sample_device(logits.data_ptr(), B, V, ld, hist_d.data_ptr(), off_d.data_ptr(),
@@ -583,13 +611,24 @@ def run_lmhead(args):
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except (OSError, ValueError):
         pass
-    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    if tern:
+        # no int8 figure is measured on this pool: the dense int8 tensor rate
+        # of B200 is twice its bf16 rate, so the denominator is twice the
+        # measured sustained bf16 figure
+        peak = 2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))
+        peak_src = "2 x MEASURED_PEAKS.json bf16_tflops_sustained (int8 dense = 2 x bf16)"
+    else:
+        peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+        peak_src = "MEASURED_PEAKS.json bf16_tflops_sustained"
     ids_dev = out_d.cpu().numpy()
 
     # CPU leg on a bounded sample: the oracle's RMSNorm + float64 product of
     # the same bf16 operands and the sampler oracle on the GPU's own logits
     cpu = parity = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if tern and rank == 0 and world == 1 and not args.no_cpu:
+        cpu, parity = ternary_cpu_leg(args, hidden, norm_w, lmh_norm, packed, w_scale, logits,
+                                      hist_h, off_h, u_host, ids_dev, B, V, d)
+    elif rank == 0 and world == 1 and not args.no_cpu:
         sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")]
         import lmhead_oracle as lo
         import oracle
@@ -620,26 +659,80 @@ def run_lmhead(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    if tern:
+        metric = "sampled tokens/s, final RMSNorm + ternary BitLinear lm_head + sampler (c6)"
+        dtype = "int8 x ternary GEMM (exact int32 accumulate), f32 sampler"
+        workload = ("c6 reference lm_head + sampler: hidden N(0,1), final-norm and "
+                    "BitLinear-norm weights 1+N(0,.02), ternary W [V x d] (P(0)=1/2, scale "
+                    "16) decoded to int8 once, default knobs, 256-id Zipf histories")
+        l2 = "W (103 MB int8) and the logits (B*V*4 bytes) exceed the 126 MB L2 together"
+        kern = "gemm_kernel<int8> (+ternary_prep)"
+        unit_t = "TOP/s"
+    else:
+        metric = "sampled tokens/s, fused RMSNorm + bf16 lm_head + sampler (c5)"
+        dtype = "bf16 GEMM (fp32 accumulate), f32 sampler"
+        workload = ("c5 fused lm_head + sampler: hidden N(0,1), RMSNorm weight "
+                    "1+N(0,.02), W [V x d] N(0,.02) bf16, default knobs, 256-id "
+                    "Zipf histories")
+        l2 = "W (206 MB) and the logits (B*V*4 bytes) exceed the 126 MB L2"
+        kern = "gemm_kernel (+rmsnorm)"
+        unit_t = "TFLOP/s"
     line = {
-        "metric": "sampled tokens/s, fused RMSNorm + bf16 lm_head + sampler (c5)",
+        "metric": metric,
         "value": world * B / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 GEMM (fp32 accumulate), f32 sampler",
+        "vs_baseline": None, "dtype": dtype,
         "data": "synthetic",
-        "config": {"workload": "c5 fused lm_head + sampler: hidden N(0,1), RMSNorm weight "
-                               "1+N(0,.02), W [V x d] N(0,.02) bf16, default knobs, 256-id "
-                               "Zipf histories", "B_per_gpu": B, "V": V, "d_model": d,
-                   "l2": "W (206 MB) and the logits (B*V*4 bytes) exceed the 126 MB L2"},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
-                     "frac": tflops / peak, "traffic": None, "kernel": "gemm_kernel (+rmsnorm)",
+        "config": {"workload": workload, "B_per_gpu": B, "V": V, "d_model": d, "l2": l2},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": unit_t,
+                     "frac": tflops / peak, "traffic": None, "kernel": kern,
                      "kernel_ms": gemm_ms, "flops_per_launch": flops,
-                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"},
-        "parts_ms": {"rmsnorm_plus_gemm": gemm_ms, "sampler": samp_ms, "fused_step": ms},
+                     "peak_source": peak_src},
+        "parts_ms": {"norm_plus_gemm": gemm_ms, "sampler": samp_ms, "fused_step": ms},
         "cpu_baseline": cpu, "e2e": None, "clocks": clocks.summary(),
         "gpu_launches": 3 * args.steps, "parity_sample": parity,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def ternary_cpu_leg(args, hidden, norm_f, lmh_norm, packed, w_scale, logits, hist_h, off_h,
+                    u_host, ids_dev, B, V, d):
+    """c6's CPU leg on a bounded sample: the reference's own final RMSNorm +
+    ternary lm_head (oracle/_ref, its AVX2 kernels, its thread pool over all
+    host cores) and the sampler oracle on the GPU's logits; parity of the
+    logits is bit for bit."""
+    sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")]
+    import oracle
+    import parity as parity_rule
+    import synth
+    import ternary
+    if not oracle.has_ref():
+        return None, None
+    k = synth.DEFAULT_KNOBS
+    n = min(B, 64)
+    hx = hidden[:n].cpu().numpy()
+    nf = norm_f.cpu().numpy()
+    nl = lmh_norm.cpu().numpy()
+    pk = packed.cpu().numpy()
+    cores = os.cpu_count() or 1
+    ternary.ref_logits(hx[:1], nf, nl, pk, w_scale, threads=cores)   # pool start-up
+    t0 = time.time()
+    ref_l, ks = ternary.ref_logits(hx, nf, nl, pk, w_scale, threads=cores)
+    dt = time.time() - t0
+    gpu_l = np.ascontiguousarray(logits[:n, :V].cpu().numpy())
+    diff = int((gpu_l.view(np.uint32) != ref_l.view(np.uint32)).sum())
+    rb = synth.Batch(gpu_l, hist_h[:256 * n], off_h[:n + 1], np.full(n, k["temp"]),
+                     np.full(n, k["penalty"]), np.full(n, k["min_p"]),
+                     np.full(n, k["top_p"]), np.full(n, k["top_k"]))
+    rids, _, res = oracle.sample_batch(rb, u_host[:n])
+    rep = parity_rule.compare(ids_dev[:n], None, rids, None, res)
+    cpu = {"value": n / dt, "unit": UNIT, "cores": cores, "kind": "reference",
+           "sample": f"first {n} rows: the reference's final RMSNorm + ternary lm_head "
+                     f"({ks} kernels, {cores} threads), logits only"}
+    par = {"rows": n, "logits_bit_identical_to_reference": diff == 0,
+           "logits_differing": diff, "identical_ids": rep["exact"], "bad": rep["bad"]}
+    return cpu, par
 
 
 def main():
@@ -653,16 +746,17 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c3",
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "c6"], default="c3",
                     help="c3 is the benchmark; the others report the other configs "
-                         "(c5: the fused lm_head + sampler step)")
+                         "(c5: the fused bf16 lm_head + sampler step; c6: the reference's "
+                         "ternary lm_head + sampler)")
     ap.add_argument("--d-model", type=int, default=2048)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload == "c5":
+    if args.workload in ("c5", "c6"):
         return run_lmhead(args)
     return run_ours(args)
 

@@ -95,6 +95,13 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
         "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
 }
+__device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      sa(bar))
@@ -121,9 +128,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
 // warp 1 lane 0 issues the MMAs, warps 2-5 drain the accumulators.  Two
 // 256-column accumulators in tensor memory let the drain of tile i overlap
 // the MMAs of tile i + 1.
+//
+// I8: int8 operands (kind::i8, K = 32 per instruction, so a 128-byte stage row
+// holds 128 elements), exact int32 accumulation, and the epilogue
+// out = (float) acc * row_scale[row]; otherwise bf16 operands (kind::f16,
+// 64 elements per stage row) and fp32 accumulators stored as they are.  The
+// shared-memory tiles are byte-identical in shape either way.
+template <bool I8>
 __global__ void __launch_bounds__(NTH, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                float *out, int M, int N, int K, int64_t ldo, int *err) {
+                float *out, int M, int N, int K, int64_t ldo, const float *row_scale, int *err) {
+    constexpr int BKE = I8 ? 128 : BK;  // elements per 128-byte stage row
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // the 128-byte swizzle pattern repeats every 1024 bytes: tiles start on
     // a 1024-byte boundary
@@ -139,7 +154,7 @@ __global__ void __launch_bounds__(NTH, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int MT = (M + BM - 1) / BM, NTL = (N + BN - 1) / BN;
     const int tiles = MT * NTL;
-    const int KT = (K + BK - 1) / BK;
+    const int KT = (K + BKE - 1) / BKE;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -182,14 +197,16 @@ __global__ void __launch_bounds__(NTH, 1)
                 }
                 unsigned char *st = smem + (size_t)s * STAGE_BYTES;
                 mbar_expect_tx(&full[s], STAGE_BYTES);
-                tma_load_2d(st, &tmA, kt * BK, m0, &full[s]);
-                tma_load_2d(st + A_BYTES, &tmB, kt * BK, n0, &full[s]);
+                tma_load_2d(st, &tmA, kt * BKE, m0, &full[s]);
+                tma_load_2d(st + A_BYTES, &tmB, kt * BKE, n0, &full[s]);
             }
         }
     } else if (threadIdx.x == 32) {
-        // MMA issuer: bf16 x bf16 -> fp32, A and B K-major, M=128, N=256
-        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                               ((uint32_t)(BM >> 4) << 24);
+        // MMA issuer, A and B K-major, M=128, N=256: bf16 x bf16 -> fp32
+        // (D format 1, A/B format 1 = bf16) or s8 x s8 -> s32 (D format 2,
+        // A/B format 1 = signed)
+        const uint32_t idesc = ((I8 ? 2u : 1u) << 4) | (1u << 7) | (1u << 10) |
+                               ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
         int g = 0, i = 0;
         for (int t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x, ++i) {
             const int b = i & 1;
@@ -207,10 +224,16 @@ __global__ void __launch_bounds__(NTH, 1)
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a0 = sa(smem + (size_t)s * STAGE_BYTES), b0 = a0 + A_BYTES;
+                // four instructions of 32 bytes of K each (16 bf16 or 32 int8)
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k)
-                    umma_f16(acc, sdesc(a0 + k * 32), sdesc(b0 + k * 32), idesc,
-                             (kt > 0 || k > 0) ? 1u : 0u);
+                for (int k = 0; k < 4; ++k) {
+                    if (I8)
+                        umma_i8(acc, sdesc(a0 + k * 32), sdesc(b0 + k * 32), idesc,
+                                (kt > 0 || k > 0) ? 1u : 0u);
+                    else
+                        umma_f16(acc, sdesc(a0 + k * 32), sdesc(b0 + k * 32), idesc,
+                                 (kt > 0 || k > 0) ? 1u : 0u);
+                }
                 umma_commit(&empty[s]);
             }
             umma_commit(&accf[b]);  // arrives once every MMA of this tile completed
@@ -231,10 +254,16 @@ __global__ void __launch_bounds__(NTH, 1)
             const int m0 = (t % MT) * BM, n0 = (t / MT) * BN;
             const int row = m0 + q * 32 + lane;
             const uint32_t tb = tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16);
+            const float sc = (I8 && row < M) ? row_scale[row] : 1.0f;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld32(tb + c * 32, r);
+                if (I8) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        r[j] = __float_as_uint(__fmul_rn(__int2float_rn((int)r[j]), sc));
+                }
                 const int col0 = n0 + c * 32;
                 if (row < M && col0 < N) {
                     float *o = out + (int64_t)row * ldo + col0;
@@ -313,6 +342,111 @@ __global__ void __launch_bounds__(RN_WARPS * 32)
     }
 }
 
+// ------------------------------------------------------ ternary lm_head --
+// The reference's logits producer on x86-64 (AVX2 kernels):
+//   final_feat = rms_norm(x, norm_f)                  src/model.c:1225
+//   xn = rms_norm(final_feat, lm_head_norm), max|xn|  src/arch/avx2.c:278
+//   scale_x = 127 / (max|xn| + 1e-5f)                 src/arch/avx2.c:279
+//   xq = int8(round_even(max(-128, min(xn * scale_x, 127))))
+//                                                      src/arch/avx2.c:290-315
+//   inv_scale = 1 / (scale_x * w_scale)               src/arch/avx2.c:684
+// rms_norm in avx2_rms_norm's order (src/arch/avx2.c:22-83, D % 32 == 0):
+// lane j of the warp is the reference's accumulator j (four 8-wide vectors),
+// taking x[j], x[j + 32], ... by fused multiply-add; lanes combine as
+// (s[l] + s[l + 8]) + (s[l + 16] + s[l + 24]), l = 0..7, added left to right
+// from 0; rms = 1 / sqrtf(sum / D + 1e-6f); out = (x * rms) * w.
+__device__ __forceinline__ float rms_x86(const float *buf, int D, int lane) {
+    float s = 0.0f;
+#pragma unroll 8
+    for (int i = lane; i < D; i += 32) s = __fmaf_rn(buf[i], buf[i], s);
+    const float a = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 8));
+    const float t = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 16));
+    float sum = 0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, t, l));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), 1e-6f)));
+}
+
+// One warp per row; both norm weights staged once per block, the row in
+// shared memory.  xq: [B x D] int8, inv_scale: [B].
+__global__ void __launch_bounds__(RN_WARPS * 32)
+    ternary_prep_kernel(const float *x, int B, int D, const float *norm_f, const float *lmh_norm,
+                        float w_scale, int8_t *xq, float *inv_scale) {
+    extern __shared__ float4 tp_smem4[];
+    float *wl = reinterpret_cast<float *>(tp_smem4);
+    float *wf = wl + D;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *buf = wf + D + (size_t)warp * D;
+    const int D4 = D / 4;
+    for (int i = threadIdx.x; i < D4; i += blockDim.x) {
+        reinterpret_cast<float4 *>(wl)[i] = reinterpret_cast<const float4 *>(lmh_norm)[i];
+        if (norm_f) reinterpret_cast<float4 *>(wf)[i] = reinterpret_cast<const float4 *>(norm_f)[i];
+    }
+    __syncthreads();
+    for (int r = blockIdx.x * RN_WARPS + warp; r < B; r += gridDim.x * RN_WARPS) {
+        const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)r * D);
+#pragma unroll 4
+        for (int i = lane; i < D4; i += 32) reinterpret_cast<float4 *>(buf)[i] = xr[i];
+        __syncwarp();
+        if (norm_f) {
+            const float rms = rms_x86(buf, D, lane);
+            for (int i = lane; i < D; i += 32) buf[i] = __fmul_rn(__fmul_rn(buf[i], rms), wf[i]);
+            __syncwarp();
+        }
+        const float rms = rms_x86(buf, D, lane);
+        float ma = 0.0f;
+        for (int i = lane; i < D; i += 32) {
+            const float v = __fmul_rn(__fmul_rn(buf[i], rms), wl[i]);
+            buf[i] = v;
+            ma = fmaxf(ma, fabsf(v));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+        __syncwarp();
+        const float scale_x = __fdiv_rn(127.0f, __fadd_rn(ma, 1e-5f));
+        char4 *qr = reinterpret_cast<char4 *>(xq + (int64_t)r * D);
+        for (int i = lane; i < D4; i += 32) {
+            const float4 v4 = reinterpret_cast<const float4 *>(buf)[i];
+            const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+            signed char qv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float v = __fmul_rn(vv[j], scale_x);
+                v = v < 127.0f ? v : 127.0f;
+                v = -128.0f > v ? -128.0f : v;
+                qv[j] = (signed char)__float2int_rn(v);
+            }
+            qr[i] = make_char4(qv[0], qv[1], qv[2], qv[3]);
+        }
+        if (lane == 0) inv_scale[r] = __fdiv_rn(1.0f, __fmul_rn(scale_x, w_scale));
+        __syncwarp();
+    }
+}
+
+// 2-bit codes (four per byte, lowest bits first; src/quantization.c:27-31
+// decodes code c as min(c, 2) - 1) to int8 {-1, 0, 1}: 4 packed bytes in,
+// 16 weights out per step.  The packed rows are D / 4 bytes, the int8 rows D
+// bytes, so the flat byte order carries over.
+__global__ void ternary_unpack_kernel(const uint32_t *packed, int64_t n4, uint4 *w8) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t p = packed[i];
+        uint32_t o[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t c = (p >> (8 * b + 2 * j)) & 3u;
+                const uint32_t v = (uint32_t)((int)(c < 2u ? c : 2u) - 1) & 0xffu;
+                w |= v << (8 * j);
+            }
+            o[b] = w;
+        }
+        w8[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_mu;
 
@@ -328,17 +462,42 @@ cudaError_t get_encode() {
     return cudaSuccess;
 }
 
-// rows x K bf16 row-major, box BK x box_rows, 128-byte swizzle, zero fill
-cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int K, int box_rows) {
+// rows x K row-major (bf16, or int8 when i8), box of one 128-byte row of K
+// (64 bf16 / 128 int8) x box_rows, 128-byte swizzle, zero fill
+cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int K, int box_rows, bool i8) {
+    const int esz = i8 ? 1 : 2;
     const cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)K * esz};
+    const cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+    const CUresult r = g_encode(m, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                2, const_cast<void *>(base),
                                 gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// a, W: [M x K] and [N x K] K-major (int8 when row_scale is given, else bf16)
+cudaError_t launch_gemm(const void *a, const void *W, int M, int N, int K, const float *row_scale,
+                        float *out, int64_t ldo, int *err, cudaStream_t s) {
+    const bool i8 = row_scale != nullptr;
+    CUtensorMap ma, mb;
+    cudaError_t e;
+    if ((e = make_map(&ma, a, M, K, BM, i8)) != cudaSuccess) return e;
+    if ((e = make_map(&mb, W, N, K, BN, i8)) != cudaSuccess) return e;
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    if (tiles > (1LL << 30)) return cudaErrorInvalidValue;
+    const int grid = (int)(tiles < sms ? tiles : sms);
+    if (i8)
+        gemm_kernel<true><<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, row_scale, err);
+    else
+        gemm_kernel<false><<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, nullptr, err);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -346,8 +505,14 @@ cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int K, int box_
 cudaError_t prepare() {
     cudaError_t e = get_encode();
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)GEMM_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)GEMM_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(ternary_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)((RN_WARPS + 2) * RN_MAXD * sizeof(float)));
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)((RN_WARPS + 1) * RN_MAXD * sizeof(float)));
@@ -374,17 +539,45 @@ cudaError_t gemm_bf16(const uint16_t *a, const uint16_t *W, int M, int N, int K,
         return cudaErrorInvalidValue;
     cudaError_t e = get_encode();
     if (e != cudaSuccess) return e;
-    CUtensorMap ma, mb;
-    if ((e = make_map(&ma, a, M, K, BM)) != cudaSuccess) return e;
-    if ((e = make_map(&mb, W, N, K, BN)) != cudaSuccess) return e;
-    int dev = 0, sms = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-        return e;
-    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    if (tiles > (1LL << 30)) return cudaErrorInvalidValue;
-    const int grid = (int)(tiles < sms ? tiles : sms);
-    gemm_kernel<<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, err);
+    return launch_gemm(a, W, M, N, K, nullptr, out, ldo, err, s);
+}
+
+cudaError_t gemm_i8(const int8_t *a, const int8_t *W, int M, int N, int K, const float *row_scale,
+                    float *out, int64_t ldo, int *err, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (K <= 0 || K % 16 || (reinterpret_cast<uintptr_t>(a) & 15) ||
+        (reinterpret_cast<uintptr_t>(W) & 15) || ldo < N || !row_scale)
+        return cudaErrorInvalidValue;
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    return launch_gemm(a, W, M, N, K, row_scale, out, ldo, err, s);
+}
+
+cudaError_t ternary_prep(const float *x, int B, int D, const float *norm_f, const float *lmh_norm,
+                         float w_scale, int8_t *xq, float *inv_scale, cudaStream_t s) {
+    if (B <= 0) return cudaSuccess;
+    if (D <= 0 || D > RN_MAXD || D % 32 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(lmh_norm) & 15) ||
+        (norm_f && (reinterpret_cast<uintptr_t>(norm_f) & 15)) ||
+        (reinterpret_cast<uintptr_t>(xq) & 3))
+        return cudaErrorInvalidValue;
+    int grid = (B + RN_WARPS - 1) / RN_WARPS;
+    if (grid > 148 * 8) grid = 148 * 8;
+    ternary_prep_kernel<<<grid, RN_WARPS * 32, (size_t)(RN_WARPS + 2) * D * sizeof(float), s>>>(
+        x, B, D, norm_f, lmh_norm, w_scale, xq, inv_scale);
+    return cudaGetLastError();
+}
+
+cudaError_t ternary_unpack(const uint8_t *packed, int V, int D, int8_t *w8, cudaStream_t s) {
+    if (V <= 0) return cudaSuccess;
+    if (D <= 0 || D % 16 || (reinterpret_cast<uintptr_t>(packed) & 3) ||
+        (reinterpret_cast<uintptr_t>(w8) & 15))
+        return cudaErrorInvalidValue;
+    const int64_t n4 = (int64_t)V * (D / 16);
+    int64_t grid = (n4 + 255) / 256;
+    if (grid > 148 * 16) grid = 148 * 16;
+    ternary_unpack_kernel<<<(int)grid, 256, 0, s>>>(reinterpret_cast<const uint32_t *>(packed), n4,
+                                                   reinterpret_cast<uint4 *>(w8));
     return cudaGetLastError();
 }
 

@@ -43,6 +43,11 @@ struct bm_ctx {
     float *d_lm;
     size_t cap_lm;
     int lm_ready;
+    // ternary lm_head: int8 activations and per-row output scales
+    int8_t *d_q;
+    size_t cap_q;
+    float *d_isc;
+    size_t cap_isc;
 };
 
 namespace {
@@ -225,6 +230,8 @@ void bm_ctx_destroy(bm_ctx_t *c) {
     cudaFree(c->d_stats);
     cudaFree(c->d_a);
     cudaFree(c->d_lm);
+    cudaFree(c->d_q);
+    cudaFree(c->d_isc);
     if (c->stream) cudaStreamDestroy(c->stream);
     free(c);
 }
@@ -322,6 +329,73 @@ int bm_lmhead_sample_batch(bm_ctx_t *c, const float *d_hidden, int B, int d_mode
     CK(cudaSetDevice(c->device));
     if ((rc = grow(&c->d_lm, &c->cap_lm, (size_t)B * (size_t)ld)) != BM_OK) return rc;
     rc = bm_lmhead_logits(c, d_hidden, B, d_model, d_norm_w, d_W, V, c->d_lm, ld, stream);
+    if (rc != BM_OK) return rc;
+    return bm_sample_batch(c, c->d_lm, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
+                           d_uniform, d_out_id, d_out_prob, d_stats, stream);
+}
+
+int bm_ternary_unpack(bm_ctx_t *c, const uint8_t *d_packed, int V, int d_model, int8_t *d_w8,
+                      void *stream) {
+    if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    if (V < 1 || !d_packed || !d_w8)
+        return fail(BM_ERR_INVALID_ARG, "V = %d, packed and w8 must be non-NULL", V);
+    if (d_model <= 0 || d_model % 32 || d_model > 4096)
+        return fail(BM_ERR_UNSUPPORTED, "d_model = %d (needs a multiple of 32, <= 4096)", d_model);
+    if ((reinterpret_cast<uintptr_t>(d_packed) & 3) || (reinterpret_cast<uintptr_t>(d_w8) & 15))
+        return fail(BM_ERR_INVALID_ARG, "packed not 4-byte or w8 not 16-byte aligned");
+    CK(cudaSetDevice(c->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    CK(bml::ternary_unpack(d_packed, V, d_model, d_w8, s));
+    return BM_OK;
+}
+
+int bm_ternary_logits(bm_ctx_t *c, const float *d_hidden, int B, int d_model,
+                      const float *d_norm_f, const float *d_lmh_norm, const int8_t *d_w8,
+                      float w_scale, int V, float *d_logits, int64_t ld, void *stream) {
+    if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    if (B < 0 || V < 1 || ld < V)
+        return fail(BM_ERR_INVALID_ARG, "B = %d, V = %d, ld = %lld", B, V, (long long)ld);
+    if (B == 0) return BM_OK;
+    if (!d_hidden || !d_lmh_norm || !d_w8 || !d_logits)
+        return fail(BM_ERR_INVALID_ARG, "hidden, lm_head norm, w8 and logits must be non-NULL");
+    if (d_model <= 0 || d_model % 32 || d_model > 4096)
+        return fail(BM_ERR_UNSUPPORTED, "d_model = %d (needs a multiple of 32, <= 4096)", d_model);
+    if ((reinterpret_cast<uintptr_t>(d_w8) & 15) || (reinterpret_cast<uintptr_t>(d_hidden) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_lmh_norm) & 15) ||
+        (d_norm_f && (reinterpret_cast<uintptr_t>(d_norm_f) & 15)) ||
+        (reinterpret_cast<uintptr_t>(d_logits) & 3))
+        return fail(BM_ERR_INVALID_ARG,
+                    "w8 / hidden / norm weights not 16-byte or logits not 4-byte aligned");
+    if (!(w_scale == w_scale)) return fail(BM_ERR_INVALID_ARG, "w_scale is NaN");
+    CK(cudaSetDevice(c->device));
+    if (!c->lm_ready) {
+        CK(bml::prepare());
+        c->lm_ready = 1;
+    }
+    int rc = grow(&c->d_q, &c->cap_q, (size_t)B * d_model);
+    if (rc != BM_OK) return rc;
+    if ((rc = grow(&c->d_isc, &c->cap_isc, (size_t)B)) != BM_OK) return rc;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    CK(bml::ternary_prep(d_hidden, B, d_model, d_norm_f, d_lmh_norm, w_scale, c->d_q, c->d_isc, s));
+    CK(bml::gemm_i8(c->d_q, d_w8, B, V, d_model, c->d_isc, d_logits, ld, c->d_err, s));
+    return BM_OK;
+}
+
+int bm_ternary_sample_batch(bm_ctx_t *c, const float *d_hidden, int B, int d_model,
+                            const float *d_norm_f, const float *d_lmh_norm, const int8_t *d_w8,
+                            float w_scale, int V, const int32_t *d_hist,
+                            const int64_t *d_hist_off, const bm_knobs_t *d_knobs,
+                            int64_t knob_stride, const float *d_uniform, int32_t *d_out_id,
+                            float *d_out_prob, bm_row_stats_t *d_stats, void *stream) {
+    if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
+    const int64_t ld = ((int64_t)V + 3) / 4 * 4;  // 16-byte rows for the GEMM's stores
+    int rc = check_batch_args(c, d_hidden, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
+                              d_uniform, d_out_id);
+    if (rc != BM_OK || B == 0) return rc;
+    CK(cudaSetDevice(c->device));
+    if ((rc = grow(&c->d_lm, &c->cap_lm, (size_t)B * (size_t)ld)) != BM_OK) return rc;
+    rc = bm_ternary_logits(c, d_hidden, B, d_model, d_norm_f, d_lmh_norm, d_w8, w_scale, V,
+                           c->d_lm, ld, stream);
     if (rc != BM_OK) return rc;
     return bm_sample_batch(c, c->d_lm, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
                            d_uniform, d_out_id, d_out_prob, d_stats, stream);

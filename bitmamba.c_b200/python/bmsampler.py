@@ -72,6 +72,12 @@ def lib():
         L.bm_lmhead_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
                                              ctypes.c_int, _P, _P, _P, ctypes.c_int64, _P, _P,
                                              _P, _P, _P]
+        L.bm_ternary_unpack.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P]
+        L.bm_ternary_logits.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P,
+                                        ctypes.c_float, ctypes.c_int, _P, ctypes.c_int64, _P]
+        L.bm_ternary_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P,
+                                              ctypes.c_float, ctypes.c_int, _P, _P, _P,
+                                              ctypes.c_int64, _P, _P, _P, _P, _P]
         L.bm_rng_seed.argtypes = [ctypes.c_uint64]
         L.bm_rng_seed.restype = None
         L.bm_rng_next.restype = ctypes.c_uint64
@@ -178,6 +184,34 @@ class Context:
                                            c(out_prob_ptr) if out_prob_ptr else None,
                                            c(stats_ptr) if stats_ptr else None,
                                            c(stream) if stream else None))
+
+    def ternary_unpack(self, packed_ptr, V, d_model, w8_ptr, stream=None):
+        """bm_ternary_unpack on raw device pointers (ints): 2-bit codes -> int8."""
+        c = ctypes.c_void_p
+        check(lib().bm_ternary_unpack(self._c, c(packed_ptr), V, d_model, c(w8_ptr),
+                                      c(stream) if stream else None))
+
+    def ternary_logits(self, hidden_ptr, B, d_model, norm_f_ptr, lmh_norm_ptr, w8_ptr, w_scale,
+                       V, logits_ptr, ld, stream=None):
+        """bm_ternary_logits on raw device pointers (ints): the reference's final
+        RMSNorm + ternary BitLinear lm_head."""
+        c = ctypes.c_void_p
+        check(lib().bm_ternary_logits(self._c, c(hidden_ptr), B, d_model,
+                                      c(norm_f_ptr) if norm_f_ptr else None, c(lmh_norm_ptr),
+                                      c(w8_ptr), w_scale, V, c(logits_ptr), ld,
+                                      c(stream) if stream else None))
+
+    def ternary_sample(self, hidden_ptr, B, d_model, norm_f_ptr, lmh_norm_ptr, w8_ptr, w_scale,
+                       V, hist_ptr, off_ptr, knobs_ptr, knob_stride, u_ptr, out_id_ptr,
+                       out_prob_ptr=None, stats_ptr=None, stream=None):
+        """bm_ternary_sample_batch on raw device pointers (ints)."""
+        c = ctypes.c_void_p
+        check(lib().bm_ternary_sample_batch(
+            self._c, c(hidden_ptr), B, d_model, c(norm_f_ptr) if norm_f_ptr else None,
+            c(lmh_norm_ptr), c(w8_ptr), w_scale, V, c(hist_ptr) if hist_ptr else None,
+            c(off_ptr) if off_ptr else None, c(knobs_ptr), knob_stride, c(u_ptr),
+            c(out_id_ptr), c(out_prob_ptr) if out_prob_ptr else None,
+            c(stats_ptr) if stats_ptr else None, c(stream) if stream else None))
 
     def sample_host(self, logits, hist, hist_off, knobs, uniform, want_prob=True,
                     want_stats=True):

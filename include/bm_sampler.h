@@ -208,6 +208,52 @@ int bm_lmhead_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_mo
                            float *d_out_prob, bm_row_stats_t *d_stats,
                            void *stream);
 
+/* ---- the reference's ternary BitLinear lm_head feeding the sampler --------- */
+
+/*
+ * Decodes the lm_head's 2-bit ternary weights (the model file's packed
+ * layout, src/model.c:367-475 loads it; 4 codes per byte, lowest bits first,
+ * code c -> min(c, 2) - 1, src/quantization.c:27-31; rows of d_model / 4
+ * bytes) into int8 {-1, 0, 1}, V x d_model row-major, on the device: the
+ * one-time weight preparation of bm_ternary_logits.  d_model % 32 == 0;
+ * d_packed 4-byte and d_w8 16-byte aligned.  Stream-ordered.
+ */
+int bm_ternary_unpack(bm_ctx_t *ctx, const uint8_t *d_packed, int V, int d_model,
+                      int8_t *d_w8, void *stream);
+
+/*
+ * The reference's logits producer (src/model.c:1222-1262) for B rows of
+ * d_model fp32 hidden states: the final RMSNorm with d_norm_f (skipped when
+ * NULL), the BitLinear's RMSNorm with d_lmh_norm, int8 absmax quantisation
+ * (scale_x = 127 / (max|x| + 1e-5f)), the ternary product on the tensor
+ * cores with exact int32 accumulation, logits = (float) dot * (1 / (scale_x *
+ * w_scale)).  The arithmetic follows the reference's x86 AVX2 kernels
+ * (src/arch/avx2.c:22-83 norm, 276-315 quantisation, 159 output), so the
+ * logits are bit-identical to the reference's on such a host.  d_w8 comes
+ * from bm_ternary_unpack.  d_model % 32 == 0, d_model <= 4096; hidden and
+ * norm weights 16-byte aligned, logits 4-byte aligned, ld >= V.
+ * Stream-ordered; errors of the kernels show in bm_ctx_check.
+ */
+int bm_ternary_logits(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
+                      const float *d_norm_f, const float *d_lmh_norm,
+                      const int8_t *d_w8, float w_scale, int V, float *d_logits,
+                      int64_t ld, void *stream);
+
+/*
+ * bm_ternary_logits into a context-owned logits buffer, then bm_sample_batch
+ * on it: the reference's decode-step tail from the last layer's output to the
+ * next token (src/model.c:1222-1307), the sampler's arguments as in
+ * bm_sample_batch.
+ */
+int bm_ternary_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
+                            const float *d_norm_f, const float *d_lmh_norm,
+                            const int8_t *d_w8, float w_scale, int V,
+                            const int32_t *d_hist, const int64_t *d_hist_off,
+                            const bm_knobs_t *d_knobs, int64_t knob_stride,
+                            const float *d_uniform, int32_t *d_out_id,
+                            float *d_out_prob, bm_row_stats_t *d_stats,
+                            void *stream);
+
 /* ---- batched sampling, host buffers ---------------------------------------- */
 
 /*

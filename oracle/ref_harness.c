@@ -142,3 +142,72 @@ int bm_ref_sample_batch(const float *logits, int B, int V, long long ld,
     free(jobs); free(th);
     return rc ? -1 : 0;
 }
+
+/*
+ * The reference's logits producer, unmodified: the final RMSNorm
+ * (src/model.c:1225) and the ternary BitLinear lm_head (src/model.c:1257,
+ * the single-node branch), through the kernel table dispatch_init() fills
+ * for this host (AVX2 on x86-64 with AVX2+FMA, src/dispatch.c:31-38).  Row b
+ * of x [B x d] gives logits out[b * ld .. + V).  When xq_out / inv_out are
+ * given, the BitLinear's own prepare step (src/arch/avx2.c:276-318) is run
+ * once more to expose its int8 activations and 1 / (scale_x * w_scale).
+ * n_threads > 0 sizes the reference's thread pool (bm_set_threads).
+ * Returns 1 when the AVX2 kernels ran, 0 for the scalar ones.
+ */
+static pthread_once_t g_disp_once = PTHREAD_ONCE_INIT;
+static int g_pool_threads = -1;
+
+static void bm_ref_disp_init(void)
+{
+    dispatch_init();
+    init_lut();
+}
+
+int bm_ref_ternary_lmhead(const float *x, int B, int d, const float *norm_f,
+                          const float *lmh_norm, const uint8_t *packed, int V,
+                          float w_scale, float *out, long long ld, int8_t *xq_out,
+                          float *inv_out, int n_threads)
+{
+    pthread_once(&g_disp_once, bm_ref_disp_init);
+    if (n_threads > 0 && n_threads != g_pool_threads) {
+        bm_set_threads(n_threads);
+        g_pool_threads = n_threads;
+    }
+    tensor_t w;
+    memset(&w, 0, sizeof(w));
+    w.packed_data = packed;
+    w.rows = V;
+    w.cols = d;
+    w.n_elements = (size_t) V * (size_t) d;
+    w.is_bitnet = true;
+    w.scale = w_scale;
+    tensor_t nw;
+    memset(&nw, 0, sizeof(nw));
+    nw.data = lmh_norm;
+    nw.rows = 1;
+    nw.cols = d;
+    nw.n_elements = (size_t) d;
+    float *feat = malloc((size_t) d * sizeof(float));
+    float *xn = malloc((size_t) d * sizeof(float));
+    int8_t *xq = malloc((size_t) d);
+    if (!feat || !xn || !xq) {
+        free(feat); free(xn); free(xq);
+        return -1;
+    }
+    for (int b = 0; b < B; b++) {
+        const float *xr = x + (size_t) b * d;
+        if (norm_f) {
+            g_kernels.rms_norm(xr, d, norm_f, feat);
+            xr = feat;
+        }
+        g_kernels.bitlinear_forward(xr, d, &w, &nw, out + (size_t) b * ld, xn, xq);
+        if (xq_out)
+            memcpy(xq_out + (size_t) b * d, xq, (size_t) d);
+        if (inv_out && g_kernels.bitlinear_prepare) {
+            const float sx = g_kernels.bitlinear_prepare(xr, d, &nw, xn, xq);
+            inv_out[b] = 1.0f / (sx * w_scale);
+        }
+    }
+    free(feat); free(xn); free(xq);
+    return strcmp(g_kernels.name, "avx2") == 0 ? 1 : 0;
+}

@@ -263,3 +263,50 @@ def make_c5(seed: int, B: int, V: int = VOCAB, d: int = 2048, H: int = 256) -> L
           np.full(B, k["min_p"], np.float32), np.full(B, k["top_p"], np.float32),
           np.full(B, k["top_k"], np.int32))
     return LmBatch(hidden, norm_w, w_bits, hist, off, kn)
+
+
+def ternary_codes(seed: int, stream: int, V: int, d: int, raw: bool = False) -> np.ndarray:
+    """2-bit packed ternary weights [V x d/4] from the counter hash: codes 0, 1,
+    2 (-1, 0, +1) with probabilities 1/4, 1/2, 1/4 (a hash code 3 becomes 1,
+    as the exporter never writes 3); raw=True keeps the 3s (decoded as +1)."""
+    n = V * d // 4
+    h = hash_stream(seed, stream, (n + 7) // 8)
+    p = h.view(np.uint8)[:n].copy()
+    if not raw:
+        m = p & (p >> np.uint8(1)) & np.uint8(0x55)
+        p = p & ~(m << np.uint8(1))
+    return p.reshape(V, d // 4)
+
+
+class TernaryBatch:
+    """Inputs of the ternary lm_head + sampler (config c6)."""
+
+    def __init__(self, hidden, norm_f, lmh_norm, packed, w_scale, hist, hist_off, knobs):
+        self.hidden = np.ascontiguousarray(hidden, np.float32)
+        self.norm_f = np.ascontiguousarray(norm_f, np.float32)
+        self.lmh_norm = np.ascontiguousarray(lmh_norm, np.float32)
+        self.packed = np.ascontiguousarray(packed, np.uint8)
+        self.w_scale = np.float32(w_scale)
+        self.hist = np.ascontiguousarray(hist, np.int32)
+        self.hist_off = np.ascontiguousarray(hist_off, np.int64)
+        self.temp, self.penalty, self.min_p, self.top_p, self.top_k = knobs
+
+
+def make_c6(seed: int, B: int, V: int = VOCAB, d: int = 2048, H: int = 256,
+            raw: bool = False) -> TernaryBatch:
+    """c6: the reference's own logits producer: hidden N(0,1) (the last
+    layer's output), final-norm and BitLinear-norm weights 1+N(0,.02), ternary
+    W (2-bit packed, P(0) = 1/2), weight scale 16 (the exporter's 1 / mean|W|,
+    scripts/export-bin.py:172-176, for which the logits have a standard
+    deviation near 2 at d = 2048), default knobs, 256-id Zipf(1.1)
+    histories."""
+    hidden = normal(seed, 6001, B * d).astype(np.float32).reshape(B, d)
+    norm_f = (1.0 + 0.02 * normal(seed, 6002, d)).astype(np.float32)
+    lmh_norm = (1.0 + 0.02 * normal(seed, 6003, d)).astype(np.float32)
+    packed = ternary_codes(seed, 6004, V, d, raw)
+    hist, off = _csr([ids_zipf(seed, 6100 + r, H, V) for r in range(B)])
+    k = DEFAULT_KNOBS
+    kn = (np.full(B, k["temp"], np.float32), np.full(B, k["penalty"], np.float32),
+          np.full(B, k["min_p"], np.float32), np.full(B, k["top_p"], np.float32),
+          np.full(B, k["top_k"], np.int32))
+    return TernaryBatch(hidden, norm_f, lmh_norm, packed, 16.0, hist, off, kn)
