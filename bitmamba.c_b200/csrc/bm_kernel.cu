@@ -716,7 +716,16 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
     const float2 it2 = make_float2(inv_temp, inv_temp), z2 = make_float2(0.0f, 0.0f);
     auto consume = [&](int s, float4 x, unsigned valid) {
         float t[4] = {x.x, x.y, x.z, x.w};
-        if (!PEN && !GREEDY && valid == 0xfu) {
+        if (PEN) {
+            const unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
+            if (nib) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if ((nib >> q) & 1u) t[q] = penalize(t[q], penalty);
+                r4[s] = make_float4(t[0], t[1], t[2], t[3]);
+            }
+        }
+        if (!GREEDY && valid == 0xfu) {
             // whole slot: two three-input max / min, two packed checks
             float2 a = make_float2(t[0], t[1]), b = make_float2(t[2], t[3]);
             if (SCALE) { a = __fmul2_rn(a, it2); b = __fmul2_rn(b, it2); }
@@ -727,15 +736,6 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
             chk2 = __ffma2_rn(a, z2, chk2);
             chk2 = __ffma2_rn(b, z2, chk2);
             return;
-        }
-        if (PEN) {
-            const unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
-            if (nib) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    if ((nib >> q) & 1u) t[q] = penalize(t[q], penalty);
-                r4[s] = make_float4(t[0], t[1], t[2], t[3]);
-            }
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -2789,7 +2789,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             if (scale) load_pass<false, false, true>(c, mx, xmin, chk, gv, gi);
             else load_pass<false, false, false>(c, mx, xmin, chk, gv, gi);
         }
-        if (__syncthreads_or(v->fail)) {
+        // a plain barrier, then the flag from shared memory (measured faster
+        // here than a barrier reduction of the flag)
+        __syncthreads();
+        if (v->fail) {
             // a bounded wait expired: wait (bounded) for this row's copies,
             // then stop; the host sees the error flag
             if (tid == 0) {
