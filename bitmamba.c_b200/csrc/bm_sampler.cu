@@ -240,6 +240,12 @@ int bm_max_vocab(const bm_ctx_t *c) { return c ? c->max_vocab : 0; }
 
 void *bm_ctx_stream(bm_ctx_t *c) { return c ? static_cast<void *>(c->stream) : nullptr; }
 
+int bm_ctx_device(const bm_ctx_t *c, int *device) {
+    if (!c || !device) return fail(BM_ERR_INVALID_ARG, "ctx or device is NULL");
+    *device = c->device;
+    return BM_OK;
+}
+
 int bm_ctx_check(bm_ctx_t *c) {
     if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
     CK(cudaSetDevice(c->device));
@@ -602,3 +608,6 @@ int bm_sample_row(float *logits, int V, const int *history, int history_len, flo
 }
 
 }  // extern "C"
+
+// The library's error channel for the other translation units (bm_decode.cu).
+int bm_detail_fail(int code, const char *msg) { return fail(code, "%s", msg); }

@@ -43,6 +43,15 @@ assert ctypes.sizeof(Knobs) == 32 and KNOBS_DTYPE.itemsize == 32
 _lib = None
 _P = ctypes.c_void_p
 
+HISTORY_MAX = 256
+DECODE_ACTIVE, DECODE_STOP_EOS, DECODE_STOP_TOKEN, DECODE_STOP_MAX = 0, 1, 2, 3
+
+
+class DecodeViews(ctypes.Structure):
+    """bm_decode_views_t: device pointers of a decode state."""
+    _fields_ = [("ring", _P), ("ring_off", _P), ("current", _P), ("status", _P),
+                ("n_generated", _P), ("n_pushed", _P), ("n_active", _P)]
+
 
 def lib():
     global _lib
@@ -78,6 +87,18 @@ def lib():
         L.bm_ternary_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P,
                                               ctypes.c_float, ctypes.c_int, _P, _P, _P,
                                               ctypes.c_int64, _P, _P, _P, _P, _P]
+        L.bm_ctx_device.argtypes = [_P, ctypes.POINTER(ctypes.c_int)]
+        L.bm_decode_create.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int,
+                                       ctypes.POINTER(_P)]
+        L.bm_decode_destroy.argtypes = [_P]
+        L.bm_decode_reset.argtypes = [_P, _P, _P]
+        L.bm_decode_step.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int64, _P, ctypes.c_int64,
+                                     _P, _P, _P]
+        L.bm_decode_ternary_step.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, ctypes.c_float,
+                                             ctypes.c_int, _P, ctypes.c_int64, _P, _P, _P]
+        L.bm_decode_views.argtypes = [_P, ctypes.POINTER(DecodeViews)]
+        L.bm_decode_active.argtypes = [_P, _P, ctypes.POINTER(ctypes.c_int32)]
+        L.bm_decode_read.argtypes = [_P, _P, _P, _P, _P]
         L.bm_rng_seed.argtypes = [ctypes.c_uint64]
         L.bm_rng_seed.restype = None
         L.bm_rng_next.restype = ctypes.c_uint64
@@ -278,3 +299,73 @@ def header_symbols() -> list:
     txt = open(HEADER).read()
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
     return sorted(set(re.findall(r"\b(bm_[a-z0-9_]+)\s*\(", txt)))
+
+
+class Decode:
+    """A device-resident decode loop state (bm_decode_*): per-row 256-id
+    history windows, current tokens and stop status on the GPU."""
+
+    def __init__(self, ctx, B, max_tokens=0, stop_ids=()):
+        self._ctx = ctx
+        self._d = _P()
+        self.B = B
+        stop = np.ascontiguousarray(np.asarray(stop_ids, np.int32))
+        check(lib().bm_decode_create(ctx._c, B, max_tokens,
+                                     stop.ctypes.data_as(_P) if stop.size else None,
+                                     int(stop.size), ctypes.byref(self._d)))
+
+    def close(self):
+        if self._d:
+            lib().bm_decode_destroy(self._d)
+            self._d = _P()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self, prompts):
+        """prompts: one sequence of ids per row."""
+        prompts = [np.asarray(p, np.int32) for p in prompts]
+        off = np.zeros(len(prompts) + 1, np.int64)
+        off[1:] = np.cumsum([len(p) for p in prompts])
+        ids = np.ascontiguousarray(np.concatenate(prompts) if off[-1] else np.zeros(1, np.int32),
+                                   dtype=np.int32)
+        check(lib().bm_decode_reset(self._d, ids.ctypes.data_as(_P), off.ctypes.data_as(_P)))
+
+    def step(self, logits_ptr, V, ld, knobs_ptr, knob_stride, u_ptr, out_id_ptr=None,
+             stream=None):
+        c = ctypes.c_void_p
+        check(lib().bm_decode_step(self._d, c(logits_ptr), V, ld, c(knobs_ptr), knob_stride,
+                                   c(u_ptr), c(out_id_ptr) if out_id_ptr else None,
+                                   c(stream) if stream else None))
+
+    def ternary_step(self, hidden_ptr, d_model, norm_f_ptr, lmh_norm_ptr, w8_ptr, w_scale, V,
+                     knobs_ptr, knob_stride, u_ptr, out_id_ptr=None, stream=None):
+        c = ctypes.c_void_p
+        check(lib().bm_decode_ternary_step(
+            self._d, c(hidden_ptr), d_model, c(norm_f_ptr) if norm_f_ptr else None,
+            c(lmh_norm_ptr), c(w8_ptr), w_scale, V, c(knobs_ptr), knob_stride, c(u_ptr),
+            c(out_id_ptr) if out_id_ptr else None, c(stream) if stream else None))
+
+    def views(self):
+        v = DecodeViews()
+        check(lib().bm_decode_views(self._d, ctypes.byref(v)))
+        return {k: getattr(v, k) for k, _ in DecodeViews._fields_}
+
+    def read(self):
+        """The state on the host: dict of current, status, n_generated [B] and
+        ring [B x 256] (synchronises)."""
+        B = self.B
+        cur, st, ng = (np.empty(B, np.int32) for _ in range(3))
+        ring = np.empty((B, HISTORY_MAX), np.int32)
+        check(lib().bm_decode_read(self._d, cur.ctypes.data_as(_P), st.ctypes.data_as(_P),
+                                   ng.ctypes.data_as(_P), ring.ctypes.data_as(_P)))
+        return {"current": cur, "status": st, "n_generated": ng, "ring": ring}
+
+    def active(self, stream=None):
+        n = ctypes.c_int32()
+        check(lib().bm_decode_active(self._d, ctypes.c_void_p(stream) if stream else None,
+                                     ctypes.byref(n)))
+        return n.value

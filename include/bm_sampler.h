@@ -111,6 +111,9 @@ int bm_ctx_check(bm_ctx_t *ctx);
  * reference sampler is synchronous on the calling thread. */
 void *bm_ctx_stream(bm_ctx_t *ctx);
 
+/* The CUDA device ordinal the context was created on. */
+int bm_ctx_device(const bm_ctx_t *ctx, int *device);
+
 /* ---- batched sampling, device buffers -------------------------------------- */
 
 /*
@@ -253,6 +256,89 @@ int bm_ternary_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_m
                             const float *d_uniform, int32_t *d_out_id,
                             float *d_out_prob, bm_row_stats_t *d_stats,
                             void *stream);
+
+/* ---- device-resident decode loop state ------------------------------------- */
+
+/*
+ * The reference generation loop's bookkeeping kept on the GPU
+ * (src/main.c:42-50, 455-500), so that repeated decode steps run without a
+ * host round trip: per row a 256-id history window (src/main.c:19,
+ * history_push), the token the next forward step consumes, the number of
+ * tokens generated and a stop status.  A step samples every row with the
+ * window as its penalty history, then for each active row counts the token,
+ * makes it current, pushes it and stops the row on EOS (50256) or token 0
+ * (src/main.c:498-499), on a user stop token (src/chat.c:1069-1081) or at
+ * max_tokens (the loop bound, src/main.c:473; 0 = no bound).  Stopped rows
+ * are still sampled (rows are independent) but left unchanged, and their id
+ * is reported as -1.
+ *
+ * The window is a ring of BM_HISTORY_MAX slots per row (slot p % 256 holds
+ * the p-th pushed id, empty slots -1), read by the sampler as the history
+ * CSR ring[256 r .. 256 r + 256): the penalty uses the set of distinct
+ * in-range ids, so this equals the reference's shifted array.
+ */
+#define BM_HISTORY_MAX 256
+
+enum {
+    BM_DECODE_ACTIVE = 0,
+    BM_DECODE_STOP_EOS = 1,    /* sampled 50256 or 0 */
+    BM_DECODE_STOP_TOKEN = 2,  /* sampled a user stop token */
+    BM_DECODE_STOP_MAX = 3     /* max_tokens generated, or no prompt pushed yet */
+};
+
+typedef struct bm_decode bm_decode_t;
+
+/* Device views of a decode state (row-major, B rows). */
+typedef struct {
+    int32_t *ring;         /* [B x 256] history windows, -1 = empty */
+    int64_t *ring_off;     /* [B + 1] = 256 r: the windows as a history CSR */
+    int32_t *current;      /* [B] token of the next forward step */
+    int32_t *status;       /* [B] BM_DECODE_* */
+    int32_t *n_generated;  /* [B] tokens generated since the reset */
+    int32_t *n_pushed;     /* [B] ids pushed (prompt + generated) */
+    int32_t *n_active;     /* [1] rows with status BM_DECODE_ACTIVE */
+} bm_decode_views_t;
+
+/* B rows on ctx's device; every row starts stopped until bm_decode_reset.
+ * stop_ids (host, n_stop entries) may be NULL when n_stop == 0. */
+int bm_decode_create(bm_ctx_t *ctx, int B, int max_tokens, const int32_t *stop_ids,
+                     int n_stop, bm_decode_t **out);
+int bm_decode_destroy(bm_decode_t *d);
+
+/* Starts every row from its prompt (host CSR: row r's ids at
+ * h_prompt[h_prompt_off[r] .. h_prompt_off[r + 1])): pushes the prompt ids
+ * (the window keeps the last 256), current = the last prompt id (0 for an
+ * empty prompt), n_generated = 0, every row active.  Synchronous. */
+int bm_decode_reset(bm_decode_t *d, const int32_t *h_prompt, const int64_t *h_prompt_off);
+
+/* One decode step from this step's logits (B rows, as bm_sample_batch):
+ * sample with the windows as history, then update the state.  d_out_id
+ * (optional, [B]) receives the step's tokens, -1 for stopped rows.
+ * Stream-ordered (stream NULL: the context stream). */
+int bm_decode_step(bm_decode_t *d, const float *d_logits, int V, int64_t ld,
+                   const bm_knobs_t *d_knobs, int64_t knob_stride,
+                   const float *d_uniform, int32_t *d_out_id, void *stream);
+
+/* The same step from the last layer's output through the reference's final
+ * RMSNorm + ternary lm_head (bm_ternary_sample_batch). */
+int bm_decode_ternary_step(bm_decode_t *d, const float *d_hidden, int d_model,
+                           const float *d_norm_f, const float *d_lmh_norm,
+                           const int8_t *d_w8, float w_scale, int V,
+                           const bm_knobs_t *d_knobs, int64_t knob_stride,
+                           const float *d_uniform, int32_t *d_out_id, void *stream);
+
+/* Device pointers of the state (valid until bm_decode_destroy). */
+int bm_decode_views(const bm_decode_t *d, bm_decode_views_t *views);
+
+/* Copies the state to host buffers (each optional: [B] current, status,
+ * n_generated; [B x 256] ring).  Synchronises the context stream and the
+ * device; for inspection, not for the step loop. */
+int bm_decode_read(bm_decode_t *d, int32_t *h_current, int32_t *h_status,
+                   int32_t *h_n_generated, int32_t *h_ring);
+
+/* Reads the active-row count (4 bytes to pinned host memory; synchronises
+ * the stream). */
+int bm_decode_active(bm_decode_t *d, void *stream, int32_t *h_n_active);
 
 /* ---- batched sampling, host buffers ---------------------------------------- */
 
