@@ -47,6 +47,23 @@ HISTORY_MAX = 256
 DECODE_ACTIVE, DECODE_STOP_EOS, DECODE_STOP_TOKEN, DECODE_STOP_MAX = 0, 1, 2, 3
 
 
+class ModelHeadHost(ctypes.Structure):
+    """bm_model_head_host_t."""
+    _fields_ = [("vocab_size", ctypes.c_int32), ("d_model", ctypes.c_int32),
+                ("n_layers", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+                ("w_scale", ctypes.c_float), ("norm_f", ctypes.POINTER(ctypes.c_float)),
+                ("lm_head_norm", ctypes.POINTER(ctypes.c_float)),
+                ("packed", ctypes.POINTER(ctypes.c_uint8))]
+
+
+class ModelHeadInfo(ctypes.Structure):
+    """bm_model_head_info_t."""
+    _fields_ = [("vocab_size", ctypes.c_int32), ("d_model", ctypes.c_int32),
+                ("n_layers", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+                ("w_scale", ctypes.c_float), ("d_norm_f", _P), ("d_lmh_norm", _P),
+                ("d_w8", _P), ("d_packed", _P)]
+
+
 class DecodeViews(ctypes.Structure):
     """bm_decode_views_t: device pointers of a decode state."""
     _fields_ = [("ring", _P), ("ring_off", _P), ("current", _P), ("status", _P),
@@ -99,6 +116,13 @@ def lib():
         L.bm_decode_views.argtypes = [_P, ctypes.POINTER(DecodeViews)]
         L.bm_decode_active.argtypes = [_P, _P, ctypes.POINTER(ctypes.c_int32)]
         L.bm_decode_read.argtypes = [_P, _P, _P, _P, _P]
+        L.bm_model_head_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ModelHeadHost)]
+        L.bm_model_head_host_free.argtypes = [ctypes.POINTER(ModelHeadHost)]
+        L.bm_model_head_host_free.restype = None
+        L.bm_model_head_load.argtypes = [_P, ctypes.c_char_p, ctypes.POINTER(_P)]
+        L.bm_model_head_info.argtypes = [_P, ctypes.POINTER(ModelHeadInfo)]
+        L.bm_model_head_free.argtypes = [_P]
+        L.bm_model_head_free.restype = None
         L.bm_rng_seed.argtypes = [ctypes.c_uint64]
         L.bm_rng_seed.restype = None
         L.bm_rng_next.restype = ctypes.c_uint64
@@ -369,3 +393,42 @@ class Decode:
         check(lib().bm_decode_active(self._d, ctypes.c_void_p(stream) if stream else None,
                                      ctypes.byref(n)))
         return n.value
+
+
+def read_model_head(path):
+    """bm_model_head_read (host only): the decode tail's tensors of a packed
+    model file as numpy arrays."""
+    h = ModelHeadHost()
+    check(lib().bm_model_head_read(os.fsencode(path), ctypes.byref(h)))
+    try:
+        d, V = h.d_model, h.vocab_size
+        pk = V * ((d + 3) // 4)
+        return {"vocab_size": V, "d_model": d, "n_layers": h.n_layers, "n_heads": h.n_heads,
+                "w_scale": h.w_scale,
+                "norm_f": np.ctypeslib.as_array(h.norm_f, (d,)).copy(),
+                "lm_head_norm": np.ctypeslib.as_array(h.lm_head_norm, (d,)).copy(),
+                "packed": np.ctypeslib.as_array(h.packed, (pk,)).copy().reshape(V, -1)}
+    finally:
+        lib().bm_model_head_host_free(ctypes.byref(h))
+
+
+class ModelHead:
+    """bm_model_head_load: the decode tail's tensors on the device."""
+
+    def __init__(self, ctx, path):
+        self._h = _P()
+        check(lib().bm_model_head_load(ctx._c, os.fsencode(path), ctypes.byref(self._h)))
+        i = ModelHeadInfo()
+        check(lib().bm_model_head_info(self._h, ctypes.byref(i)))
+        self.info = {k: getattr(i, k) for k, _ in ModelHeadInfo._fields_}
+
+    def close(self):
+        if self._h:
+            lib().bm_model_head_free(self._h)
+            self._h = _P()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -340,6 +340,49 @@ int bm_decode_read(bm_decode_t *d, int32_t *h_current, int32_t *h_status,
  * the stream). */
 int bm_decode_active(bm_decode_t *d, void *stream, int32_t *h_n_active);
 
+/* ---- model file: the decode tail's tensors --------------------------------- */
+
+/*
+ * Reads jserv/bitmamba.c's packed model file (magic 0x42495432; written by
+ * scripts/export-bin.py:110-200, loaded by src/model.c:477-783) for the
+ * tensors the decode tail needs: norm_f, lm_head.norm and the ternary
+ * lm_head with its scale.  The file is walked tensor by tensor, as the
+ * reference loader does, with the loader's checks (header bounds, per-tensor
+ * bounds, shapes and float / packed types); a malformed file fails with
+ * BM_ERR_INVALID_ARG and bm_last_error naming the check.
+ */
+typedef struct {
+    int32_t vocab_size, d_model, n_layers, n_heads;
+    float w_scale;          /* lm_head scale (the exporter's 1 / mean|W|) */
+    float *norm_f;          /* [d_model] */
+    float *lm_head_norm;    /* [d_model] */
+    uint8_t *packed;        /* [vocab_size x (d_model + 3) / 4] 2-bit codes */
+} bm_model_head_host_t;
+
+/* Host only (no GPU needed): fills *out with copies; free with
+ * bm_model_head_host_free. */
+int bm_model_head_read(const char *path, bm_model_head_host_t *out);
+void bm_model_head_host_free(bm_model_head_host_t *h);
+
+typedef struct bm_model_head bm_model_head_t;
+
+typedef struct {
+    int32_t vocab_size, d_model, n_layers, n_heads;
+    float w_scale;
+    const float *d_norm_f;      /* [d_model] on the device */
+    const float *d_lmh_norm;    /* [d_model] */
+    const int8_t *d_w8;         /* [vocab_size x d_model] decoded ternary weights */
+    const uint8_t *d_packed;    /* [vocab_size x d_model / 4] as stored */
+} bm_model_head_info_t;
+
+/* Reads the file, uploads the tensors to ctx's device and decodes the
+ * ternary weights (bm_ternary_unpack), ready for bm_ternary_logits /
+ * bm_ternary_sample_batch / bm_decode_ternary_step.  d_model must be a
+ * multiple of 32 (<= 4096), else BM_ERR_UNSUPPORTED.  Synchronous. */
+int bm_model_head_load(bm_ctx_t *ctx, const char *path, bm_model_head_t **out);
+int bm_model_head_info(const bm_model_head_t *head, bm_model_head_info_t *info);
+void bm_model_head_free(bm_model_head_t *head);
+
 /* ---- batched sampling, host buffers ---------------------------------------- */
 
 /*

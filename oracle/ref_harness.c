@@ -211,3 +211,37 @@ int bm_ref_ternary_lmhead(const float *x, int B, int d, const float *norm_f,
     free(feat); free(xn); free(xq);
     return strcmp(g_kernels.name, "avx2") == 0 ? 1 : 0;
 }
+
+/*
+ * The reference's own model loader (src/model.c:477-783) on a packed model
+ * file, then its logits producer on caller-supplied last-layer outputs: the
+ * final RMSNorm and the ternary lm_head read from the loaded model
+ * (src/model.c:1225, 1257).  Returns -1 when model_load rejects the file,
+ * else the vocabulary size; *d_model_out receives d_model.  `out` holds
+ * B x ld floats (ld >= vocab).
+ */
+int bm_ref_model_lmhead(const char *path, const float *x, int B, float *out, long long ld,
+                        int *d_model_out)
+{
+    pthread_once(&g_disp_once, bm_ref_disp_init);
+    bitmamba_model_t m;
+    memset(&m, 0, sizeof(m));
+    if (!model_load(&m, path))
+        return -1;
+    const int d = m.config.d_model, V = m.config.vocab_size;
+    if (d_model_out)
+        *d_model_out = d;
+    if (x && out) {
+        float *feat = malloc((size_t) d * sizeof(float));
+        float *xn = malloc((size_t) d * sizeof(float));
+        int8_t *xq = malloc((size_t) d);
+        for (int b = 0; feat && xn && xq && b < B; b++) {
+            g_kernels.rms_norm(x + (size_t) b * d, d, m.norm_f.data, feat);
+            g_kernels.bitlinear_forward(feat, d, &m.lm_head, &m.lm_head_norm,
+                                        out + (size_t) b * ld, xn, xq);
+        }
+        free(feat); free(xn); free(xq);
+    }
+    model_free(&m);
+    return V;
+}
