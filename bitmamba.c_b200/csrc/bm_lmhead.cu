@@ -8,7 +8,7 @@
 //   gemm      logits[r, n] = sum_k a[r, k] * W[n, k] in 128 x 256 output
 //             tiles on persistent CTAs (one per SM): a TMA producer thread
 //             streams 128 x 64 (a) and 256 x 64 (W) bf16 tiles with 128-byte
-//             swizzle through a 4-stage shared-memory ring (no multicast),
+//             swizzle through a 4-stage shared-memory ring (plain loads),
 //             one thread issues tcgen05.mma (kind::f16, M=128, N=256, K=16)
 //             into one of two 256-column fp32 accumulators in tensor memory
 //             and frees each stage with tcgen05.commit; four warps drain the
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
     }
     return false;
 }
-// 2-D tiled TMA load (no multicast): box at (x = k, y = row) into smem
+// 2-D tiled TMA load into this CTA only: box at (x = k, y = row) into smem
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
     asm volatile(
