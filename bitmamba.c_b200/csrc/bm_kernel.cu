@@ -741,7 +741,9 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         for (int q = 0; q < 4; ++q) {
             if (!((valid >> q) & 1u)) continue;
             if (GREEDY) {
-                if (t[q] > gv) { gv = t[q]; gi = 4 * s + q - sh; }
+                // (the ragged head slot comes last: ties keep the lower id)
+                const int e = 4 * s + q - sh;
+                if (t[q] > gv || (t[q] == gv && gi != INT_MAX && e < gi)) { gv = t[q]; gi = e; }
             } else {
                 const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
                 if (l > mx) gi = s;
@@ -791,6 +793,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         for (int s = threadIdx.x; s < nslots; s += NT) plain(s);
     }
     // interior, chunk by chunk
+    bool ok = true;
     if (nint > 0) {
         for (int ch = 0; ch < NCHUNK; ++ch) {
             const int a = s0 + (ch * nint) / NCHUNK, b = s0 + ((ch + 1) * nint) / NCHUNK;
@@ -799,14 +802,15 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
             if (!mbar_wait(&c.mbar[ch], c.parity)) {
                 atomicOr(c.err, 1);
                 v->fail = 1;
-                return;
+                ok = false;
+                break;
             }
             for (; s < b; s += NT) consume(s, r4[s], 0xfu);
         }
     }
     if (es >= 0) {
         cp_async_wait_all();
-        consume(es, r4[es], evld);
+        if (ok) consume(es, r4[es], evld);
     }
     chk = __fadd_rn(chk, __fadd_rn(chk2.x, chk2.y));
 }

@@ -102,3 +102,32 @@ def test_large_batches(gpu_ctx, sampler_lib, oracle_lib, name, rows):
     b = synth.MAKERS[name](303, rows)
     u = synth.uniform(303, 9, rows).astype(np.float32)
     _run(gpu_ctx, sampler_lib, oracle_lib, b, u, name)
+
+
+@pytest.mark.parametrize("variant", ["plain", "both_penalised", "other_penalised"])
+def test_greedy_ties_in_the_ragged_head(gpu_ctx, sampler_lib, oracle_lib, variant):
+    """Greedy rows whose maximum is shared by an id in the ragged head slot
+    (ids 0-2 of a row whose base is not 16-byte aligned, consumed after the
+    interior) and a later id: the lower id wins (src/model.c:144-154), with
+    and without those ids penalised."""
+    B = 16
+    z = synth.normal(12, 1, B * V).reshape(B, V).astype(np.float32)
+    hist = []
+    for r in range(B):
+        z[r, r % 3] = np.float32(9.0)
+        z[r, 1000 + 37 * r] = np.float32(9.0)
+        if variant == "both_penalised":
+            hist.append(np.array([r % 3, 1000 + 37 * r, 5], np.int32))
+        elif variant == "other_penalised":
+            hist.append(np.array([7, 4000 + r], np.int32))
+        else:
+            hist.append(np.zeros(0, np.int32))
+    off = np.zeros(B + 1, np.int64)
+    off[1:] = np.cumsum([len(h) for h in hist])
+    full = lambda x, t: np.full(B, x, t)
+    b = synth.Batch(z, np.concatenate(hist), off, full(0.0, np.float32),
+                    full(1.0 if variant == "plain" else 1.5, np.float32), full(0.0, np.float32),
+                    full(0.9, np.float32), full(0, np.int32))
+    u = synth.uniform(12, 2, B).astype(np.float32)
+    rep = _run(gpu_ctx, sampler_lib, oracle_lib, b, u, "greedy ties " + variant)
+    assert rep["exact"] == B
