@@ -696,6 +696,126 @@ def run_lmhead(args):
     return 0
 
 
+def run_decode(args):
+    """Config c7: the device-resident decode loop (bm_decode_ternary_step):
+    B rows per GPU, K steps per timed iteration, each step the reference's
+    final RMSNorm + ternary lm_head + sampler with the 256-id history windows,
+    then the loop state update (push, stop checks) on the GPU.  The hidden
+    state is held fixed (the model's layers are out of scope), so each step
+    differs only through the windows.  Reported against the same steps with a
+    host round trip per step (ids copied to the host and the stream
+    synchronised), which a host-side loop needs."""
+    import torch
+    import bmsampler as bm
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (no CPU fallback)")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    sys.path[:0] = [os.path.join(ROOT, "tests", "golden")]
+    import synth
+    B, V, d, K = args.B, args.V, args.d_model, args.decode_steps
+    dev = torch.device("cuda", local)
+    ctx = bm.Context(local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(777 + rank)
+    hidden = torch.randn(B, d, generator=g, device=dev, dtype=torch.float32)
+    nf = 1.0 + 0.02 * torch.randn(d, generator=g, device=dev, dtype=torch.float32)
+    nl = 1.0 + 0.02 * torch.randn(d, generator=g, device=dev, dtype=torch.float32)
+    pk = torch.randint(0, 256, (V, d // 4), generator=g, device=dev, dtype=torch.int32)
+    packed = (pk & ~((pk & (pk >> 1) & 0x55) << 1)).to(torch.uint8).contiguous()
+    del pk
+    W = torch.empty((V, d), dtype=torch.int8, device=dev)
+    ctx.ternary_unpack(packed.data_ptr(), V, d, W.data_ptr())
+    k = synth.DEFAULT_KNOBS
+    knobs = bm.knobs_array(k["temp"], k["penalty"], k["min_p"], k["top_p"], k["top_k"])
+    knobs_d = torch.from_numpy(knobs.view(np.uint8).copy()).to(dev)
+    steps_total = (args.warmup + args.steps) * K
+    u_d = torch.rand(steps_total * B, generator=g, device=dev, dtype=torch.float32)
+    ids_d = torch.empty(B, dtype=torch.int32, device=dev)
+    ids_h = torch.empty(B, dtype=torch.int32).pin_memory()
+    prompts = [synth.ids_zipf(31 + rank, 7000 + r, 64, V) for r in range(B)]
+    dec = bm.Decode(ctx, B, max_tokens=0, stop_ids=[])
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)
+    st = [0]
+
+    def step(host_round_trip):
+        u = u_d[st[0] * B:(st[0] + 1) * B]
+        st[0] += 1
+        dec.ternary_step(hidden.data_ptr(), d, nf.data_ptr(), nl.data_ptr(), W.data_ptr(), 16.0,
+                         V, knobs_d.data_ptr(), 0, u.data_ptr(), ids_d.data_ptr(),
+                         stream.cuda_stream)
+        if host_round_trip:
+            with torch.cuda.stream(stream):
+                ids_h.copy_(ids_d, non_blocking=True)
+            stream.synchronize()
+
+    def run(host_round_trip, iters):
+        dec.reset(prompts)
+        st[0] = 0
+        for _ in range(args.warmup * K):
+            step(host_round_trip)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters * K):
+            step(host_round_trip)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        return max_over_ranks(dist, e0.elapsed_time(e1), dev) / (iters * K)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    t_a = time.time()
+    ms = run(False, args.steps)
+    t_b = time.time()
+    clocks.window = (t_a, t_b)
+    ms_rt = run(True, args.steps)
+    time.sleep(0.25)
+    clocks.stop()
+    ctx.check()
+    active = dec.active()
+    dec.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "sampled tokens/s, device-resident decode loop (c7: ternary lm_head + "
+                  "sampler + history / stop state per step)",
+        "value": world * B / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 x ternary GEMM (exact int32), f32 sampler",
+        "data": "synthetic",
+        "config": {"workload": "c7 decode loop: c6 inputs held fixed, 64-id Zipf prompts, "
+                               "default knobs, no stop tokens", "B_per_gpu": B, "V": V,
+                   "d_model": d, "decode_steps_per_iteration": K},
+        "host_round_trip": {"ms_per_step": ms_rt, "tokens_per_s": world * B / (ms_rt / 1e3),
+                            "note": "the same steps with the ids copied to pinned host memory "
+                                    "and the stream synchronised after each step"},
+        "rows_active_at_end": active, "cpu_baseline": None, "e2e": None,
+        "clocks": clocks.summary(), "gpu_launches": 4 * K * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def ternary_cpu_leg(args, hidden, norm_f, lmh_norm, packed, w_scale, logits, hist_h, off_h,
                     u_host, ids_dev, B, V, d):
     """c6's CPU leg on a bounded sample: the reference's own final RMSNorm +
@@ -746,11 +866,15 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "c6"], default="c3",
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "c6", "c7"],
+                    default="c3",
                     help="c3 is the benchmark; the others report the other configs "
                          "(c5: the fused bf16 lm_head + sampler step; c6: the reference's "
-                         "ternary lm_head + sampler)")
+                         "ternary lm_head + sampler; c7: the device-resident decode "
+                         "loop)")
     ap.add_argument("--d-model", type=int, default=2048)
+    ap.add_argument("--decode-steps", type=int, default=16,
+                    help="c7: decode steps per timed iteration")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -758,6 +882,8 @@ def main():
         return run_reference(args)
     if args.workload in ("c5", "c6"):
         return run_lmhead(args)
+    if args.workload == "c7":
+        return run_decode(args)
     return run_ours(args)
 
 
