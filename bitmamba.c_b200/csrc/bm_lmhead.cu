@@ -73,6 +73,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
     }
     return false;
 }
+// 16-byte asynchronous global -> shared copy (every copy of a row in flight
+// at once), and the wait for this thread's copies
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_own() {
+    asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
+}
 // 2-D tiled TMA load into this CTA only: box at (x = k, y = row) into smem
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
@@ -315,8 +323,8 @@ __global__ void __launch_bounds__(RN_WARPS * 32)
     __syncthreads();
     for (int r = blockIdx.x * RN_WARPS + warp; r < B; r += gridDim.x * RN_WARPS) {
         const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)r * D);
-#pragma unroll 4
-        for (int i = lane; i < D4; i += 32) reinterpret_cast<float4 *>(buf)[i] = xr[i];
+        for (int i = lane; i < D4; i += 32) cp_async16(buf + 4 * i, xr + i);
+        cp_async_wait_own();
         __syncwarp();
         float s = 0.0f;
         if (lane < 4) {
@@ -385,8 +393,8 @@ __global__ void __launch_bounds__(RN_WARPS * 32)
     __syncthreads();
     for (int r = blockIdx.x * RN_WARPS + warp; r < B; r += gridDim.x * RN_WARPS) {
         const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)r * D);
-#pragma unroll 4
-        for (int i = lane; i < D4; i += 32) reinterpret_cast<float4 *>(buf)[i] = xr[i];
+        for (int i = lane; i < D4; i += 32) cp_async16(buf + 4 * i, xr + i);
+        cp_async_wait_own();
         __syncwarp();
         if (norm_f) {
             const float rms = rms_x86(buf, D, lane);
