@@ -855,6 +855,67 @@ def ternary_cpu_leg(args, hidden, norm_f, lmh_norm, packed, w_scale, logits, his
     return cpu, par
 
 
+def run_row_latency(args):
+    """c1 as the reference's decode loop calls its sampler: one row per step
+    through bm_sample_row, the drop-in for the tail of model_forward_step
+    (src/model.c:1268-1307): host logits and history, the global XorShift64*
+    stream, the id returned.  Each call is synchronous and includes its
+    host-to-device and device-to-host copies, so it is timed on the host
+    clock (time.perf_counter around the ctypes call).  Beside it the
+    reference's own sampler (oracle/_ref, else the oracle port) runs on one
+    host thread over the same rows and uniforms, as the reference's CLI runs
+    it; the ids of the two are compared."""
+    import torch  # noqa: F401  (the library makes its own context on device 0)
+    import bmsampler as bm
+    sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests", "golden")]
+    import synth
+    V, n = args.V, 256
+    b = synth.MAKERS["c1"](1000, n, V=V)
+    rows = [np.ascontiguousarray(b.logits[r]) for r in range(n)]
+    hists = [np.ascontiguousarray(b.hist[b.hist_off[r]:b.hist_off[r + 1]]) for r in range(n)]
+    knobs = [(float(b.penalty[r]), float(b.temp[r]), float(b.min_p[r]), float(b.top_p[r]),
+              int(b.top_k[r])) for r in range(n)]
+
+    def call(r):
+        return bm.sample_row(rows[r], hists[r], *knobs[r])
+
+    for w in range(args.warmup):
+        call(w % n)
+    steps = args.steps
+    bm.rng_seed(RNG_SEED)
+    ids = np.empty(steps, np.int32)
+    lat = np.empty(steps)
+    for s in range(steps):
+        t = time.perf_counter()
+        ids[s] = call(s % n)
+        lat[s] = time.perf_counter() - t
+    # the uniforms those calls drew (every c1 row draws: temp 0.8)
+    bm.rng_seed(RNG_SEED)
+    u = np.array([bm.rng_float() for _ in range(n)], np.float32)
+    best = None
+    for _ in range(3):
+        ref_ids, dt, kind = cpu_leg(b, u, 1)
+        best = dt if best is None else min(best, dt)
+    m = min(n, steps)
+    same = int((ref_ids[:m] == ids[:m]).sum())
+    line = {
+        "metric": "bm_sample_row latency, one row per call (c1 row, host buffers)",
+        "value": float(np.median(lat) * 1e6), "unit": "us", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "higher_is_better": False, "dtype": "f32",
+        "data": "synthetic", "p99_us": float(np.percentile(lat, 99) * 1e6),
+        "mean_us": float(lat.mean() * 1e6),
+        "config": {"workload": "c1row: " + CONFIG_DESC["c1"] + "; one row per call through "
+                               "bm_sample_row, rows cycled from a pool of 256",
+                   "V": V, "history_ids": 400},
+        "cpu_baseline": {"value": best / n * 1e6, "unit": "us per row", "cores": 1,
+                         "kind": kind, "sample": f"the pool's {n} rows, best of 3 passes"},
+        "identical_ids": f"{same}/{m}",
+        "gpu_launches": steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -866,12 +927,14 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "c6", "c7"],
+    ap.add_argument("--workload",
+                    choices=["c1", "c2", "c3", "c4", "c5", "c6", "c7", "c1row"],
                     default="c3",
                     help="c3 is the benchmark; the others report the other configs "
                          "(c5: the fused bf16 lm_head + sampler step; c6: the reference's "
                          "ternary lm_head + sampler; c7: the device-resident decode "
-                         "loop)")
+                         "loop; c1row: per-call latency of bm_sample_row on one c1 row "
+                         "beside the reference's sampler on one thread)")
     ap.add_argument("--d-model", type=int, default=2048)
     ap.add_argument("--decode-steps", type=int, default=16,
                     help="c7: decode steps per timed iteration")
@@ -884,6 +947,8 @@ def main():
         return run_lmhead(args)
     if args.workload == "c7":
         return run_decode(args)
+    if args.workload == "c1row":
+        return run_row_latency(args)
     return run_ours(args)
 
 

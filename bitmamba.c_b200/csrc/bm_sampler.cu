@@ -48,6 +48,12 @@ struct bm_ctx {
     size_t cap_q;
     float *d_isc;
     size_t cap_isc;
+    // small host-buffer calls: one pinned host region and its device mirror,
+    // laid out [words | outputs | inputs]; uploaded whole, [words | outputs]
+    // read back (one copy each way, one synchronisation)
+    unsigned char *h_stage;
+    unsigned char *d_stage;
+    size_t cap_stage;
 };
 
 namespace {
@@ -232,6 +238,8 @@ void bm_ctx_destroy(bm_ctx_t *c) {
     cudaFree(c->d_lm);
     cudaFree(c->d_q);
     cudaFree(c->d_isc);
+    cudaFree(c->d_stage);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
     if (c->stream) cudaStreamDestroy(c->stream);
     free(c);
 }
@@ -443,6 +451,87 @@ int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,
     return BM_OK;
 }
 
+namespace {
+
+// Host-buffer calls whose staged bytes fit STAGE_MAX (B = 1 is 201 KB at
+// V = 50257): every input is packed into one pinned host region together with
+// a zeroed error / row-schedule word group for the launch, uploaded with one
+// copy, and the word group and outputs come back with one copy, so a call
+// costs two copies, one launch and one synchronisation instead of a copy per
+// buffer (pageable copies each wait for the host) and a separate read of the
+// context's error word.
+constexpr size_t STAGE_MAX = size_t(16) << 20;
+constexpr size_t r16h(size_t x) { return (x + 15) & ~size_t(15); }
+
+int sample_host_small(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t ld,
+                      const int32_t *h_hist, const int64_t *h_hist_off,
+                      const bm_knobs_t *h_knobs, int64_t knob_stride, const float *h_uniform,
+                      int32_t *h_out_id, float *h_out_prob, bm_row_stats_t *h_stats,
+                      size_t nk, int64_t h1, size_t o_id, size_t o_prob, size_t o_st,
+                      size_t o_in, size_t o_log, size_t o_kn, size_t o_u, size_t o_h,
+                      size_t o_off, size_t total) {
+    const size_t rows = (size_t)B;
+    cudaStream_t s = c->stream;
+    if (total > c->cap_stage) {
+        CK(cudaStreamSynchronize(s));
+        cudaFree(c->d_stage);
+        if (c->h_stage) cudaFreeHost(c->h_stage);
+        c->d_stage = nullptr;
+        c->h_stage = nullptr;
+        c->cap_stage = 0;
+        const size_t n = total + total / 4 + 256;
+        cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&c->d_stage), n);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(small staging)");
+        e = cudaHostAlloc(reinterpret_cast<void **>(&c->h_stage), n, cudaHostAllocDefault);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(small staging)");
+        c->cap_stage = n;
+    }
+    // (every call leaves the stream idle, so no copy still reads the region)
+    unsigned char *h = c->h_stage, *d = c->d_stage;
+    memset(h, 0, 16);  // error word and the two row-schedule counters
+    memcpy(h + o_log, h_logits, rows * (size_t)ld * sizeof(float));
+    memcpy(h + o_kn, h_knobs, nk * sizeof(bm_knobs_t));
+    memcpy(h + o_u, h_uniform, rows * sizeof(float));
+    if (h_hist) {
+        if (h1 > 0) memcpy(h + o_h, h_hist, (size_t)h1 * sizeof(int32_t));
+        memcpy(h + o_off, h_hist_off, (rows + 1) * sizeof(int64_t));
+    }
+    CK(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, s));
+    bmk::Params p;
+    p.logits = reinterpret_cast<const float *>(d + o_log);
+    p.ld = ld;
+    p.B = B;
+    p.V = V;
+    p.hist = h_hist ? reinterpret_cast<const int32_t *>(d + o_h) : nullptr;
+    p.hist_off = h_hist ? reinterpret_cast<const int64_t *>(d + o_off) : nullptr;
+    p.knobs = reinterpret_cast<const bm_knobs_t *>(d + o_kn);
+    p.knob_stride = knob_stride;
+    p.uniform = reinterpret_cast<const float *>(d + o_u);
+    p.out_id = reinterpret_cast<int32_t *>(d + o_id);
+    p.out_prob = h_out_prob ? reinterpret_cast<float *>(d + o_prob) : nullptr;
+    p.stats = h_stats ? reinterpret_cast<bm_row_stats_t *>(d + o_st) : nullptr;
+    p.err = reinterpret_cast<int *>(d);
+    p.sched = reinterpret_cast<int *>(d) + 1;
+    const int grid = B < c->sms ? B : c->sms;
+    cudaError_t e = bmk::launch(p, grid, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h, d, o_in, cudaMemcpyDeviceToHost, s);
+    // synchronise on the failure path too: the upload may still read the region
+    const cudaError_t es = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "small host-buffer call");
+    if (es != cudaSuccess) return cuda_fail(es, "cudaStreamSynchronize");
+    int err = 0;
+    memcpy(&err, h, sizeof(int));
+    if (err)
+        return fail(BM_ERR_DEVICE, "device error flag 0x%x (bounded wait expired or select "
+                                   "did not converge)", err);
+    memcpy(h_out_id, h + o_id, rows * sizeof(int32_t));
+    if (h_out_prob) memcpy(h_out_prob, h + o_prob, rows * sizeof(float));
+    if (h_stats) memcpy(h_stats, h + o_st, rows * sizeof(bm_row_stats_t));
+    return BM_OK;
+}
+
+}  // namespace
+
 int bm_sample_batch_host(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t ld,
                          const int32_t *h_hist, const int64_t *h_hist_off,
                          const bm_knobs_t *h_knobs, int64_t knob_stride,
@@ -454,6 +543,26 @@ int bm_sample_batch_host(bm_ctx_t *c, const float *h_logits, int B, int V, int64
     CK(cudaSetDevice(c->device));
     cudaStream_t s = c->stream;
     const size_t rows = (size_t)B;
+    {
+        const size_t nk = knob_stride ? rows : 1;
+        int64_t h1 = 0;
+        if (h_hist) {
+            const int64_t h0 = h_hist_off[0];
+            h1 = h_hist_off[B];
+            if (h0 < 0 || h1 < h0) return fail(BM_ERR_INVALID_ARG, "hist_off not monotone");
+        }
+        const size_t o_id = 16, o_prob = o_id + r16h(rows * 4), o_st = o_prob + r16h(rows * 4);
+        const size_t o_in = o_st + r16h(rows * sizeof(bm_row_stats_t));
+        const size_t o_log = o_in, o_kn = o_log + r16h(rows * (size_t)ld * 4);
+        const size_t o_u = o_kn + r16h(nk * sizeof(bm_knobs_t)), o_h = o_u + r16h(rows * 4);
+        const size_t o_off = o_h + (h_hist ? r16h((size_t)h1 * 4) : 0);
+        const size_t total = o_off + (h_hist ? r16h((rows + 1) * 8) : 0);
+        if (total <= STAGE_MAX)
+            return sample_host_small(c, h_logits, B, V, ld, h_hist, h_hist_off, h_knobs,
+                                     knob_stride, h_uniform, h_out_id, h_out_prob, h_stats, nk,
+                                     h1, o_id, o_prob, o_st, o_in, o_log, o_kn, o_u, o_h, o_off,
+                                     total);
+    }
     if ((rc = grow(&c->d_logits, &c->cap_logits, rows * (size_t)ld)) != BM_OK) return rc;
     if (rows > c->cap_rows) {
         // the four per-row buffers share one capacity

@@ -390,7 +390,10 @@ void bm_model_head_free(bm_model_head_t *head);
  * inputs to the context's device staging buffers, samples, copies ids (and
  * probabilities / stats when non-NULL) back, and synchronises.  Host buffers
  * may be pageable or pinned (pinned is faster).  h_hist_off may be NULL with
- * h_hist NULL.
+ * h_hist NULL.  Calls whose buffers total at most 16 MB (B = 1 through about
+ * 80 rows at V = 50257) pack every input into one pinned staging region of
+ * the context (grown on demand), so they make one copy each way and one
+ * synchronisation.
  */
 int bm_sample_batch_host(bm_ctx_t *ctx, const float *h_logits, int B, int V,
                          int64_t ld, const int32_t *h_hist,
