@@ -176,3 +176,38 @@ def test_invalid_arguments_rejected(gpu_ctx, sampler_lib):
     with pytest.raises(sampler_lib.BmError) as e:
         gpu_ctx.sample_host(x[None, :], None, None, k, np.zeros(1, np.float32))
     assert e.value.code == -4
+
+
+def test_host_calls_small_and_large_match_device_call(gpu_ctx, sampler_lib):
+    """bm_sample_batch_host packs calls of at most 16 MB into one pinned
+    staging region (one copy each way) and stages larger ones buffer by
+    buffer.  Both must return exactly what bm_sample_batch returns on device
+    buffers: 1 and 60 rows (small), 90 rows (18 MB: large), then 1 and 3
+    rows again after the staging region grew, with per-row knobs and
+    histories."""
+    import torch
+    dev = torch.device("cuda", 0)
+    b = synth.make_c4(606, 90)
+    u_all = synth.uniform(606, 7, 90).astype(np.float32)
+    for n in (1, 60, 90, 1, 3):
+        sub = b.rows(np.arange(n))
+        u = u_all[:n]
+        kn = knobs_of(sampler_lib, sub)
+        ids, probs, st = gpu_ctx.sample_host(sub.logits, sub.hist, sub.hist_off, kn, u)
+        lg = torch.from_numpy(sub.logits).to(dev)
+        hist = torch.from_numpy(sub.hist if sub.hist.size else np.zeros(1, np.int32)).to(dev)
+        off = torch.from_numpy(sub.hist_off).to(dev)
+        knd = torch.from_numpy(kn.view(np.uint8).copy()).to(dev)
+        ud = torch.from_numpy(u).to(dev)
+        out = torch.empty(n, dtype=torch.int32, device=dev)
+        prob = torch.empty(n, dtype=torch.float32, device=dev)
+        std = torch.zeros(n * 4, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        gpu_ctx.sample_device(lg.data_ptr(), n, sub.V, sub.V, hist.data_ptr(), off.data_ptr(),
+                              knd.data_ptr(), 1 if n > 1 else 0, ud.data_ptr(),
+                              out.data_ptr(), prob.data_ptr(), std.data_ptr(), None)
+        gpu_ctx.check()
+        assert np.array_equal(ids, out.cpu().numpy()), f"n={n}: ids"
+        assert np.array_equal(probs.view(np.uint32), prob.cpu().numpy().view(np.uint32)), \
+            f"n={n}: probabilities"
+        assert np.array_equal(st.view(np.int32).reshape(-1), std.cpu().numpy()), f"n={n}: stats"
