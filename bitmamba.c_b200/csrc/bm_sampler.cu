@@ -463,14 +463,36 @@ namespace {
 constexpr size_t STAGE_MAX = size_t(16) << 20;
 constexpr size_t r16h(size_t x) { return (x + 15) & ~size_t(15); }
 
+// Byte offsets of the staging region's sections (16-byte aligned):
+// [words 16 B | ids | probabilities | stats | logits | knobs | uniforms |
+//  history ids | history offsets]; `o_in` is where the inputs start.
+struct StageLayout {
+    size_t o_id, o_prob, o_st, o_in, o_log, o_kn, o_u, o_h, o_off, total;
+};
+StageLayout stage_layout(size_t rows, int64_t ld, size_t nk, int64_t h1, bool hist) {
+    StageLayout L;
+    L.o_id = 16;
+    L.o_prob = L.o_id + r16h(rows * sizeof(int32_t));
+    L.o_st = L.o_prob + r16h(rows * sizeof(float));
+    L.o_in = L.o_st + r16h(rows * sizeof(bm_row_stats_t));
+    L.o_log = L.o_in;
+    L.o_kn = L.o_log + r16h(rows * (size_t)ld * sizeof(float));
+    L.o_u = L.o_kn + r16h(nk * sizeof(bm_knobs_t));
+    L.o_h = L.o_u + r16h(rows * sizeof(float));
+    L.o_off = L.o_h + (hist ? r16h((size_t)h1 * sizeof(int32_t)) : 0);
+    L.total = L.o_off + (hist ? r16h((rows + 1) * sizeof(int64_t)) : 0);
+    return L;
+}
+
 int sample_host_small(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t ld,
                       const int32_t *h_hist, const int64_t *h_hist_off,
                       const bm_knobs_t *h_knobs, int64_t knob_stride, const float *h_uniform,
                       int32_t *h_out_id, float *h_out_prob, bm_row_stats_t *h_stats,
-                      size_t nk, int64_t h1, size_t o_id, size_t o_prob, size_t o_st,
-                      size_t o_in, size_t o_log, size_t o_kn, size_t o_u, size_t o_h,
-                      size_t o_off, size_t total) {
+                      size_t nk, int64_t h1, const StageLayout &L) {
     const size_t rows = (size_t)B;
+    const size_t o_id = L.o_id, o_prob = L.o_prob, o_st = L.o_st, o_in = L.o_in;
+    const size_t o_log = L.o_log, o_kn = L.o_kn, o_u = L.o_u, o_h = L.o_h, o_off = L.o_off;
+    const size_t total = L.total;
     cudaStream_t s = c->stream;
     if (total > c->cap_stage) {
         CK(cudaStreamSynchronize(s));
@@ -551,17 +573,11 @@ int bm_sample_batch_host(bm_ctx_t *c, const float *h_logits, int B, int V, int64
             h1 = h_hist_off[B];
             if (h0 < 0 || h1 < h0) return fail(BM_ERR_INVALID_ARG, "hist_off not monotone");
         }
-        const size_t o_id = 16, o_prob = o_id + r16h(rows * 4), o_st = o_prob + r16h(rows * 4);
-        const size_t o_in = o_st + r16h(rows * sizeof(bm_row_stats_t));
-        const size_t o_log = o_in, o_kn = o_log + r16h(rows * (size_t)ld * 4);
-        const size_t o_u = o_kn + r16h(nk * sizeof(bm_knobs_t)), o_h = o_u + r16h(rows * 4);
-        const size_t o_off = o_h + (h_hist ? r16h((size_t)h1 * 4) : 0);
-        const size_t total = o_off + (h_hist ? r16h((rows + 1) * 8) : 0);
-        if (total <= STAGE_MAX)
+        const StageLayout L = stage_layout(rows, ld, nk, h1, h_hist != nullptr);
+        if (L.total <= STAGE_MAX)
             return sample_host_small(c, h_logits, B, V, ld, h_hist, h_hist_off, h_knobs,
                                      knob_stride, h_uniform, h_out_id, h_out_prob, h_stats, nk,
-                                     h1, o_id, o_prob, o_st, o_in, o_log, o_kn, o_u, o_h, o_off,
-                                     total);
+                                     h1, L);
     }
     if ((rc = grow(&c->d_logits, &c->cap_logits, rows * (size_t)ld)) != BM_OK) return rc;
     if (rows > c->cap_rows) {
