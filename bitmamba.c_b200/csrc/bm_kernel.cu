@@ -86,6 +86,7 @@ struct __align__(16) Vars {
     int top_k, greedy, pen, k;
     int sh, nslots, s_int0, s_int1;
     int h0, h1, released, fail;
+    int fail2;      // the exact select of this row did not converge
     int kcut, kcnt, n_cand, own;
     int clean, ln0, ln2, ln3;
     int sel_found, sel_j, res_id, n_final;
@@ -596,6 +597,7 @@ struct Ctx {
     bm_row_stats_t *stats;
     int rowid;
     int claim;  // thread 0: the row claimed to follow this one
+    int mark;   // failed rows get id -1 (the allocation-free entry point)
     uint32_t parity;
     // Point the shared-memory fields at the dynamic shared array.  Called at
     // the top of every non-inlined function: pointers that arrive as
@@ -675,6 +677,8 @@ __device__ __forceinline__ void release_row(Ctx &c) {
 __device__ __forceinline__ void write_result(const Ctx &c, int id, float p, int path, int n_cand,
                                              int n_final, int consumed) {
     if (threadIdx.x == 0) {
+        // an exact select that did not converge leaves the row unresolved
+        if (c.mark && c.v->fail2) id = -1;
         c.out_id[c.rowid] = id;
         if (c.out_prob) c.out_prob[c.rowid] = p;
         if (c.stats) {
@@ -1627,7 +1631,10 @@ __device__ __noinline__ Sel select_slow(Ctx c, bool scale, int mode, double T, i
         if (classify(u, mode, T, m) == 0) lb = mid + 1u;
         else ub = mid;
     }
-    if (threadIdx.x == 0) atomicOr(c.err, 2);
+    // did not converge: the error word says so, and on the allocation-free
+    // path the row's id is -1 (write_result)
+    if (threadIdx.x == 0) { atomicOr(c.err, 2); v->fail2 = 1; }
+    __syncthreads();
     return out;
 }
 
@@ -2156,11 +2163,12 @@ __device__ __forceinline__ void full_path(Ctx &c) {
     int ncand;
     double mex = msum;
     int cex = cntv ? csum : my_nc;
+    // the window buckets start unset; the scan's barriers order this before
+    // the bucket owners' writes below
+    if (threadIdx.x == 0) { v->bc = NB; v->bc_hi = NB; v->bk = NB; v->bd0 = NB; v->bd_hi = NB; }
     block_xscan_di(mex, cex, mt, ncand, c.red);
     if (clean && !cntv) ncand = c.V;  // every logit finite and a candidate
-    if (threadIdx.x == 0) {
-        v->n_cand = ncand; v->bc = NB; v->bc_hi = NB; v->bk = NB; v->bd0 = NB; v->bd_hi = NB;
-    }
+    if (threadIdx.x == 0) v->n_cand = ncand;
     if (ncand == 0) {  // argmax guard (src/model.c:296-303)
         release_row(c);
         const int id = guard_argmax(c);
@@ -2698,6 +2706,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     c.out_id = P.out_id;
     c.out_prob = P.out_prob;
     c.stats = P.stats;
+    c.mark = P.mark_failed_rows;
     c.attach();
     Vars *v = c.v;
     const int V = P.V;
@@ -2739,6 +2748,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             v->s_int0 = (i0 + sh) >> 2;
             v->s_int1 = v->s_int0 + (n4 >> 2);
             v->released = 0;
+            v->fail2 = 0;
             v->amax = INT_MAX;
             const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
             v->temp = kn.temp;
@@ -2860,12 +2870,14 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     }
     // the last release of this CTA claimed a row >= B and issued nothing, so
     // no copy is in flight when the kernel ends.  The last CTA to finish
-    // rewinds the schedule for the next launch.
+    // rewinds the schedule for the next launch (and, on the allocation-free
+    // path, clears the error word: failed rows carry id -1 instead).
     if (tid == 0) {
         __threadfence();
         if (atomicAdd(&P.sched[1], 1) == (int)gridDim.x - 1) {
             P.sched[0] = 0;
             P.sched[1] = 0;
+            if (P.mark_failed_rows) P.err[0] = 0;
             __threadfence();
         }
     }

@@ -30,11 +30,13 @@ struct Params {
     int32_t *out_id;
     float *out_prob;
     bm_row_stats_t *stats;
-    int *err;    // device error word: bit 0 = bounded wait expired
+    int *err;    // device error word: bit 0 = bounded wait expired, bit 1 = an
+                 // exact select did not converge
     int *sched;  // row schedule: [0] rows claimed past the first grid, [1] CTAs
                  // finished; both zero between launches
-    int mark_failed_rows = 0;  // nonzero: a row whose bounded wait expired
-                               // gets id -1
+    int mark_failed_rows = 0;  // nonzero: a row whose bounded wait expired or
+                               // whose exact select did not converge gets id
+                               // -1, and the last CTA clears the error word
 };
 
 // Dynamic shared memory the kernel needs for vocabulary V.

@@ -167,8 +167,9 @@ int bm_sample_batch(bm_ctx_t *ctx, const float *d_logits, int B, int V,
  *
  * Limits: V <= bm_max_vocab (50268 on a B200) else BM_ERR_UNSUPPORTED;
  * B <= 2^30 rows per call else BM_ERR_INVALID_ARG.  There is no context
- * error flag to check: a row whose bounded wait in the kernel expired gets
- * id -1.
+ * error flag to check: a row whose bounded wait in the kernel expired, or
+ * whose exact selection (the rare fallback over global memory) did not
+ * converge, gets id -1; the launch leaves the error word cleared.
  */
 int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,
                             const int32_t *d_hist, const int64_t *d_hist_off,
@@ -389,8 +390,10 @@ void bm_model_head_free(bm_model_head_t *head);
  * Same as bm_sample_batch with every buffer in host memory: copies the
  * inputs to the context's device staging buffers, samples, copies ids (and
  * probabilities / stats when non-NULL) back, and synchronises.  Host buffers
- * may be pageable or pinned (pinned is faster).  h_hist_off may be NULL with
- * h_hist NULL.  Calls whose buffers total at most 16 MB (B = 1 through about
+ * may be pageable or pinned (pinned is faster).  h_logits holds B * ld
+ * floats (the last row's pitch included: the rows are copied whole).
+ * h_hist_off may be NULL with h_hist NULL.  Calls whose buffers total at
+ * most 16 MB (B = 1 through about
  * 80 rows at V = 50257) pack every input into one pinned staging region of
  * the context (grown on demand), so they make one copy each way and one
  * synchronisation.

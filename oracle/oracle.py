@@ -32,10 +32,25 @@ _lib = None
 _ref = None
 
 
+def reference_tree() -> str | None:
+    """The reference checkout whose sources oracle/_ref is compiled from:
+    $BM_REFERENCE_SRC, else a `reference` directory beside this repository's
+    checkout; None when neither holds src/model.c."""
+    cands = [os.environ.get("BM_REFERENCE_SRC"),
+             os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.isfile(os.path.join(c, "src", "model.c")):
+            return c
+    return None
+
+
 def build(ref: bool = True) -> None:
     """Compile the oracle (and the reference harness when its sources exist)."""
-    target = "all" if ref else "oracle"
-    subprocess.run(["make", "-s", "-C", HERE, target], check=True)
+    cmd = ["make", "-s", "-C", HERE, "oracle"]
+    tree = reference_tree() if ref else None
+    if tree:
+        cmd = ["make", "-s", "-C", HERE, "all", f"REF={tree}"]
+    subprocess.run(cmd, check=True)
 
 
 def _p(a, t):
