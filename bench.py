@@ -35,7 +35,12 @@ UNIT = "tokens/s"
 KNOBS = dict(temp=1.0, penalty=1.0, min_p=0.0, top_p=0.95, top_k=0)
 RNG_SEED = 42
 FALLBACK_HBM_GBS = 6650.0
-PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "sample_kernel_c3.md")
+# DRAM bytes (read + write) per row of the c3 workload, from one ncu capture
+# of sample_kernel on B = 1024 rows (dram__bytes_read.sum 206.01 MB +
+# dram__bytes_write.sum 3.86 MB, profiles/sample_kernel_c3.md); traffic grows
+# with the rows processed (each row is read once), so a launch of B rows moves
+# about B times this.
+DRAM_BYTES_PER_ROW_C3 = (206.008576e6 + 3.862528e6) / 1024
 
 
 def workload_config(B, V):
@@ -157,17 +162,6 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def read_traffic():
-    """dram bytes per launch of the sampling kernel from the committed ncu summary."""
-    try:
-        for line in open(PROFILE_TRAFFIC):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
-
-
 def peak_hbm():
     try:
         d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -220,25 +214,29 @@ def run_reference(args):
     import torch
     B, V = args.B, args.V
     threads = host_threads()
-    # a bounded sample of the workload, sized so warmup + steps stay within
-    # about two minutes on this host
-    pool_rows = 512
-    logits = make_logits(torch, pool_rows, V, 1234, "cpu").numpy()
-    u = ref_uniforms(pool_rows)
+    # the whole B-row workload (the same generator and distribution as the
+    # GPU arm's), of which every step samples a bounded share: a different
+    # slice of one fixed permutation of the rows per step, sized so warmup +
+    # steps stay within about two minutes on this host
+    logits = make_logits(torch, B, V, 1234, "cpu").numpy()
+    u = ref_uniforms(B)
+    perm = np.random.default_rng(RNG_SEED).permutation(B)
     per_row_s = 0.006  # measured scale of the full-sort rows on one core
     budget = 120.0
-    rows_per_step = int(max(threads, min(pool_rows, budget / (args.steps + args.warmup)
+    rows_per_step = int(max(threads, min(B, budget / (args.steps + args.warmup)
                                          * threads / per_row_s)))
-    rows_per_step = max(1, min(pool_rows, rows_per_step))
+    rows_per_step = max(1, min(B, rows_per_step))
     kind = None
+
+    def step_rows(k):
+        return perm[(k * rows_per_step + np.arange(rows_per_step)) % B]
+
     for w in range(args.warmup):
-        s = (w * rows_per_step) % pool_rows
-        sel = np.arange(s, s + rows_per_step) % pool_rows
+        sel = step_rows(w)
         _, _, kind = cpu_leg(oracle_batch(np.ascontiguousarray(logits[sel])), u[sel], threads)
     total = 0.0
     for k in range(args.steps):
-        s = (k * rows_per_step) % pool_rows
-        sel = np.arange(s, s + rows_per_step) % pool_rows
+        sel = step_rows(args.warmup + k)
         _, dt, kind = cpu_leg(oracle_batch(np.ascontiguousarray(logits[sel])), u[sel], threads)
         total += dt
     value = rows_per_step * args.steps / total
@@ -249,8 +247,9 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(B, V), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"{rows_per_step} rows of the workload per step "
-                                   f"(pool of {pool_rows} rows), row-parallel pthreads"},
+                         "sample": f"{rows_per_step} rows of the {B}-row workload per step "
+                                   f"(a different slice of one permutation each step), "
+                                   f"row-parallel pthreads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -446,6 +445,12 @@ def run_ours(args):
         ids_cpu, dt, kind = cpu_leg(rb, u_host[:n], threads)
         cpu = {"value": n / dt, "unit": UNIT, "cores": threads, "kind": kind,
                "sample": f"first {n} rows of the workload, row-parallel pthreads"}
+        # the reference's native form: one thread, as model_forward_step calls
+        # its sampler once per decode step (src/model.c:1268-1307)
+        n1 = min(n, args.cpu_rows_single)
+        _, dt1, kind1 = cpu_leg(wl.batch(h[:n1], n1), u_host[:n1], 1)
+        cpu["single_thread"] = {"value": n1 / dt1, "unit": UNIT, "cores": 1, "kind": kind1,
+                                "sample": f"first {n1} rows of the workload, one thread"}
         same = int((ids_cpu == ids_dev[:n]).sum())
         parity = {"rows": n, "identical_ids": same}
         if same < n:
@@ -465,7 +470,7 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    traffic = read_traffic()
+    traffic = DRAM_BYTES_PER_ROW_C3 * B if wl.name == "c3" else None
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
@@ -925,6 +930,7 @@ def main():
     ap.add_argument("--B", type=int, default=4096)
     ap.add_argument("--V", type=int, default=50257)
     ap.add_argument("--cpu-rows", type=int, default=2048)
+    ap.add_argument("--cpu-rows-single", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload",
