@@ -626,6 +626,8 @@ def run_lmhead(args):
         peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
         peak_src = "MEASURED_PEAKS.json bf16_tflops_sustained"
     ids_dev = out_d.cpu().numpy()
+    fused()
+    fb_sampled, fb_computed = ctx.fused_fallback_rows()
 
     # CPU leg on a bounded sample: the oracle's RMSNorm + float64 product of
     # the same bf16 operands and the sampler oracle on the GPU's own logits
@@ -694,6 +696,9 @@ def run_lmhead(args):
                      "kernel_ms": gemm_ms, "flops_per_launch": flops,
                      "peak_source": peak_src},
         "parts_ms": {"norm_plus_gemm": gemm_ms, "sampler": samp_ms, "fused_step": ms},
+        "fused_rows_from_logits": {"sampled": fb_sampled, "recomputed": fb_computed,
+                                   "note": "rows the per-tile lists could not decide (the "
+                                           "rest never had logits in HBM)"},
         "cpu_baseline": cpu, "e2e": None, "clocks": clocks.summary(),
         "gpu_launches": 3 * args.steps, "parity_sample": parity,
     }

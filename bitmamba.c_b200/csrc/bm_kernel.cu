@@ -87,6 +87,8 @@ struct __align__(16) Vars {
     int sh, nslots, s_int0, s_int1;
     int h0, h1, released, fail;
     int fail2;      // the exact select of this row did not converge
+    int fb;         // summary rows: the lists cannot decide the row (full path)
+    float sumvk;    // summary rows: the largest value a tile's list may omit
     int kcut, kcnt, n_cand, own;
     int clean, ln0, ln2, ln3;
     int sel_found, sel_j, res_id, n_final;
@@ -598,6 +600,8 @@ struct Ctx {
     int rowid;
     int claim;  // thread 0: the row claimed to follow this one
     int mark;   // failed rows get id -1 (the allocation-free entry point)
+    int summary;  // the merge kernel: candidates come from per-tile lists
+    const int32_t *row_map;  // launch row -> row of the per-row arrays (or NULL)
     uint32_t parity;
     // Point the shared-memory fields at the dynamic shared array.  Called at
     // the top of every non-inlined function: pointers that arrive as
@@ -660,16 +664,19 @@ __device__ __forceinline__ void release_row(Ctx &c) {
             c.v->next_row = next_row;
         }
         if (next_row < c.B) {
+            const int nr = c.row_map ? (int)c.row_map[next_row] : next_row;
             if (lane < NCHUNK)
-                issue_chunk(c.logits + (int64_t)next_row * c.ld, c.V, c.mbar, c.row, lane);
+                issue_chunk(c.logits + (int64_t)nr * c.ld, c.V, c.mbar, c.row, lane);
             // the next row's knobs, uniform and history offsets into L1
             const Vars *v = c.v;
-            if (lane == NCHUNK + 1) prefetch_l1(v->p_knobs + (int64_t)next_row * v->p_knob_stride);
-            if (lane == NCHUNK + 2 && v->p_uniform) prefetch_l1(v->p_uniform + next_row);
-            if (lane == NCHUNK + 3 && v->p_hist_off) prefetch_l1(v->p_hist_off + next_row);
+            if (lane == NCHUNK + 1) prefetch_l1(v->p_knobs + (int64_t)nr * v->p_knob_stride);
+            if (lane == NCHUNK + 2 && v->p_uniform) prefetch_l1(v->p_uniform + nr);
+            if (lane == NCHUNK + 3 && v->p_hist_off) prefetch_l1(v->p_hist_off + nr);
             // warm L2 with the row claimed about one round later
             const int pre = next_row + (int)gridDim.x;
-            if (lane == NCHUNK && pre < c.B) prefetch_row(c.logits + (int64_t)pre * c.ld, c.V);
+            if (lane == NCHUNK && pre < c.B)
+                prefetch_row(c.logits + (int64_t)(c.row_map ? (int)c.row_map[pre] : pre) * c.ld,
+                             c.V);
         }
     }
 }
@@ -880,7 +887,61 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
     // marks them (a bit per element, no branch), a gather lists them, and the
     // histogram, cut and extraction work on that list.
     bool listed = false;
-    if (v->min_p > 0.0f) {
+    if (c.summary) {
+        // The merge kernel listed every tile-list entry with l >= thr.  Each
+        // tile's list holds its KS largest values, so it holds every value of
+        // the tile above the tile's KS-th (v->sumvk: their largest).  The
+        // cut's buckets and the extraction set are exact when every value
+        // they contain lies above sumvk; otherwise the row takes the full
+        // path (v->fb).
+        listed = true;
+        if (v->kcnt > KCAP) {  // more than the list holds: the full path
+            if (threadIdx.x == 0) v->fb = 1;
+            __syncthreads();
+            return;
+        }
+        for (int q = threadIdx.x; q < 8 * HB; q += NT) kh[q] = 0;
+        __syncthreads();
+        const int tot = v->kcnt;
+        for (int q = threadIdx.x; q < tot; q += NT) {
+            const float l = __uint_as_float((unsigned)(kc[q] & 0xffffffffu));
+            int b = x86_cvtt(__fmul_rn(__fsub_rn(mx, l), bscale));
+            b = min(max(b, 0), HB - 1);
+            if (b < HB - 1) atomicAdd(&kh[b], 1u);
+        }
+        __syncthreads();
+        cut_of();
+        const int cut = v->kcut;
+        const float bthr = __fsub_rn(mx, __fdiv_rn((float)(cut + 1), bscale));  // src/model.c:210-211
+        ethr = bthr > thr ? bthr : thr;                                      // src/model.c:213-214
+        // lowest value in buckets 0..cut (half a bucket of margin) or at or
+        // above ethr
+        const float lb = __fsub_rn(mx, __fdiv_rn((float)cut + 1.5f, bscale));
+        const float need = fmaxf(thr, fminf(lb, ethr));
+        if (!(v->sumvk < need) || !(fabsf(mx) < 1e30f)) {
+            if (threadIdx.x == 0) v->fb = 1;
+            __syncthreads();
+            return;
+        }
+        constexpr int PQ = KCAP / NT;
+        unsigned long long e[PQ];
+        bool keep[PQ];
+        int mine = 0;
+#pragma unroll
+        for (int q = 0; q < PQ; ++q) {
+            const int jj = threadIdx.x + q * NT;
+            e[q] = (jj < tot) ? kc[jj] : 0ull;
+            keep[q] = jj < tot && __uint_as_float((unsigned)(e[q] & 0xffffffffu)) >= ethr;
+            mine += keep[q] ? 1 : 0;
+        }
+        int n2;
+        int o = block_xscan_i(mine, n2, c.red);
+#pragma unroll
+        for (int q = 0; q < PQ; ++q)
+            if (keep[q]) kc[o++] = e[q];
+        if (threadIdx.x == 0) v->kcnt = n2;
+        __syncthreads();
+    } else if (v->min_p > 0.0f) {
         uint32_t *mk = reinterpret_cast<uint32_t *>(kc);  // MASKW words per thread
         uint32_t w = 0;
         int i = 0;
@@ -1075,9 +1136,15 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
         }
     }
     const int n = v->kcnt;
+    if (c.summary && (n == 0 || n > KCAP)) {
+        // the guard and the overflow paths read the logits: the full path
+        if (threadIdx.x == 0) v->fb = 1;
+        __syncthreads();
+        return;
+    }
     // the buffer is no longer needed: the rest works on the candidate list
     // (or re-reads global memory on the rare overflow / guard paths)
-    release_row(c);
+    if (!c.summary) release_row(c);
     if (n == 0) {  // argmax guard (src/model.c:227-237)
         const int id = guard_argmax(c);
         write_result(c, id, 1.0f, 2, 0, 0, 0);
@@ -2697,9 +2764,13 @@ __device__ __forceinline__ void full_path(Ctx &c) {
 __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     const Layout L = layout(P.V);
     Ctx c;
+    // the launch's rows: B, or a count an earlier kernel wrote
+    const int B = P.dB ? min(*P.dB, P.B) : P.B;
+    // launch row r is row orow(r) of the per-row arrays
+    auto orow = [&](int r) { return P.row_map ? (int)P.row_map[r] : r; };
     c.logits = P.logits;
     c.ld = P.ld;
-    c.B = P.B;
+    c.B = B;
     c.V = P.V;
     c.err = P.err;
     c.sched = P.sched;
@@ -2707,6 +2778,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     c.out_prob = P.out_prob;
     c.stats = P.stats;
     c.mark = P.mark_failed_rows;
+    c.summary = 0;
+    c.row_map = P.row_map;
     c.attach();
     Vars *v = c.v;
     const int V = P.V;
@@ -2720,14 +2793,16 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         for (int i = 0; i < NCHUNK; ++i) mbar_init(&c.mbar[i], 1);
         fence_mbar_init();
         v->fail = 0;
-        if ((int)blockIdx.x < P.B) issue_row(P.logits + (int64_t)blockIdx.x * P.ld, V, c.mbar, c.row);
+        if ((int)blockIdx.x < B)
+            issue_row(P.logits + (int64_t)orow(blockIdx.x) * P.ld, V, c.mbar, c.row);
         const int pre = (int)(blockIdx.x + gridDim.x);
-        if (pre < P.B) prefetch_row(P.logits + (int64_t)pre * P.ld, V);
+        if (pre < B) prefetch_row(P.logits + (int64_t)orow(pre) * P.ld, V);
     }
     __syncthreads();
 
     uint32_t it = 0;
-    for (int row = blockIdx.x; row < P.B; ++it) {
+    for (int lrow = blockIdx.x; lrow < B; ++it) {
+        const int row = orow(lrow);
         c.rowid = row;
         c.parity = it & 1u;
         c.g = P.logits + (int64_t)row * P.ld;
@@ -2814,7 +2889,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
                 if (P.mark_failed_rows) {
                     // this row and the one claimed for after it stay unsampled
                     P.out_id[row] = -1;
-                    if (c.claim < P.B) P.out_id[c.claim] = -1;
+                    if (c.claim < B) P.out_id[orow(c.claim)] = -1;
                 }
             }
             __syncthreads();
@@ -2866,7 +2941,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         __syncthreads();
         if (!v->released) release_row(c);
         __syncthreads();
-        row = v->next_row;
+        lrow = v->next_row;
     }
     // the last release of this CTA claimed a row >= B and issued nothing, so
     // no copy is in flight when the kernel ends.  The last CTA to finish
@@ -2880,6 +2955,181 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             if (P.mark_failed_rows) P.err[0] = 0;
             __threadfence();
         }
+    }
+}
+
+// ------------------------------------------------------------ merge --
+// The fused lm_head + sampler's second kernel: one CTA per row at a time.
+// The row's lists (the GEMM's summary epilogue: per 128 columns the KS
+// largest penalised, scaled logits, unordered) are staged in the row
+// buffer's place.  Every column's maximum is in its list, and a list that is
+// not full holds every value of its columns.
+//   greedy rows: the argmax over the lists (the lowest id among equal
+//     maxima), strict '>' from -1e9 (src/model.c:144-154);
+//   top_k rows (1 <= top_k <= 256): the maximum, the min_p threshold
+//     (src/model.c:165-173), every listed value at or above it, and the top_k
+//     path on that list, which checks that no full list's omitted values (at
+//     most its smallest entry) can reach the cut's buckets or the extraction
+//     set (else the row goes to the fallback lists);
+//   other rows (their logits were stored by the GEMM): the fallback list.
+__global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const SumParams P) {
+    Ctx c;
+    c.logits = nullptr;
+    c.ld = 0;
+    c.B = P.B;
+    c.V = P.V;
+    c.err = P.err;
+    c.sched = nullptr;
+    c.out_id = P.out_id;
+    c.out_prob = P.out_prob;
+    c.stats = P.stats;
+    c.mark = 0;
+    c.summary = 1;
+    c.row_map = nullptr;
+    c.g = nullptr;
+    c.claim = 0;
+    c.parity = 0;
+    c.attach();
+    Vars *v = c.v;
+    const int tid = threadIdx.x;
+    const int ks = P.ks, ne = P.tiles * P.ks;
+    unsigned long long *se = reinterpret_cast<unsigned long long *>(c.row);
+    unsigned long long *kc = reinterpret_cast<unsigned long long *>(c.scr + 4096);
+    constexpr unsigned NONE = 0xffffffffu;  // unused list slot
+    for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
+        c.rowid = row;
+        if (tid == 0) {
+            const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
+            v->temp = kn.temp;
+            v->penalty = kn.penalty;
+            v->min_p = kn.min_p;
+            v->top_p = kn.top_p;
+            v->top_k = kn.top_k;
+            v->inv_temp = kn.inv_temp;
+            v->log_min_p = kn.log_min_p;
+            v->u = P.uniform ? P.uniform[row] : 0.0f;
+            v->greedy = (kn.temp < 0.05f);                                   // src/model.c:144
+            v->k = (kn.top_k > 0 && kn.top_k <= 256) ? kn.top_k : 0;        // src/model.c:175
+            v->pen = 0;
+            v->fb = 0;
+            v->fail2 = 0;
+            v->kcnt = 0;
+            v->released = 1;
+            v->sh = 0;
+            v->nslots = 0;
+        }
+        // the row's lists, 16-byte loads (ne is even: ks is)
+        const uint4 *src = reinterpret_cast<const uint4 *>(P.summ + (int64_t)row * ne);
+        for (int i = tid; i < ne / 2; i += NT) reinterpret_cast<uint4 *>(se)[i] = src[i];
+        __syncthreads();
+        if (v->greedy) {
+            float gv = -1e9f;
+            int gi = INT_MAX;
+            for (int i = tid; i < ne; i += NT) {
+                const unsigned long long e = se[i];
+                const unsigned id = (unsigned)e;
+                const float x = __uint_as_float((unsigned)(e >> 32));
+                if (id != NONE && (x > gv || (x == gv && gi != INT_MAX && (int)id < gi))) {
+                    gv = x;
+                    gi = (int)id;
+                }
+            }
+            block_argmax(gv, gi, c.red);
+            write_result(c, gi == INT_MAX ? 0 : gi, 1.0f, 1, 0, 0, 0);
+            __syncthreads();
+            continue;
+        }
+        if (v->k > 0) {
+            // the maximum, and the largest value a full list may have left
+            // out (at most its smallest entry)
+            float mx = -1e30f, nvk = PINF;
+            for (int t = tid; t < P.tiles; t += NT) {
+                float lmax = -PINF, lmin = PINF;
+                int cnt = 0;
+                for (int k = 0; k < ks; ++k) {
+                    const unsigned long long e = se[(int64_t)t * ks + k];
+                    if ((unsigned)e == NONE) continue;
+                    const float x = __uint_as_float((unsigned)(e >> 32));
+                    lmax = fmaxf(lmax, x);
+                    lmin = fminf(lmin, x);
+                    ++cnt;
+                }
+                mx = fmaxf(mx, lmax);
+                if (cnt == ks) nvk = fminf(nvk, -lmin);
+            }
+            block_maxmin_f(mx, nvk, c.red);
+            if (tid == 0) {
+                v->mx = mx;
+                // src/model.c:169-173 (logf from the host)
+                float thr = -1e30f;
+                if (v->min_p >= 1.0f) thr = mx;
+                else if (v->min_p > 0.0f) thr = __fadd_rn(mx, v->log_min_p);
+                v->thr = thr;
+                v->sumvk = -nvk;
+            }
+            // the listed candidates (l >= thr, src/model.c:185) by the
+            // reference's 128 buckets: the first bucket where their count
+            // reaches top_k lies at or past the row's own cut (the lists hold
+            // a subset of the row), so every candidate the cut or the
+            // extraction can need lies in the buckets up to one past it
+            uint32_t *hb = reinterpret_cast<uint32_t *>(c.scr);
+            const float bscale = __fdiv_rn(127.0f, 20.0f);  // src/model.c:184
+            for (int q = tid; q < HB; q += NT) hb[q] = 0u;
+            __syncthreads();
+            const float thr = v->thr, mxr = v->mx;
+            auto bucket_of = [&](float l) {
+                const int b = x86_cvtt(__fmul_rn(__fsub_rn(mxr, l), bscale));
+                return min(max(b, 0), HB - 1);
+            };
+            for (int i = tid; i < ne; i += NT) {
+                const unsigned long long e = se[i];
+                if ((unsigned)e == NONE) continue;
+                const float x = __uint_as_float((unsigned)(e >> 32));
+                if (x >= thr) {
+                    const int b = bucket_of(x);
+                    if (b < HB - 1) atomicAdd(&hb[b], 1u);
+                }
+            }
+            __syncthreads();
+            if (tid < 32) {
+                uint32_t cq[4], ls = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) { cq[q] = hb[4 * tid + q]; ls += cq[q]; }
+                const uint32_t inc = warp_iscan(ls, tid);
+                uint32_t run = inc - ls;
+                int hit = INT_MAX;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    run += cq[q];
+                    if (hit == INT_MAX && run >= (uint32_t)v->k) hit = 4 * tid + q;
+                }
+                hit = warp_imin(hit);
+                if (tid == 0) v->kcut = (hit == INT_MAX) ? HB - 1 : hit;
+            }
+            __syncthreads();
+            const int lim = min(v->kcut + 1, HB - 1);
+            for (int i = tid; i < ne; i += NT) {
+                const unsigned long long e = se[i];
+                if ((unsigned)e == NONE) continue;
+                const float x = __uint_as_float((unsigned)(e >> 32));
+                if (x >= thr && bucket_of(x) <= lim) {
+                    const int pos = atomicAdd(&v->kcnt, 1);
+                    if (pos < KCAP) kc[pos] = ((unsigned long long)(unsigned)e << 32) | (e >> 32);
+                }
+            }
+            __syncthreads();
+            topk_path<false>(c);
+        } else if (tid == 0) {
+            v->fb = 1;
+        }
+        __syncthreads();
+        if (tid == 0 && v->fb) {
+            // left for the full sampler: with its logits (stored by the GEMM)
+            // or after a GEMM of its own (a top_k row the lists cannot decide)
+            P.fb[1 + atomicAdd(&P.fb[0], 1)] = row;
+            if (v->k > 0) P.nl[1 + atomicAdd(&P.nl[0], 1)] = row;
+        }
+        __syncthreads();
     }
 }
 
@@ -2908,6 +3158,25 @@ int max_vocab(size_t limit) {
 cudaError_t prepare(int V) {
     return cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)smem_bytes(V));
+}
+
+static size_t summary_smem(int V, int tiles, int ks) {
+    return layout(V).row + (size_t)tiles * ks * 8;
+}
+
+cudaError_t prepare_summary(int V, int tiles, int ks) {
+    cudaError_t e = cudaFuncSetAttribute(summary_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)summary_smem(V, tiles, ks));
+    if (e != cudaSuccess) return e;
+    // MERGE_CTAS_PER_SM CTAs' shared memory per SM
+    return cudaFuncSetAttribute(summary_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
+}
+
+cudaError_t launch_summary(const SumParams &p, int grid, cudaStream_t s) {
+    if (p.ks % 2 || p.tiles <= 0) return cudaErrorInvalidValue;
+    summary_kernel<<<grid, NT, summary_smem(p.V, p.tiles, p.ks), s>>>(p);
+    return cudaGetLastError();
 }
 
 cudaError_t launch(const Params &p, int grid, cudaStream_t s) {

@@ -37,7 +37,38 @@ struct Params {
     int mark_failed_rows = 0;  // nonzero: a row whose bounded wait expired or
                                // whose exact select did not converge gets id
                                // -1, and the last CTA clears the error word
+    const int *dB = nullptr;   // optional: the row count, read at launch from
+                               // this device word (at most B)
+    const int32_t *row_map = nullptr;  // optional: launch row i is row
+                                       // row_map[i] of every per-row array,
+                                       // the logits included
 };
+
+// The merge kernel of the fused lm_head + sampler: per row, the per-tile
+// lists of the GEMM's summary epilogue (tiles x ks entries, (bits(value) <<
+// 32) | id) finish the greedy argmax or the top_k path; rows they cannot
+// decide, and rows of the full-vocabulary path, are appended to the fallback
+// lists (fb = [count, rows...]: to be sampled from logits; nl = [count,
+// rows...]: their logits still to be computed).
+struct SumParams {
+    const uint64_t *summ;
+    int tiles, ks;
+    int B, V;
+    const bm_knobs_t *knobs;
+    int64_t knob_stride;
+    const float *uniform;
+    int32_t *out_id;
+    float *out_prob;
+    bm_row_stats_t *stats;
+    int *fb;
+    int *nl;
+    int *err;
+};
+// The merge kernel's rows are independent and its serial phases short of
+// work, so several CTAs share an SM (their phases overlap).
+constexpr int MERGE_CTAS_PER_SM = 4;
+cudaError_t launch_summary(const SumParams &p, int grid, cudaStream_t s);
+cudaError_t prepare_summary(int V, int tiles, int ks);
 
 // Dynamic shared memory the kernel needs for vocabulary V.
 size_t smem_bytes(int V);

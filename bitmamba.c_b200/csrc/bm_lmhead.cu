@@ -11,10 +11,18 @@
 //             swizzle through a 4-stage shared-memory ring (plain loads),
 //             one thread issues tcgen05.mma (kind::f16, M=128, N=256, K=16)
 //             into one of two 256-column fp32 accumulators in tensor memory
-//             and frees each stage with tcgen05.commit; four warps drain the
+//             and frees each stage with tcgen05.commit; eight warps drain the
 //             other accumulator with tcgen05.ld and store fp32 logits while
 //             the next tile's MMAs run.  Tiles go M-index first, so CTAs
 //             running together share W tiles and W streams from HBM once.
+//   summary   (the fused top_k path) the drain warps store no logits: each
+//             thread owns one row and 128 columns of the tile, applies the
+//             row's repetition penalty (a per-row bitset of its history ids)
+//             and temperature, and writes the KS largest values of those
+//             columns (ties: lower id first) with their ids -- 64 bytes per
+//             row and 128 columns instead of 512 bytes of logits.  A merge
+//             kernel finishes the sampler's top_k path from these lists
+//             (bm_kernel.cu).
 //
 // The reference computes its lm_head as a ternary BitLinear (src/model.c:
 // 1239-1262); this bf16 variant has no counterpart there and is checked
@@ -25,18 +33,43 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
+#include <climits>
 #include <mutex>
 
 namespace bml {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int EPI_WARPS = 4, NTH = 32 * (2 + EPI_WARPS);  // producer, MMA, 4 drain warps
+// producer, MMA and the drain warps: four (one per accumulator lane quarter)
+// storing logits, eight (two per quarter, each taking half of the tile's 256
+// columns) for the summary epilogue
+template <bool SUM>
+__host__ __device__ constexpr int epi_warps() { return SUM ? 8 : 4; }
+template <bool SUM>
+__host__ __device__ constexpr int gemm_threads() { return 32 * (2 + epi_warps<SUM>()); }
 constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 2 * BN;  // two fp32 accumulators, one column per n
 constexpr size_t GEMM_SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+// the summary epilogue's staging: 32 columns x 256 drain threads of fp32
+// (column j of drain thread t at [j][t]: bank t % 32, conflict-free for any
+// column per thread)
+constexpr size_t EPI_STAGE = 32 * 256 * 4;
+constexpr size_t GEMM_SMEM_SUM = GEMM_SMEM + EPI_STAGE;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
+
+// GPT-2 ids the reference never penalises (src/bitmamba.h:21-24).
+__device__ __forceinline__ bool protected_id(int id) {
+    return id == 50256 || id == 198 || id == 628 || id == 13;
+}
+// src/model.c:1298-1304: l > 0 ? l / penalty : l * penalty
+__device__ __forceinline__ float penalize(float l, float pen) {
+    return (l > 0.0f) ? __fdiv_rn(l, pen) : __fmul_rn(l, pen);
+}
+// (a, ia) ahead of (b, ib): larger value, then lower id (NaN never ahead)
+__device__ __forceinline__ bool ahead(float a, int ia, float b, int ib) {
+    return a > b || (a == b && ia < ib);
+}
 
 __device__ __forceinline__ uint32_t sa(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -142,11 +175,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
 // out = (float) acc * row_scale[row]; otherwise bf16 operands (kind::f16,
 // 64 elements per stage row) and fp32 accumulators stored as they are.  The
 // shared-memory tiles are byte-identical in shape either way.
-template <bool I8>
-__global__ void __launch_bounds__(NTH, 1)
+template <bool I8, bool SUM>
+__global__ void __launch_bounds__(gemm_threads<SUM>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                float *out, int M, int N, int K, int64_t ldo, const float *row_scale, int *err) {
+                float *out, int M, int N, int K, int64_t ldo, const float *row_scale, int *err,
+                const SumArgs sg, const int *dM, const int *out_rows) {
     constexpr int BKE = I8 ? 128 : BK;  // elements per 128-byte stage row
+    if (dM) M = *dM;  // a row count the previous kernel wrote (0: no tiles)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // the 128-byte swizzle pattern repeats every 1024 bytes: tiles start on
     // a 1024-byte boundary
@@ -171,7 +206,7 @@ __global__ void __launch_bounds__(NTH, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], EPI_WARPS);
+            mbar_init(&acce[b], epi_warps<SUM>());
         }
         *abort_ = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -247,9 +282,13 @@ __global__ void __launch_bounds__(NTH, 1)
             umma_commit(&accf[b]);  // arrives once every MMA of this tile completed
         }
     } else if (warp >= 2) {
-        // drain: warp w reads accumulator lanes (rows) 32 (w % 4) .. + 31
-        const int q = warp & 3;
+        // drain: warp w reads accumulator lanes (rows) 32 (w % 4) .. + 31 and
+        // (summary) columns 128 h .. + 127 of the tile, h = (w - 2) / 4
+        constexpr int CPW = (BN / 32) * 4 / epi_warps<SUM>();  // 32-column chunks per warp
+        const int q = warp & 3, h = (warp - 2) >> 2, td = (warp - 2) * 32 + lane;
         const bool vec = ((ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+        // this drain thread's column of the staging area
+        float *cv = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + 256) + td;
         int i = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
             const int b = i & 1;
@@ -263,8 +302,59 @@ __global__ void __launch_bounds__(NTH, 1)
             const int row = m0 + q * 32 + lane;
             const uint32_t tb = tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16);
             const float sc = (I8 && row < M) ? row_scale[row] : 1.0f;
+            // summary: the row's knobs (greedy rows keep the raw penalised
+            // logits, src/model.c:144-154; others are scaled by 1 / temp,
+            // :156-163) and the KS best (value, id) of the 128 columns, as an
+            // unordered set with its worst entry (wv, wi in slot ws) tracked
+            float pen = 1.0f, inv = 1.0f;
+            bool has_pen = false, row_full = false;
+            float tv[KS], wv = -__builtin_huge_valf();
+            int ti[KS], wi = INT_MAX, ws = 0;
+#pragma unroll
+            for (int k = 0; k < KS; ++k) { tv[k] = -__builtin_huge_valf(); ti[k] = INT_MAX; }
+            // (value, id) into the set in place of its worst entry when ahead
+            // of it; then the new worst by a three-level comparison tree
+            auto put = [&](float x, int col) {
+                if (!ahead(x, col, wv, wi)) return;
+#pragma unroll
+                for (int k = 0; k < KS; ++k) {
+                    tv[k] = (k == ws) ? x : tv[k];
+                    ti[k] = (k == ws) ? col : ti[k];
+                }
+                float v4[KS / 2];
+                int i4[KS / 2], s4[KS / 2];
+#pragma unroll
+                for (int k = 0; k < KS / 2; ++k) {
+                    const bool a = ahead(tv[2 * k], ti[2 * k], tv[2 * k + 1], ti[2 * k + 1]);
+                    v4[k] = a ? tv[2 * k + 1] : tv[2 * k];
+                    i4[k] = a ? ti[2 * k + 1] : ti[2 * k];
+                    s4[k] = a ? 2 * k + 1 : 2 * k;
+                }
+#pragma unroll
+                for (int n = KS / 4; n >= 1; n >>= 1) {
+#pragma unroll
+                    for (int k = 0; k < n; ++k) {
+                        const bool a = ahead(v4[2 * k], i4[2 * k], v4[2 * k + 1], i4[2 * k + 1]);
+                        v4[k] = a ? v4[2 * k + 1] : v4[2 * k];
+                        i4[k] = a ? i4[2 * k + 1] : i4[2 * k];
+                        s4[k] = a ? s4[2 * k + 1] : s4[2 * k];
+                    }
+                }
+                wv = v4[0];
+                wi = i4[0];
+                ws = s4[0];
+            };
+            if (SUM && row < M) {
+                const bm_knobs_t kn = sg.knobs[(int64_t)row * sg.knob_stride];
+                inv = (kn.temp < 0.05f) ? 1.0f : kn.inv_temp;
+                pen = kn.penalty;
+                // rows of the full-vocabulary path (src/model.c:282-360) get
+                // their logits stored instead
+                row_full = !(kn.temp < 0.05f) && !(kn.top_k > 0 && kn.top_k <= 256);
+                has_pen = sg.pbits && (kn.penalty > 0.0f) && (kn.penalty != 1.0f);
+            }
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = CPW * h; c < CPW * h + CPW; ++c) {
                 uint32_t r[32];
                 tmem_ld32(tb + c * 32, r);
                 if (I8) {
@@ -273,8 +363,39 @@ __global__ void __launch_bounds__(NTH, 1)
                         r[j] = __float_as_uint(__fmul_rn(__int2float_rn((int)r[j]), sc));
                 }
                 const int col0 = n0 + c * 32;
+                if (SUM && !row_full) {
+                    if (row < M && col0 < N) {
+                        // stage the chunk, mark the columns ahead of the set's
+                        // worst entry (branch-free), insert only those; the
+                        // penalised columns (history ids, rare) separately
+                        const int nv = min(32, N - col0);
+                        const uint32_t live = nv < 32 ? (1u << nv) - 1u : 0xffffffffu;
+                        const uint32_t pm =
+                            (has_pen ? sg.pbits[(int64_t)row * sg.pw + (col0 >> 5)] : 0u) & live;
+                        const float lv = wv;
+                        const int li = wi;
+                        uint32_t mask = 0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float x = __uint_as_float(r[j]);
+                            cv[j * 256] = x;
+                            const float y = __fmul_rn(x, inv);
+                            mask |= (ahead(y, col0 + j, lv, li) ? 1u : 0u) << j;
+                        }
+                        mask &= live & ~pm;
+                        for (; mask; mask &= mask - 1) {
+                            const int j = __ffs(mask) - 1;
+                            put(__fmul_rn(cv[j * 256], inv), col0 + j);
+                        }
+                        for (uint32_t m = pm; m; m &= m - 1) {
+                            const int j = __ffs(m) - 1;
+                            put(__fmul_rn(penalize(cv[j * 256], pen), inv), col0 + j);
+                        }
+                    }
+                    continue;
+                }
                 if (row < M && col0 < N) {
-                    float *o = out + (int64_t)row * ldo + col0;
+                    float *o = out + (int64_t)(out_rows ? out_rows[row] : row) * ldo + col0;
                     if (vec && col0 + 32 <= N) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
@@ -286,6 +407,18 @@ __global__ void __launch_bounds__(NTH, 1)
                         for (int j = 0; j < 32; ++j)
                             if (col0 + j < N) o[j] = __uint_as_float(r[j]);
                     }
+                }
+            }
+            if (SUM && row < M && !row_full) {
+                // entries (bits(value) << 32) | id in no order, unused slots
+                // id 0xffffffff; list 2 t' + h of the row for tile column t'
+                uint4 *o = reinterpret_cast<uint4 *>(
+                    sg.summ + ((int64_t)row * 2 * NTL + 2 * (t / MT) + h) * KS);
+#pragma unroll
+                for (int k = 0; k < KS; k += 2) {
+                    const uint32_t i0 = ti[k] == INT_MAX ? 0xffffffffu : (uint32_t)ti[k];
+                    const uint32_t i1 = ti[k + 1] == INT_MAX ? 0xffffffffu : (uint32_t)ti[k + 1];
+                    o[k / 2] = make_uint4(i0, __float_as_uint(tv[k]), i1, __float_as_uint(tv[k + 1]));
                 }
             }
             // the accumulator is free for the MMAs of tile i + 2
@@ -486,10 +619,13 @@ cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int K, int box_
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// a, W: [M x K] and [N x K] K-major (int8 when row_scale is given, else bf16)
+// a, W: [M x K] and [N x K] K-major (int8 when row_scale is given, else bf16);
+// sg.summ set: the summary epilogue instead of the logits
 cudaError_t launch_gemm(const void *a, const void *W, int M, int N, int K, const float *row_scale,
-                        float *out, int64_t ldo, int *err, cudaStream_t s) {
+                        float *out, int64_t ldo, int *err, cudaStream_t s, const SumArgs &sg,
+                        const int *dM, const int *out_rows) {
     const bool i8 = row_scale != nullptr;
+    const bool sum = sg.summ != nullptr;
     CUtensorMap ma, mb;
     cudaError_t e;
     if ((e = make_map(&ma, a, M, K, BM, i8)) != cudaSuccess) return e;
@@ -501,11 +637,46 @@ cudaError_t launch_gemm(const void *a, const void *W, int M, int N, int K, const
     const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     if (tiles > (1LL << 30)) return cudaErrorInvalidValue;
     const int grid = (int)(tiles < sms ? tiles : sms);
-    if (i8)
-        gemm_kernel<true><<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, row_scale, err);
+    if (i8 && sum)
+        gemm_kernel<true, true><<<grid, gemm_threads<true>(), GEMM_SMEM_SUM, s>>>(ma, mb, out, M, N, K, ldo, row_scale,
+                                                            err, sg, dM, out_rows);
+    else if (i8)
+        gemm_kernel<true, false><<<grid, gemm_threads<false>(), GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, row_scale,
+                                                             err, sg, dM, out_rows);
+    else if (sum)
+        gemm_kernel<false, true><<<grid, gemm_threads<true>(), GEMM_SMEM_SUM, s>>>(ma, mb, out, M, N, K, ldo, nullptr,
+                                                             err, sg, dM, out_rows);
     else
-        gemm_kernel<false><<<grid, NTH, GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, nullptr, err);
+        gemm_kernel<false, false><<<grid, gemm_threads<false>(), GEMM_SMEM, s>>>(ma, mb, out, M, N, K, ldo, nullptr,
+                                                              err, sg, dM, out_rows);
     return cudaGetLastError();
+}
+
+// One CTA per row: clear the row's bits, then set those of its history.
+__global__ void __launch_bounds__(256) penbits_kernel(const int32_t *hist, const int64_t *off,
+                                                      int V, uint32_t *bits, int pw) {
+    const int r = blockIdx.x;
+    uint32_t *b = bits + (int64_t)r * pw;
+    for (int i = threadIdx.x; i < pw; i += blockDim.x) b[i] = 0u;
+    __syncthreads();
+    const int64_t h0 = off[r], h1 = off[r + 1];
+    for (int64_t i = h0 + threadIdx.x; i < h1; i += blockDim.x) {
+        const int id = hist[i];
+        if (id >= 0 && id < V && !protected_id(id)) atomicOr(&b[id >> 5], 1u << (id & 31));
+    }
+}
+
+// Rows of 16-byte words: block-stride over the listed rows.
+__global__ void gather_kernel(const uint4 *src, int64_t w16, const int *list, uint4 *dst,
+                              const float *ssc, float *dsc) {
+    const int n = list[0];
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        const int r = list[1 + i];
+        const uint4 *sr = src + (int64_t)r * w16;
+        uint4 *dr = dst + (int64_t)i * w16;
+        for (int64_t k = threadIdx.x; k < w16; k += blockDim.x) dr[k] = sr[k];
+        if (ssc && threadIdx.x == 0) dsc[i] = ssc[r];
+    }
 }
 
 }  // namespace
@@ -513,11 +684,17 @@ cudaError_t launch_gemm(const void *a, const void *W, int M, int N, int K, const
 cudaError_t prepare() {
     cudaError_t e = get_encode();
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)GEMM_SMEM);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)GEMM_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)GEMM_SMEM_SUM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)GEMM_SMEM_SUM);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(ternary_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)((RN_WARPS + 2) * RN_MAXD * sizeof(float)));
@@ -540,25 +717,72 @@ cudaError_t rmsnorm_bf16(const float *x, int B, int D, const float *w, uint16_t 
 }
 
 cudaError_t gemm_bf16(const uint16_t *a, const uint16_t *W, int M, int N, int K, float *out,
-                      int64_t ldo, int *err, cudaStream_t s) {
+                      int64_t ldo, int *err, cudaStream_t s, const int *dM, const int *out_rows) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (K <= 0 || K % 8 || (reinterpret_cast<uintptr_t>(a) & 15) ||
         (reinterpret_cast<uintptr_t>(W) & 15) || ldo < N)
         return cudaErrorInvalidValue;
     cudaError_t e = get_encode();
     if (e != cudaSuccess) return e;
-    return launch_gemm(a, W, M, N, K, nullptr, out, ldo, err, s);
+    return launch_gemm(a, W, M, N, K, nullptr, out, ldo, err, s, SumArgs{}, dM, out_rows);
 }
 
 cudaError_t gemm_i8(const int8_t *a, const int8_t *W, int M, int N, int K, const float *row_scale,
-                    float *out, int64_t ldo, int *err, cudaStream_t s) {
+                    float *out, int64_t ldo, int *err, cudaStream_t s, const int *dM,
+                    const int *out_rows) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (K <= 0 || K % 16 || (reinterpret_cast<uintptr_t>(a) & 15) ||
         (reinterpret_cast<uintptr_t>(W) & 15) || ldo < N || !row_scale)
         return cudaErrorInvalidValue;
     cudaError_t e = get_encode();
     if (e != cudaSuccess) return e;
-    return launch_gemm(a, W, M, N, K, row_scale, out, ldo, err, s);
+    return launch_gemm(a, W, M, N, K, row_scale, out, ldo, err, s, SumArgs{}, dM, out_rows);
+}
+
+cudaError_t gemm_bf16_summary(const uint16_t *a, const uint16_t *W, int M, int N, int K,
+                              const SumArgs &sg, float *out, int64_t ldo, int *err,
+                              cudaStream_t s) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (K <= 0 || K % 8 || (reinterpret_cast<uintptr_t>(a) & 15) || !out || ldo < N ||
+        (reinterpret_cast<uintptr_t>(W) & 15) || !sg.summ || !sg.knobs ||
+        (reinterpret_cast<uintptr_t>(sg.summ) & 15) || (sg.pbits && sg.pw < (N + 31) / 32))
+        return cudaErrorInvalidValue;
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    return launch_gemm(a, W, M, N, K, nullptr, out, ldo, err, s, sg, nullptr, nullptr);
+}
+
+cudaError_t gemm_i8_summary(const int8_t *a, const int8_t *W, int M, int N, int K,
+                            const float *row_scale, const SumArgs &sg, float *out, int64_t ldo,
+                            int *err, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (K <= 0 || K % 16 || (reinterpret_cast<uintptr_t>(a) & 15) || !out || ldo < N ||
+        (reinterpret_cast<uintptr_t>(W) & 15) || !row_scale || !sg.summ || !sg.knobs ||
+        (reinterpret_cast<uintptr_t>(sg.summ) & 15) || (sg.pbits && sg.pw < (N + 31) / 32))
+        return cudaErrorInvalidValue;
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    return launch_gemm(a, W, M, N, K, row_scale, out, ldo, err, s, sg, nullptr, nullptr);
+}
+
+cudaError_t penalty_bits(const int32_t *hist, const int64_t *hist_off, int B, int V,
+                         uint32_t *bits, int pw, cudaStream_t s) {
+    if (B <= 0) return cudaSuccess;
+    if (!hist || !hist_off || !bits || pw < (V + 31) / 32) return cudaErrorInvalidValue;
+    penbits_kernel<<<B, 256, 0, s>>>(hist, hist_off, V, bits, pw);
+    return cudaGetLastError();
+}
+
+cudaError_t gather_rows(const void *src, int64_t row_bytes, const int *list, void *dst,
+                        const float *ssc, float *dsc, int max_rows, cudaStream_t s) {
+    if (max_rows <= 0) return cudaSuccess;
+    if (row_bytes % 16 || (reinterpret_cast<uintptr_t>(src) & 15) ||
+        (reinterpret_cast<uintptr_t>(dst) & 15))
+        return cudaErrorInvalidValue;
+    const int grid = max_rows < 148 * 4 ? max_rows : 148 * 4;
+    gather_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const uint4 *>(src), row_bytes / 16, list,
+                                       reinterpret_cast<uint4 *>(dst), ssc, dsc);
+    return cudaGetLastError();
 }
 
 cudaError_t ternary_prep(const float *x, int B, int D, const float *norm_f, const float *lmh_norm,

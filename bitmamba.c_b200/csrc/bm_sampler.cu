@@ -48,6 +48,22 @@ struct bm_ctx {
     size_t cap_q;
     float *d_isc;
     size_t cap_isc;
+    // fused lm_head + sampler: the rows' history bits, the GEMM's per-tile
+    // lists, the fallback row lists and the gathered activations of the rows
+    // whose lists cannot decide them
+    uint32_t *d_pb;
+    size_t cap_pb;
+    uint64_t *d_summ;
+    size_t cap_summ;
+    int *d_fb;
+    size_t cap_fb;
+    int *d_nl;
+    size_t cap_nl;
+    unsigned char *d_a2;
+    size_t cap_a2;
+    float *d_isc2;
+    size_t cap_isc2;
+    int sum_ready;
     // small host-buffer calls: one pinned host region and its device mirror,
     // laid out [words | outputs | inputs]; uploaded whole, [words | outputs]
     // read back (one copy each way, one synchronisation)
@@ -120,6 +136,107 @@ int check_batch_args(const bm_ctx_t *ctx, const void *logits, int B, int V, int6
     if (!ctx) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
     return check_args(ctx->max_vocab, logits, B, V, ld, hist, off, knobs, knob_stride, uniform,
                       out_id);
+}
+
+// The sampler's grid: one CTA per SM, never more CTAs than rows.
+int launch_grid(int B, int sms) { return B < sms ? B : sms; }
+
+// The fused lm_head + sampler on activations A ([B x d]: bf16, or int8 with
+// per-row output scales isc) and weights W ([V x d]), on stream s:
+//   1. the rows' history bits (penalty), when there are histories;
+//   2. the GEMM with the summary epilogue: per row and 128 columns the KS
+//      best penalised, scaled logits (greedy and top_k rows), or the row's
+//      logits (rows of the full-vocabulary path);
+//   3. the merge kernel: greedy and top_k rows resolved from the lists; the
+//      rest appended to the fallback lists (fb: to sample; nl: logits
+//      missing, the rows whose lists could not decide them);
+//   4. the nl rows' activations gathered and their logits computed (a GEMM
+//      of those rows only; its row count is read on the device);
+//   5. the sampler on the fb rows (row count and row map read on the device).
+// Steps 4-5 find empty lists in the common case and return at once.  No
+// logits cross HBM for rows the lists decide, and nothing here waits for the
+// host.
+int fused_sample(bm_ctx_t *c, bool i8, const void *A, const float *isc, const void *W, int B,
+                 int d, int V, const int32_t *d_hist, const int64_t *d_hist_off,
+                 const bm_knobs_t *d_knobs, int64_t knob_stride, const float *d_uniform,
+                 int32_t *d_out_id, float *d_out_prob, bm_row_stats_t *d_stats, cudaStream_t s) {
+    const int lists = bml::summary_lists(V);
+    const int pw = (V + 31) / 32;
+    const int64_t ld = ((int64_t)V + 3) / 4 * 4;  // 16-byte rows for the GEMM's stores
+    const size_t esz = i8 ? 1 : 2;
+    int rc;
+    if ((rc = grow(&c->d_summ, &c->cap_summ, (size_t)B * lists * bml::KS)) != BM_OK) return rc;
+    if (d_hist && (rc = grow(&c->d_pb, &c->cap_pb, (size_t)B * pw)) != BM_OK) return rc;
+    if ((rc = grow(&c->d_fb, &c->cap_fb, (size_t)B + 1)) != BM_OK) return rc;
+    if ((rc = grow(&c->d_nl, &c->cap_nl, (size_t)B + 1)) != BM_OK) return rc;
+    if ((rc = grow(&c->d_lm, &c->cap_lm, (size_t)B * (size_t)ld)) != BM_OK) return rc;
+    if ((rc = grow(&c->d_a2, &c->cap_a2, (size_t)B * d * esz)) != BM_OK) return rc;
+    if (i8 && (rc = grow(&c->d_isc2, &c->cap_isc2, (size_t)B)) != BM_OK) return rc;
+    if (!c->sum_ready) {
+        CK(bmk::prepare_summary(c->max_vocab, bml::summary_lists(c->max_vocab), bml::KS));
+        c->sum_ready = 1;
+    }
+    if (d_hist) CK(bml::penalty_bits(d_hist, d_hist_off, B, V, c->d_pb, pw, s));
+    bml::SumArgs sg;
+    sg.pbits = d_hist ? c->d_pb : nullptr;
+    sg.pw = pw;
+    sg.knobs = d_knobs;
+    sg.knob_stride = knob_stride;
+    sg.summ = c->d_summ;
+    if (i8)
+        CK(bml::gemm_i8_summary(static_cast<const int8_t *>(A), static_cast<const int8_t *>(W), B,
+                                V, d, isc, sg, c->d_lm, ld, c->d_err, s));
+    else
+        CK(bml::gemm_bf16_summary(static_cast<const uint16_t *>(A),
+                                  static_cast<const uint16_t *>(W), B, V, d, sg, c->d_lm, ld,
+                                  c->d_err, s));
+    CK(cudaMemsetAsync(c->d_fb, 0, sizeof(int), s));
+    CK(cudaMemsetAsync(c->d_nl, 0, sizeof(int), s));
+    bmk::SumParams sp;
+    sp.summ = c->d_summ;
+    sp.tiles = lists;
+    sp.ks = bml::KS;
+    sp.B = B;
+    sp.V = V;
+    sp.knobs = d_knobs;
+    sp.knob_stride = knob_stride;
+    sp.uniform = d_uniform;
+    sp.out_id = d_out_id;
+    sp.out_prob = d_out_prob;
+    sp.stats = d_stats;
+    sp.fb = c->d_fb;
+    sp.nl = c->d_nl;
+    sp.err = c->d_err;
+    const int mgrid = bmk::MERGE_CTAS_PER_SM * c->sms;
+    CK(bmk::launch_summary(sp, B < mgrid ? B : mgrid, s));
+    CK(bml::gather_rows(A, (int64_t)d * (int64_t)esz, c->d_nl, c->d_a2, isc, c->d_isc2, B, s));
+    if (i8)
+        CK(bml::gemm_i8(reinterpret_cast<const int8_t *>(c->d_a2),
+                        static_cast<const int8_t *>(W), B, V, d, c->d_isc2, c->d_lm, ld, c->d_err,
+                        s, c->d_nl, c->d_nl + 1));
+    else
+        CK(bml::gemm_bf16(reinterpret_cast<const uint16_t *>(c->d_a2),
+                          static_cast<const uint16_t *>(W), B, V, d, c->d_lm, ld, c->d_err, s,
+                          c->d_nl, c->d_nl + 1));
+    bmk::Params p;
+    p.logits = c->d_lm;
+    p.ld = ld;
+    p.B = B;
+    p.V = V;
+    p.hist = d_hist;
+    p.hist_off = d_hist_off;
+    p.knobs = d_knobs;
+    p.knob_stride = knob_stride;
+    p.uniform = d_uniform;
+    p.out_id = d_out_id;
+    p.out_prob = d_out_prob;
+    p.stats = d_stats;
+    p.err = c->d_err;
+    p.sched = c->d_err + 1;
+    p.dB = c->d_fb;
+    p.row_map = c->d_fb + 1;
+    CK(bmk::launch(p, launch_grid(B, c->sms), s));
+    return BM_OK;
 }
 
 // Per-device state of the allocation-free entry point: the scratch address
@@ -239,6 +356,12 @@ void bm_ctx_destroy(bm_ctx_t *c) {
     cudaFree(c->d_q);
     cudaFree(c->d_isc);
     cudaFree(c->d_stage);
+    cudaFree(c->d_pb);
+    cudaFree(c->d_summ);
+    cudaFree(c->d_fb);
+    cudaFree(c->d_nl);
+    cudaFree(c->d_a2);
+    cudaFree(c->d_isc2);
     if (c->h_stage) cudaFreeHost(c->h_stage);
     if (c->stream) cudaStreamDestroy(c->stream);
     free(c);
@@ -335,17 +458,40 @@ int bm_lmhead_sample_batch(bm_ctx_t *c, const float *d_hidden, int B, int d_mode
                            int32_t *d_out_id, float *d_out_prob, bm_row_stats_t *d_stats,
                            void *stream) {
     if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
-    // the sampler's checks first (a logits pointer stands in for the buffer)
-    const int64_t ld = ((int64_t)V + 3) / 4 * 4;  // 16-byte rows for the GEMM's stores
+    // the sampler's checks first (the hidden states stand in for the logits)
+    const int64_t ld = ((int64_t)V + 3) / 4 * 4;
     int rc = check_batch_args(c, d_hidden, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
                               d_uniform, d_out_id);
     if (rc != BM_OK || B == 0) return rc;
+    if (!d_norm_w || !d_W)
+        return fail(BM_ERR_INVALID_ARG, "hidden, norm weight and W must be non-NULL");
+    if (d_model <= 0 || d_model % 8 || d_model > 4096)
+        return fail(BM_ERR_UNSUPPORTED, "d_model = %d (needs a multiple of 8, <= 4096)", d_model);
+    if ((reinterpret_cast<uintptr_t>(d_W) & 15) || (reinterpret_cast<uintptr_t>(d_hidden) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_norm_w) & 15))
+        return fail(BM_ERR_INVALID_ARG, "W / hidden / norm weight not 16-byte aligned");
     CK(cudaSetDevice(c->device));
-    if ((rc = grow(&c->d_lm, &c->cap_lm, (size_t)B * (size_t)ld)) != BM_OK) return rc;
-    rc = bm_lmhead_logits(c, d_hidden, B, d_model, d_norm_w, d_W, V, c->d_lm, ld, stream);
-    if (rc != BM_OK) return rc;
-    return bm_sample_batch(c, c->d_lm, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
-                           d_uniform, d_out_id, d_out_prob, d_stats, stream);
+    if (!c->lm_ready) {
+        CK(bml::prepare());
+        c->lm_ready = 1;
+    }
+    if ((rc = grow(&c->d_a, &c->cap_a, (size_t)B * d_model)) != BM_OK) return rc;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    CK(bml::rmsnorm_bf16(d_hidden, B, d_model, d_norm_w, c->d_a, s));
+    return fused_sample(c, false, c->d_a, nullptr, d_W, B, d_model, V, d_hist, d_hist_off, d_knobs,
+                        knob_stride, d_uniform, d_out_id, d_out_prob, d_stats, s);
+}
+
+int bm_fused_fallback_rows(bm_ctx_t *c, int *n_sampled, int *n_computed) {
+    if (!c || !n_sampled || !n_computed) return fail(BM_ERR_INVALID_ARG, "NULL argument");
+    *n_sampled = *n_computed = 0;
+    if (!c->d_fb) return BM_OK;
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(n_sampled, c->d_fb, sizeof(int), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(n_computed, c->d_nl, sizeof(int), cudaMemcpyDeviceToHost));
+    return BM_OK;
 }
 
 int bm_ternary_unpack(bm_ctx_t *c, const uint8_t *d_packed, int V, int d_model, int8_t *d_w8,
@@ -402,17 +548,30 @@ int bm_ternary_sample_batch(bm_ctx_t *c, const float *d_hidden, int B, int d_mod
                             int64_t knob_stride, const float *d_uniform, int32_t *d_out_id,
                             float *d_out_prob, bm_row_stats_t *d_stats, void *stream) {
     if (!c) return fail(BM_ERR_INVALID_ARG, "ctx is NULL");
-    const int64_t ld = ((int64_t)V + 3) / 4 * 4;  // 16-byte rows for the GEMM's stores
+    const int64_t ld = ((int64_t)V + 3) / 4 * 4;
     int rc = check_batch_args(c, d_hidden, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
                               d_uniform, d_out_id);
     if (rc != BM_OK || B == 0) return rc;
+    if (!d_lmh_norm || !d_w8)
+        return fail(BM_ERR_INVALID_ARG, "hidden, lm_head norm and w8 must be non-NULL");
+    if (d_model <= 0 || d_model % 32 || d_model > 4096)
+        return fail(BM_ERR_UNSUPPORTED, "d_model = %d (needs a multiple of 32, <= 4096)", d_model);
+    if ((reinterpret_cast<uintptr_t>(d_w8) & 15) || (reinterpret_cast<uintptr_t>(d_hidden) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_lmh_norm) & 15) ||
+        (d_norm_f && (reinterpret_cast<uintptr_t>(d_norm_f) & 15)))
+        return fail(BM_ERR_INVALID_ARG, "w8 / hidden / norm weights not 16-byte aligned");
+    if (!(w_scale == w_scale)) return fail(BM_ERR_INVALID_ARG, "w_scale is NaN");
     CK(cudaSetDevice(c->device));
-    if ((rc = grow(&c->d_lm, &c->cap_lm, (size_t)B * (size_t)ld)) != BM_OK) return rc;
-    rc = bm_ternary_logits(c, d_hidden, B, d_model, d_norm_f, d_lmh_norm, d_w8, w_scale, V,
-                           c->d_lm, ld, stream);
-    if (rc != BM_OK) return rc;
-    return bm_sample_batch(c, c->d_lm, B, V, ld, d_hist, d_hist_off, d_knobs, knob_stride,
-                           d_uniform, d_out_id, d_out_prob, d_stats, stream);
+    if (!c->lm_ready) {
+        CK(bml::prepare());
+        c->lm_ready = 1;
+    }
+    if ((rc = grow(&c->d_q, &c->cap_q, (size_t)B * d_model)) != BM_OK) return rc;
+    if ((rc = grow(&c->d_isc, &c->cap_isc, (size_t)B)) != BM_OK) return rc;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    CK(bml::ternary_prep(d_hidden, B, d_model, d_norm_f, d_lmh_norm, w_scale, c->d_q, c->d_isc, s));
+    return fused_sample(c, true, c->d_q, c->d_isc, d_w8, B, d_model, V, d_hist, d_hist_off,
+                        d_knobs, knob_stride, d_uniform, d_out_id, d_out_prob, d_stats, s);
 }
 
 int bm_sample_batch_noalloc(const float *d_logits, int B, int V, int64_t ld,

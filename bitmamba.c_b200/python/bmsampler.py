@@ -93,6 +93,8 @@ def lib():
         L.bm_sample_batch_host.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int64, _P, _P, _P, ctypes.c_int64, _P,
                                            _P, _P, _P]
+        L.bm_fused_fallback_rows.argtypes = [_P, ctypes.POINTER(ctypes.c_int),
+                                             ctypes.POINTER(ctypes.c_int)]
         L.bm_lmhead_logits.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
                                        ctypes.c_int, _P, ctypes.c_int64, _P]
         L.bm_lmhead_sample_batch.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
@@ -229,6 +231,13 @@ class Context:
                                            c(out_prob_ptr) if out_prob_ptr else None,
                                            c(stats_ptr) if stats_ptr else None,
                                            c(stream) if stream else None))
+
+    def fused_fallback_rows(self):
+        """bm_fused_fallback_rows: (rows sampled from logits, rows whose logits
+        took a GEMM of their own) in the last fused call."""
+        a, b = ctypes.c_int(0), ctypes.c_int(0)
+        check(lib().bm_fused_fallback_rows(self._c, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
 
     def ternary_unpack(self, packed_ptr, V, d_model, w8_ptr, stream=None):
         """bm_ternary_unpack on raw device pointers (ints): 2-bit codes -> int8."""

@@ -198,11 +198,21 @@ int bm_lmhead_logits(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
                      float *d_logits, int64_t ld, void *stream);
 
 /*
- * bm_lmhead_logits into a context-owned logits buffer, then bm_sample_batch
- * on it: the fused decode step from the final hidden state to the next
- * token (the sampler's arguments as in bm_sample_batch).  No counterpart in
- * the reference (see bm_lmhead_logits); the sampling part replaces the tail
- * of model_forward_step (src/model.c:1268-1307).
+ * The fused decode step from the final hidden state to the next token: the
+ * final RMSNorm and the bf16 lm_head GEMM of bm_lmhead_logits, and the
+ * sampler of bm_sample_batch on those logits (same arguments, same results),
+ * without the logits making a round trip through HBM for greedy rows and
+ * rows of the top_k path (1 <= top_k <= 256): the GEMM's epilogue keeps, per
+ * row and 256-column output tile, the 8 largest penalised and
+ * temperature-scaled logits, and a merge kernel finishes the reference's
+ * top_k sampler (src/model.c:175-280) from those lists.  A row is finished
+ * from its lists only when no tile's omitted logits can reach the top_k
+ * histogram's cut buckets or the extracted candidates; other rows, and rows
+ * of the full-vocabulary path (their logits are stored by the same GEMM),
+ * go through the logits and bm_sample_batch's kernel, on the device without
+ * a host round trip.  No counterpart in the reference (see
+ * bm_lmhead_logits); the sampling part replaces the tail of
+ * model_forward_step (src/model.c:1268-1307).
  */
 int bm_lmhead_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
                            const float *d_norm_w, const uint16_t *d_W, int V,
@@ -211,6 +221,15 @@ int bm_lmhead_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_mo
                            const float *d_uniform, int32_t *d_out_id,
                            float *d_out_prob, bm_row_stats_t *d_stats,
                            void *stream);
+
+/*
+ * Diagnostics of the last fused call on this context (bm_lmhead_sample_batch
+ * or bm_ternary_sample_batch): rows sampled from logits (n_sampled: rows of
+ * the full-vocabulary path and rows their lists could not decide) and, of
+ * those, rows whose logits took a GEMM of their own (n_computed).
+ * Synchronises the device.  No reference counterpart.
+ */
+int bm_fused_fallback_rows(bm_ctx_t *ctx, int *n_sampled, int *n_computed);
 
 /* ---- the reference's ternary BitLinear lm_head feeding the sampler --------- */
 
@@ -244,10 +263,11 @@ int bm_ternary_logits(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
                       int64_t ld, void *stream);
 
 /*
- * bm_ternary_logits into a context-owned logits buffer, then bm_sample_batch
- * on it: the reference's decode-step tail from the last layer's output to the
- * next token (src/model.c:1222-1307), the sampler's arguments as in
- * bm_sample_batch.
+ * The reference's decode-step tail from the last layer's output to the next
+ * token (src/model.c:1222-1307): bm_ternary_logits and the sampler of
+ * bm_sample_batch on its logits (same arguments, same results), fused as
+ * bm_lmhead_sample_batch is: greedy rows and rows of the top_k path are
+ * finished from the GEMM epilogue's per-tile lists, the others from logits.
  */
 int bm_ternary_sample_batch(bm_ctx_t *ctx, const float *d_hidden, int B, int d_model,
                             const float *d_norm_f, const float *d_lmh_norm,
