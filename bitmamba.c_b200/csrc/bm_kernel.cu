@@ -7,9 +7,10 @@
 //             next row is issued as soon as this row's buffer is free, and the
 //             row after that is prefetched into L2), ragged head/tail by plain
 //             loads with NaN in the junk lanes so every later pass runs over
-//             whole 16-byte slots.  The repetition penalty is applied from a
-//             bitset of the row's distinct history ids (src/model.c:1277-1304);
-//             the pass reduces max / min of the scaled logits
+//             whole 16-byte slots.  The repetition penalty is applied in
+//             place once the row has landed, once per distinct history id (a
+//             bitset; src/model.c:1277-1304); the pass then reduces max / min
+//             of the scaled logits
 //             (src/model.c:156-163) or the greedy argmax (src/model.c:144-154).
 //   top_k     1 <= top_k <= 256: the reference's 128-bucket histogram cut
 //             (src/model.c:181-214) with the candidates above the min_p
@@ -602,6 +603,8 @@ struct Ctx {
     int mark;   // failed rows get id -1 (the allocation-free entry point)
     int summary;  // the merge kernel: candidates come from per-tile lists
     const int32_t *row_map;  // launch row -> row of the per-row arrays (or NULL)
+    unsigned long long *defer_list;  // top_k rows' candidate lists for the merge kernel
+    int *defer_cnt, *defer_rows;     // (NULL: the rows are finished here)
     uint32_t parity;
     // Point the shared-memory fields at the dynamic shared array.  Called at
     // the top of every non-inlined function: pointers that arrive as
@@ -709,8 +712,8 @@ __device__ __forceinline__ float logit_g(const Ctx &c, int e, bool scale) {
 // Consume the freshly loaded row chunk by chunk: apply the penalty, fill the
 // junk lanes of the ragged first / last slots with NaN, and reduce.
 template <bool GREEDY, bool PEN, bool SCALE>
-__device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float &chk, float &gv,
-                                          int &gi) {
+__device__ __forceinline__ void load_pass(Ctx &c, const int32_t *hist, float &mx, float &xmin,
+                                          float &chk, float &gv, int &gi) {
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots, s0 = v->s_int0, s1 = v->s_int1;
     const int V = c.V;
@@ -726,16 +729,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
     float2 chk2 = make_float2(0.0f, 0.0f);
     const float2 it2 = make_float2(inv_temp, inv_temp), z2 = make_float2(0.0f, 0.0f);
     auto consume = [&](int s, float4 x, unsigned valid) {
-        float t[4] = {x.x, x.y, x.z, x.w};
-        if (PEN) {
-            const unsigned nib = (c.bits[s >> 3] >> ((s & 7) * 4)) & 0xfu;
-            if (nib) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    if ((nib >> q) & 1u) t[q] = penalize(t[q], penalty);
-                r4[s] = make_float4(t[0], t[1], t[2], t[3]);
-            }
-        }
+        const float t[4] = {x.x, x.y, x.z, x.w};
         if (!GREEDY && valid == 0xfu) {
             // whole slot: two three-input max / min, two packed checks
             float2 a = make_float2(t[0], t[1]), b = make_float2(t[2], t[3]);
@@ -764,7 +758,7 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
             }
         }
     };
-    auto plain = [&](int s) {
+    auto plain = [&](int s) -> unsigned {
         float t[4];
         unsigned valid = 0;
 #pragma unroll
@@ -776,7 +770,17 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
         }
         const float4 x = make_float4(t[0], t[1], t[2], t[3]);
         r4[s] = x;
-        consume(s, x, valid);
+        return valid;
+    };
+    // lanes of slot s that hold elements
+    auto valid_of = [&](int s) {
+        unsigned valid = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int e = 4 * s + q - sh;
+            valid |= (unsigned)(e >= 0 && e < V) << q;
+        }
+        return valid;
     };
     const int nint = s1 - s0;
     // rows with a bulk-copied interior have at most one ragged head slot and
@@ -799,13 +803,76 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
             }
             cp_async_commit();
         }
-    } else {
+    } else if (!PEN) {
         // tiny row: every slot by plain loads
-        for (int s = threadIdx.x; s < nslots; s += NT) plain(s);
+        for (int s = threadIdx.x; s < nslots; s += NT) {
+            const unsigned vl = plain(s);
+            consume(s, r4[s], vl);
+        }
+    } else {
+        for (int s = threadIdx.x; s < nslots; s += NT) (void)plain(s);
     }
-    // interior, chunk by chunk
     bool ok = true;
-    if (nint > 0) {
+    if (PEN) {
+        // The row lands whole first; then the logit of each distinct history
+        // id is penalised in place by one thread (the bit's previous value
+        // tells the first claimant), and the pass reads the penalised row.
+        // (A per-slot test inside the pass diverges in most warps: about one
+        // lane in 32 holds a history id, and the division is long.)
+        const int h0 = v->h0, h1 = v->h1;
+        int i = h0 + (int)threadIdx.x;
+        int ids[4];
+        auto fetch_ids = [&]() {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ids[q] = (i + q * NT < h1) ? __ldg(&hist[i + q * NT]) : -1;
+        };
+        fetch_ids();  // (in flight during the waits)
+        if (nint > 0) {
+            for (int ch = 0; ch < NCHUNK; ++ch)
+                if (!mbar_wait(&c.mbar[ch], c.parity)) { ok = false; break; }
+            if (es >= 0) cp_async_wait_all();
+        }
+        if (!ok) {
+            atomicOr(c.err, 1);
+            v->fail = 1;
+        }
+        __syncthreads();
+        if (!v->fail) {
+            for (;;) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int id = ids[q];
+                    if (id >= 0 && id < V && !protected_id(id)) {
+                        const int b = id + sh;
+                        const uint32_t m = 1u << (b & 31);
+                        if (!(atomicOr(&c.bits[b >> 5], m) & m)) c.row[b] = penalize(c.row[b], penalty);
+                    }
+                }
+                i += 4 * NT;
+                if (i >= h1) break;
+                fetch_ids();
+            }
+        }
+        __syncthreads();
+        ok = !v->fail;
+        if (ok && nint > 0) {
+            int s = s0 + ((int)threadIdx.x - s0 % NT + NT) % NT;
+            if (s < s1) {
+                float4 xn = r4[s];
+                for (; s < s1; s += NT) {
+                    const float4 x = xn;
+                    if (s + NT < s1) xn = r4[s + NT];
+                    consume(s, x, 0xfu);
+                }
+            }
+        } else if (ok) {
+            for (int s = threadIdx.x; s < nslots; s += NT) consume(s, r4[s], valid_of(s));
+        }
+    } else if (nint > 0) {
+        // interior, chunk by chunk; each thread takes its slots of a chunk
+        // (s = tid mod NT) in ascending order, the next slot's load issued
+        // before the current slot's work (one dependent shared load a slot
+        // would leave the pass latency-bound)
         for (int ch = 0; ch < NCHUNK; ++ch) {
             const int a = s0 + (ch * nint) / NCHUNK, b = s0 + ((ch + 1) * nint) / NCHUNK;
             int s = a + ((int)threadIdx.x - a % NT + NT) % NT;
@@ -816,11 +883,16 @@ __device__ __forceinline__ void load_pass(Ctx &c, float &mx, float &xmin, float 
                 ok = false;
                 break;
             }
-            for (; s < b; s += NT) consume(s, r4[s], 0xfu);
+            float4 xn = r4[s];
+            for (; s < b; s += NT) {
+                const float4 x = xn;
+                if (s + NT < b) xn = r4[s + NT];
+                consume(s, x, 0xfu);
+            }
         }
     }
     if (es >= 0) {
-        cp_async_wait_all();
+        if (!PEN) cp_async_wait_all();
         if (ok) consume(es, r4[es], evld);
     }
     chk = __fadd_rn(chk, __fadd_rn(chk2.x, chk2.y));
@@ -985,6 +1057,23 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
                 }
             }
             __syncthreads();
+            if (c.defer_list && tot > 0 && fabsf(mx) < 1e30f) {
+                // the rest of the row (cut, heap, softmax, sort, draw: short of
+                // parallel work) goes to the merge kernel, which runs several
+                // rows per SM: the complete candidate list (every l >= thr) to
+                // global memory as (bits(l) << 32) | id
+                unsigned long long *dl = c.defer_list + (int64_t)c.rowid * KCAP;
+                for (int q = threadIdx.x; q < tot; q += NT) {
+                    const unsigned long long e = kc[q];
+                    dl[q] = (e << 32) | (e >> 32);
+                }
+                if (threadIdx.x == 0) {
+                    c.defer_cnt[c.rowid] = tot;
+                    c.defer_rows[1 + atomicAdd(&c.defer_rows[0], 1)] = c.rowid;
+                }
+                __syncthreads();
+                return;
+            }
             // histogram of the listed candidates (src/model.c:185-195); the last
             // bucket never decides the cut, so it is not counted
             for (int q = threadIdx.x; q < tot; q += NT) {
@@ -2352,25 +2441,22 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         write_result(c, v->amax, inv_sum, (ncand > 256) ? 6 : 7, ncand, 1, 1);
         return;
     }
-    if (threadIdx.x == 0) {
-        lastb = v->lastb;
-        v->inv_sum = inv_sum;
-        v->S = S;
-        v->adj[0] = v->adj[1] = v->adj[2] = 0.0;
-        v->frk[0] = v->frk[1] = v->frk[2] = INT_MAX;
-        const double tot = S * ip;
-        if (want_cut && v->bc < NB && v->bc_hi == NB) { v->bc_hi = lastb; v->ec = tot; }
+    // Every thread derives the draw range and then the window ranges itself
+    // (no serial step between the barriers); thread 0 publishes the fixed-up
+    // fields once every thread has read the old ones.
+    const int lastb_all = v->lastb;
+    const double mtot = S * ip;
+    int bc_hi = v->bc_hi;
+    double ec = v->ec;
+    if (want_cut && v->bc < NB && bc_hi == NB) { bc_hi = lastb_all; ec = mtot; }
+    {
         // range of new_sum (the cumulative mass where the walk stops), then of
         // r = u * (float)new_sum
-        double lo = tot, hi = tot;
-        if (want_cut && v->bc < NB) { lo = (double)top_p; hi = v->ec; }
+        double lo = mtot, hi = mtot;
+        if (want_cut && v->bc < NB) { lo = (double)top_p; hi = ec; }
         if (want_k && v->bk < NB) { lo = fmin(lo, v->aux0); hi = fmin(hi, v->ek); }
-        v->rlo = fmax((double)v->u * lo * (1.0 - 1e-6) - EPS, 0.0);
-        v->rhi = (double)v->u * hi * (1.0 + 1e-6) + EPS;
-    }
-    __syncthreads();
-    {
-        const double rlo = v->rlo, rhi = v->rhi;
+        const double rlo = fmax((double)v->u * lo * (1.0 - 1e-6) - EPS, 0.0);
+        const double rhi = (double)v->u * hi * (1.0 + 1e-6) + EPS;
         double run = mex;
 #pragma unroll
         for (int q = 0; q < BPT; ++q) {
@@ -2384,33 +2470,43 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         }
     }
     __syncthreads();
-    if (threadIdx.x < 3) {
-        // d range of target t as float bits (inactive: empty), one thread each
-        const int t = threadIdx.x;
-        if (t == 2 && v->bd0 < NB && v->bd_hi == NB) v->bd_hi = v->lastb;
-        const int lo_b = (t == 0) ? (want_cut ? v->bc : NB) : (t == 1) ? (want_k ? v->bk : NB) : v->bd0;
-        const int hi_b = (t == 0) ? v->bc_hi : (t == 1) ? lo_b : v->bd_hi;
-        uint32_t a = 0xffffffffu, sp = 0u;
-        if (lo_b < NB) {
-            const double rw = 1.0 / (double)inv_w;
-            const double dl = ((double)lo_b - 0.5) * rw, dh = ((double)hi_b + 0.5) * rw;
-            a = (lo_b == 0) ? 0u
-                            : __float_as_uint(fmaxf(0.0f, __double2float_rd(dl * (1.0 - 5e-7) - 1.2e-6)));
-            const uint32_t b = (hi_b >= NB - 1)
-                                   ? __float_as_uint(DNC) - 1u
-                                   : min(__float_as_uint(__double2float_ru(dh * (1.0 + 5e-7) + 1.2e-6)),
-                                         __float_as_uint(DNC) - 1u);
-            sp = b - a;
-        }
-        v->ta[t] = a;
-        v->tsp[t] = sp;
-        v->tlo[t] = lo_b;
-        v->thi[t] = hi_b;
+    if (threadIdx.x == 0) {
+        v->inv_sum = inv_sum;
+        v->S = S;
+        v->adj[0] = v->adj[1] = v->adj[2] = 0.0;
+        v->frk[0] = v->frk[1] = v->frk[2] = INT_MAX;
+        v->bc_hi = bc_hi;
+        v->ec = ec;
     }
-    __syncthreads();
     const int bc = want_cut ? v->bc : NB, bk = want_k ? v->bk : NB, bd = v->bd0;
-    const int tlo_b[3] = {v->tlo[0], v->tlo[1], v->tlo[2]}, thi_b[3] = {v->thi[0], v->thi[1], v->thi[2]};
-    const uint32_t ta[3] = {v->ta[0], v->ta[1], v->ta[2]}, tsp[3] = {v->tsp[0], v->tsp[1], v->tsp[2]};
+    int bd_hi = v->bd_hi;
+    if (bd < NB && bd_hi == NB) bd_hi = lastb_all;
+    // d range of target t as float bits (inactive: empty)
+    int tlo_b[3], thi_b[3];
+    uint32_t ta[3], tsp[3];
+    {
+        const double rw = 1.0 / (double)inv_w;
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            const int lo_b = (t == 0) ? bc : (t == 1) ? bk : bd;
+            const int hi_b = (t == 0) ? bc_hi : (t == 1) ? lo_b : bd_hi;
+            uint32_t a = 0xffffffffu, sp = 0u;
+            if (lo_b < NB) {
+                const double dl = ((double)lo_b - 0.5) * rw, dh = ((double)hi_b + 0.5) * rw;
+                a = (lo_b == 0) ? 0u
+                                : __float_as_uint(fmaxf(0.0f, __double2float_rd(dl * (1.0 - 5e-7) - 1.2e-6)));
+                const uint32_t b = (hi_b >= NB - 1)
+                                       ? __float_as_uint(DNC) - 1u
+                                       : min(__float_as_uint(__double2float_ru(dh * (1.0 + 5e-7) + 1.2e-6)),
+                                             __float_as_uint(DNC) - 1u);
+                sp = b - a;
+            }
+            ta[t] = a;
+            tsp[t] = sp;
+            tlo_b[t] = lo_b;
+            thi_b[t] = hi_b;
+        }
+    }
     // distinct ranges for the pass; rng[t] = the range of target t
     uint32_t wl[3] = {0u, 0u, 0u}, ws[3] = {0u, 0u, 0u};
     int rng[3] = {-1, -1, -1};
@@ -2538,6 +2634,8 @@ __device__ __forceinline__ void full_path(Ctx &c) {
             }
         }
     }
+    // (every thread read v->bd_hi before the gather's barriers)
+    if (threadIdx.x == 0) v->bd_hi = bd_hi;
     // release: the row buffer is no longer read on the common path (the list
     // holds the window elements, visible after its barrier; the rare
     // fallbacks read global memory)
@@ -2780,6 +2878,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     c.mark = P.mark_failed_rows;
     c.summary = 0;
     c.row_map = P.row_map;
+    c.defer_list = reinterpret_cast<unsigned long long *>(P.defer_list);
+    c.defer_cnt = P.defer_cnt;
+    c.defer_rows = P.defer_rows;
     c.attach();
     Vars *v = c.v;
     const int V = P.V;
@@ -2843,25 +2944,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         }
         __syncthreads();
         const int sh = v->sh;
-        // penalty bitset over this row's distinct, in-range, unprotected ids
+        // penalty bitset over this row's distinct, in-range, unprotected ids:
+        // cleared here, set by the load pass once the row has landed
         if (v->pen) {
-            const int h0 = v->h0, h1 = v->h1;
             for (int i = tid; i < L.nbw; i += NT) c.bits[i] = 0u;
-            __syncthreads();
-            // four loads in flight per thread before the atomics
-            for (int i = h0 + tid; i < h1; i += 4 * NT) {
-                int ids[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) ids[q] = (i + q * NT < h1) ? __ldg(&P.hist[i + q * NT]) : -1;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int id = ids[q];
-                    if (id >= 0 && id < V && !protected_id(id)) {
-                        const int b = id + sh;
-                        atomicOr(&c.bits[b >> 5], 1u << (b & 31));
-                    }
-                }
-            }
             __syncthreads();
         }
         const bool greedy = v->greedy != 0, pen = v->pen != 0;
@@ -2869,14 +2955,14 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         float mx, xmin, chk, gv;
         int gi;
         if (greedy) {
-            if (pen) load_pass<true, true, false>(c, mx, xmin, chk, gv, gi);
-            else load_pass<true, false, false>(c, mx, xmin, chk, gv, gi);
+            if (pen) load_pass<true, true, false>(c, P.hist, mx, xmin, chk, gv, gi);
+            else load_pass<true, false, false>(c, P.hist, mx, xmin, chk, gv, gi);
         } else if (pen) {
-            if (scale) load_pass<false, true, true>(c, mx, xmin, chk, gv, gi);
-            else load_pass<false, true, false>(c, mx, xmin, chk, gv, gi);
+            if (scale) load_pass<false, true, true>(c, P.hist, mx, xmin, chk, gv, gi);
+            else load_pass<false, true, false>(c, P.hist, mx, xmin, chk, gv, gi);
         } else {
-            if (scale) load_pass<false, false, true>(c, mx, xmin, chk, gv, gi);
-            else load_pass<false, false, false>(c, mx, xmin, chk, gv, gi);
+            if (scale) load_pass<false, false, true>(c, P.hist, mx, xmin, chk, gv, gi);
+            else load_pass<false, false, false>(c, P.hist, mx, xmin, chk, gv, gi);
         }
         // a plain barrier, then the flag from shared memory (measured faster
         // here than a barrier reduction of the flag)
@@ -2986,17 +3072,25 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
     c.mark = 0;
     c.summary = 1;
     c.row_map = nullptr;
+    c.defer_list = nullptr;
+    c.defer_cnt = nullptr;
+    c.defer_rows = nullptr;
     c.g = nullptr;
     c.claim = 0;
     c.parity = 0;
     c.attach();
     Vars *v = c.v;
     const int tid = threadIdx.x;
-    const int ks = P.ks, ne = P.tiles * P.ks;
+    const int ks = P.ks;
+    // flat mode: one complete list per row (counts[row] entries at stride)
+    const bool flat = P.counts != nullptr;
+    const int nrows = P.rows ? min(P.rows[0], P.B) : P.B;
     unsigned long long *se = reinterpret_cast<unsigned long long *>(c.row);
     unsigned long long *kc = reinterpret_cast<unsigned long long *>(c.scr + 4096);
     constexpr unsigned NONE = 0xffffffffu;  // unused list slot
-    for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
+    for (int ri = blockIdx.x; ri < nrows; ri += gridDim.x) {
+        const int row = P.rows ? P.rows[1 + ri] : ri;
+        const int ne = flat ? P.counts[row] : P.tiles * P.ks;
         c.rowid = row;
         if (tid == 0) {
             const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
@@ -3018,9 +3112,16 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
             v->sh = 0;
             v->nslots = 0;
         }
-        // the row's lists, 16-byte loads (ne is even: ks is)
-        const uint4 *src = reinterpret_cast<const uint4 *>(P.summ + (int64_t)row * ne);
-        for (int i = tid; i < ne / 2; i += NT) reinterpret_cast<uint4 *>(se)[i] = src[i];
+        // the row's lists
+        if (flat) {
+            const unsigned long long *src =
+                reinterpret_cast<const unsigned long long *>(P.summ) + (int64_t)row * P.stride;
+            for (int i = tid; i < ne; i += NT) se[i] = src[i];
+        } else {
+            // 16-byte loads (ne is even: ks is)
+            const uint4 *src = reinterpret_cast<const uint4 *>(P.summ + (int64_t)row * ne);
+            for (int i = tid; i < ne / 2; i += NT) reinterpret_cast<uint4 *>(se)[i] = src[i];
+        }
         __syncthreads();
         if (v->greedy) {
             float gv = -1e9f;
@@ -3043,10 +3144,12 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
             // the maximum, and the largest value a full list may have left
             // out (at most its smallest entry)
             float mx = -1e30f, nvk = PINF;
-            for (int t = tid; t < P.tiles; t += NT) {
+            // (a flat list holds every candidate: one list, never "full")
+            const int nl = flat ? 1 : P.tiles, lk = flat ? ne : ks;
+            for (int t = tid; t < nl; t += NT) {
                 float lmax = -PINF, lmin = PINF;
                 int cnt = 0;
-                for (int k = 0; k < ks; ++k) {
+                for (int k = 0; k < lk; ++k) {
                     const unsigned long long e = se[(int64_t)t * ks + k];
                     if ((unsigned)e == NONE) continue;
                     const float x = __uint_as_float((unsigned)(e >> 32));
@@ -3055,7 +3158,7 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
                     ++cnt;
                 }
                 mx = fmaxf(mx, lmax);
-                if (cnt == ks) nvk = fminf(nvk, -lmin);
+                if (!flat && cnt == ks) nvk = fminf(nvk, -lmin);
             }
             block_maxmin_f(mx, nvk, c.red);
             if (tid == 0) {
@@ -3123,7 +3226,7 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
             v->fb = 1;
         }
         __syncthreads();
-        if (tid == 0 && v->fb) {
+        if (tid == 0 && v->fb && P.fb) {
             // left for the full sampler: with its logits (stored by the GEMM)
             // or after a GEMM of its own (a top_k row the lists cannot decide)
             P.fb[1 + atomicAdd(&P.fb[0], 1)] = row;
@@ -3161,7 +3264,8 @@ cudaError_t prepare(int V) {
 }
 
 static size_t summary_smem(int V, int tiles, int ks) {
-    return layout(V).row + (size_t)tiles * ks * 8;
+    const size_t n = (size_t)tiles * ks > (size_t)KCAP ? (size_t)tiles * ks : (size_t)KCAP;
+    return layout(V).row + n * 8;
 }
 
 cudaError_t prepare_summary(int V, int tiles, int ks) {
@@ -3174,7 +3278,7 @@ cudaError_t prepare_summary(int V, int tiles, int ks) {
 }
 
 cudaError_t launch_summary(const SumParams &p, int grid, cudaStream_t s) {
-    if (p.ks % 2 || p.tiles <= 0) return cudaErrorInvalidValue;
+    if (!p.counts && (p.ks % 2 || p.tiles <= 0)) return cudaErrorInvalidValue;
     summary_kernel<<<grid, NT, summary_smem(p.V, p.tiles, p.ks), s>>>(p);
     return cudaGetLastError();
 }
