@@ -700,7 +700,10 @@ def run_lmhead(args):
                                    "note": "rows the per-tile lists could not decide (the "
                                            "rest never had logits in HBM)"},
         "cpu_baseline": cpu, "e2e": None, "clocks": clocks.summary(),
-        "gpu_launches": 3 * args.steps, "parity_sample": parity,
+        # per fused step: RMSNorm (or the ternary prep), history bits, the
+        # summary GEMM, the merge, the fallback gather, the fallback GEMM and
+        # the fallback sampler (the last three find empty row lists and return)
+        "gpu_launches": 7 * args.steps, "parity_sample": parity,
     }
     print(json.dumps(line), flush=True)
     return 0

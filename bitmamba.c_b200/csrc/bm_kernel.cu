@@ -74,7 +74,6 @@ __device__ __forceinline__ bool protected_id(int id) {
 struct __align__(16) Vars {
     double S, cs, aux0, aux1;
     double mc, ec, mk, ek, md;
-    double rlo, rhi;  // range of the draw r (normalised mass)
     double adj[3];    // per target: mass of the band elements above its buckets
     double lbm[3];    // per target: mass of the listed elements in front of its range
     const bm_knobs_t *p_knobs;  // launch parameters the row release prefetches from
@@ -96,9 +95,7 @@ struct __align__(16) Vars {
     int bc, bk, bd0, bc_hi, bd_hi, next_row, lastb;
     int amax;       // index of the maximum (lowest among equal maxima)
     uint32_t h0b;   // fixed-point mass sum of bucket 0
-    int frk[3];              // per target: rank of its range's first listed element
-    uint32_t ta[3], tsp[3];  // per target: d range as float bits (start, span)
-    int tlo[3], thi[3];      // per target: bucket range
+    int frk[3];   // per target: rank of its range's first listed element
 };
 
 struct Layout {
@@ -603,8 +600,6 @@ struct Ctx {
     int mark;   // failed rows get id -1 (the allocation-free entry point)
     int summary;  // the merge kernel: candidates come from per-tile lists
     const int32_t *row_map;  // launch row -> row of the per-row arrays (or NULL)
-    unsigned long long *defer_list;  // top_k rows' candidate lists for the merge kernel
-    int *defer_cnt, *defer_rows;     // (NULL: the rows are finished here)
     uint32_t parity;
     // Point the shared-memory fields at the dynamic shared array.  Called at
     // the top of every non-inlined function: pointers that arrive as
@@ -1057,23 +1052,6 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
                 }
             }
             __syncthreads();
-            if (c.defer_list && tot > 0 && fabsf(mx) < 1e30f) {
-                // the rest of the row (cut, heap, softmax, sort, draw: short of
-                // parallel work) goes to the merge kernel, which runs several
-                // rows per SM: the complete candidate list (every l >= thr) to
-                // global memory as (bits(l) << 32) | id
-                unsigned long long *dl = c.defer_list + (int64_t)c.rowid * KCAP;
-                for (int q = threadIdx.x; q < tot; q += NT) {
-                    const unsigned long long e = kc[q];
-                    dl[q] = (e << 32) | (e >> 32);
-                }
-                if (threadIdx.x == 0) {
-                    c.defer_cnt[c.rowid] = tot;
-                    c.defer_rows[1 + atomicAdd(&c.defer_rows[0], 1)] = c.rowid;
-                }
-                __syncthreads();
-                return;
-            }
             // histogram of the listed candidates (src/model.c:185-195); the last
             // bucket never decides the cut, so it is not counted
             for (int q = threadIdx.x; q < tot; q += NT) {
@@ -2878,9 +2856,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
     c.mark = P.mark_failed_rows;
     c.summary = 0;
     c.row_map = P.row_map;
-    c.defer_list = reinterpret_cast<unsigned long long *>(P.defer_list);
-    c.defer_cnt = P.defer_cnt;
-    c.defer_rows = P.defer_rows;
     c.attach();
     Vars *v = c.v;
     const int V = P.V;
@@ -3072,25 +3047,17 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
     c.mark = 0;
     c.summary = 1;
     c.row_map = nullptr;
-    c.defer_list = nullptr;
-    c.defer_cnt = nullptr;
-    c.defer_rows = nullptr;
     c.g = nullptr;
     c.claim = 0;
     c.parity = 0;
     c.attach();
     Vars *v = c.v;
     const int tid = threadIdx.x;
-    const int ks = P.ks;
-    // flat mode: one complete list per row (counts[row] entries at stride)
-    const bool flat = P.counts != nullptr;
-    const int nrows = P.rows ? min(P.rows[0], P.B) : P.B;
+    const int ks = P.ks, ne = P.tiles * P.ks;
     unsigned long long *se = reinterpret_cast<unsigned long long *>(c.row);
     unsigned long long *kc = reinterpret_cast<unsigned long long *>(c.scr + 4096);
     constexpr unsigned NONE = 0xffffffffu;  // unused list slot
-    for (int ri = blockIdx.x; ri < nrows; ri += gridDim.x) {
-        const int row = P.rows ? P.rows[1 + ri] : ri;
-        const int ne = flat ? P.counts[row] : P.tiles * P.ks;
+    for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
         c.rowid = row;
         if (tid == 0) {
             const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
@@ -3112,16 +3079,9 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
             v->sh = 0;
             v->nslots = 0;
         }
-        // the row's lists
-        if (flat) {
-            const unsigned long long *src =
-                reinterpret_cast<const unsigned long long *>(P.summ) + (int64_t)row * P.stride;
-            for (int i = tid; i < ne; i += NT) se[i] = src[i];
-        } else {
-            // 16-byte loads (ne is even: ks is)
-            const uint4 *src = reinterpret_cast<const uint4 *>(P.summ + (int64_t)row * ne);
-            for (int i = tid; i < ne / 2; i += NT) reinterpret_cast<uint4 *>(se)[i] = src[i];
-        }
+        // the row's lists, 16-byte loads (ne is even: ks is)
+        const uint4 *src = reinterpret_cast<const uint4 *>(P.summ + (int64_t)row * ne);
+        for (int i = tid; i < ne / 2; i += NT) reinterpret_cast<uint4 *>(se)[i] = src[i];
         __syncthreads();
         if (v->greedy) {
             float gv = -1e9f;
@@ -3144,12 +3104,10 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
             // the maximum, and the largest value a full list may have left
             // out (at most its smallest entry)
             float mx = -1e30f, nvk = PINF;
-            // (a flat list holds every candidate: one list, never "full")
-            const int nl = flat ? 1 : P.tiles, lk = flat ? ne : ks;
-            for (int t = tid; t < nl; t += NT) {
+            for (int t = tid; t < P.tiles; t += NT) {
                 float lmax = -PINF, lmin = PINF;
                 int cnt = 0;
-                for (int k = 0; k < lk; ++k) {
+                for (int k = 0; k < ks; ++k) {
                     const unsigned long long e = se[(int64_t)t * ks + k];
                     if ((unsigned)e == NONE) continue;
                     const float x = __uint_as_float((unsigned)(e >> 32));
@@ -3158,7 +3116,7 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
                     ++cnt;
                 }
                 mx = fmaxf(mx, lmax);
-                if (!flat && cnt == ks) nvk = fminf(nvk, -lmin);
+                if (cnt == ks) nvk = fminf(nvk, -lmin);
             }
             block_maxmin_f(mx, nvk, c.red);
             if (tid == 0) {
@@ -3226,7 +3184,7 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
             v->fb = 1;
         }
         __syncthreads();
-        if (tid == 0 && v->fb && P.fb) {
+        if (tid == 0 && v->fb) {
             // left for the full sampler: with its logits (stored by the GEMM)
             // or after a GEMM of its own (a top_k row the lists cannot decide)
             P.fb[1 + atomicAdd(&P.fb[0], 1)] = row;
@@ -3264,8 +3222,7 @@ cudaError_t prepare(int V) {
 }
 
 static size_t summary_smem(int V, int tiles, int ks) {
-    const size_t n = (size_t)tiles * ks > (size_t)KCAP ? (size_t)tiles * ks : (size_t)KCAP;
-    return layout(V).row + n * 8;
+    return layout(V).row + (size_t)tiles * ks * 8;
 }
 
 cudaError_t prepare_summary(int V, int tiles, int ks) {
@@ -3278,7 +3235,7 @@ cudaError_t prepare_summary(int V, int tiles, int ks) {
 }
 
 cudaError_t launch_summary(const SumParams &p, int grid, cudaStream_t s) {
-    if (!p.counts && (p.ks % 2 || p.tiles <= 0)) return cudaErrorInvalidValue;
+    if (p.ks % 2 || p.tiles <= 0) return cudaErrorInvalidValue;
     summary_kernel<<<grid, NT, summary_smem(p.V, p.tiles, p.ks), s>>>(p);
     return cudaGetLastError();
 }

@@ -42,14 +42,6 @@ struct Params {
     const int32_t *row_map = nullptr;  // optional: launch row i is row
                                        // row_map[i] of every per-row array,
                                        // the logits included
-    // optional: rows of the top_k path with min_p > 0 leave their complete
-    // candidate list (every l >= thr, (bits(l) << 32) | id) at defer_list +
-    // row * KCAP with its length in defer_cnt[row], append the row to
-    // defer_rows = [count, rows...] and leave their results to the merge
-    // kernel (launch_summary in flat mode)
-    uint64_t *defer_list = nullptr;
-    int *defer_cnt = nullptr;
-    int *defer_rows = nullptr;
 };
 
 // The merge kernel of the fused lm_head + sampler: per row, the per-tile
@@ -57,14 +49,10 @@ struct Params {
 // 32) | id) finish the greedy argmax or the top_k path; rows they cannot
 // decide, and rows of the full-vocabulary path, are appended to the fallback
 // lists (fb = [count, rows...]: to be sampled from logits; nl = [count,
-// rows...]: their logits still to be computed).  Flat mode (counts set): the
-// complete candidate lists the sampling kernel left for its deferred rows.
+// rows...]: their logits still to be computed).
 struct SumParams {
     const uint64_t *summ;
     int tiles, ks;
-    const int *counts = nullptr;  // flat mode: complete lists, counts[row] entries
-    int64_t stride = 0;           // at summ + row * stride
-    const int *rows = nullptr;    // optional: only the rows [count, rows...]
     int B, V;
     const bm_knobs_t *knobs;
     int64_t knob_stride;

@@ -64,14 +64,6 @@ struct bm_ctx {
     float *d_isc2;
     size_t cap_isc2;
     int sum_ready;
-    // the sampler's deferred top_k rows: their candidate lists (KCAP entries
-    // a row), list lengths and the row list [count, rows...]
-    uint64_t *d_dl;
-    size_t cap_dl;
-    int *d_dcnt;
-    size_t cap_dcnt;
-    int *d_drows;
-    size_t cap_drows;
     // small host-buffer calls: one pinned host region and its device mirror,
     // laid out [words | outputs | inputs]; uploaded whole, [words | outputs]
     // read back (one copy each way, one synchronisation)
@@ -370,9 +362,6 @@ void bm_ctx_destroy(bm_ctx_t *c) {
     cudaFree(c->d_nl);
     cudaFree(c->d_a2);
     cudaFree(c->d_isc2);
-    cudaFree(c->d_dl);
-    cudaFree(c->d_dcnt);
-    cudaFree(c->d_drows);
     if (c->h_stage) cudaFreeHost(c->h_stage);
     if (c->stream) cudaStreamDestroy(c->stream);
     free(c);
@@ -429,47 +418,7 @@ int bm_sample_batch(bm_ctx_t *c, const float *d_logits, int B, int V, int64_t ld
     p.sched = c->d_err + 1;
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     int grid = B < c->sms ? B : c->sms;
-    // With more rows than SMs, the top_k rows' tails (cut, heap, softmax,
-    // sort, draw: little parallel work, one row per SM) move to the merge
-    // kernel, which runs several rows per SM at once; the sampler hands each
-    // such row over as its complete candidate list.
-    const bool defer = B > c->sms;
-    if (defer) {
-        if ((rc = grow(&c->d_dl, &c->cap_dl, (size_t)B * bmk::KCAP)) != BM_OK) return rc;
-        if ((rc = grow(&c->d_dcnt, &c->cap_dcnt, (size_t)B)) != BM_OK) return rc;
-        if ((rc = grow(&c->d_drows, &c->cap_drows, (size_t)B + 1)) != BM_OK) return rc;
-        if (!c->sum_ready) {
-            CK(bmk::prepare_summary(c->max_vocab, bml::summary_lists(c->max_vocab), bml::KS));
-            c->sum_ready = 1;
-        }
-        CK(cudaMemsetAsync(c->d_drows, 0, sizeof(int), s));
-        p.defer_list = c->d_dl;
-        p.defer_cnt = c->d_dcnt;
-        p.defer_rows = c->d_drows;
-    }
     CK(bmk::launch(p, grid, s));
-    if (defer) {
-        bmk::SumParams sp;
-        sp.summ = c->d_dl;
-        sp.tiles = 0;
-        sp.ks = 0;
-        sp.counts = c->d_dcnt;
-        sp.stride = bmk::KCAP;
-        sp.rows = c->d_drows;
-        sp.B = B;
-        sp.V = V;
-        sp.knobs = d_knobs;
-        sp.knob_stride = knob_stride;
-        sp.uniform = d_uniform;
-        sp.out_id = d_out_id;
-        sp.out_prob = d_out_prob;
-        sp.stats = d_stats;
-        sp.fb = nullptr;
-        sp.nl = nullptr;
-        sp.err = c->d_err;
-        const int mgrid = bmk::MERGE_CTAS_PER_SM * c->sms;
-        CK(bmk::launch_summary(sp, B < mgrid ? B : mgrid, s));
-    }
     return BM_OK;
 }
 
