@@ -649,32 +649,36 @@ __device__ __forceinline__ void prefetch_row(const float *g, int V) {
 }
 
 // The row buffer is no longer read for this row: let the next row's copy in.
+// Warp 0 issues the copies (one lane per chunk); warp 1 the prefetches, so
+// the two sets of instructions do not run one after the other.
 __device__ __forceinline__ void release_row(Ctx &c) {
+    if (threadIdx.x == 0) {
+        // the row claimed when this one started (thread 0 holds it)
+        c.v->released = 1;
+        c.v->next_row = c.claim;
+    }
     fence_proxy_async();
     __syncthreads();
-    if (threadIdx.x < 32) {
-        // the row claimed when this one started (thread 0 holds it); one lane
-        // per chunk issues the copies
-        const int next_row = __shfl_sync(FULL, c.claim, 0);
-        const int lane = threadIdx.x;
-        if (lane == 0) {
-            c.v->released = 1;
-            c.v->next_row = next_row;
-        }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < 2) {
+        const int next_row = c.v->next_row;
         if (next_row < c.B) {
             const int nr = c.row_map ? (int)c.row_map[next_row] : next_row;
-            if (lane < NCHUNK)
-                issue_chunk(c.logits + (int64_t)nr * c.ld, c.V, c.mbar, c.row, lane);
-            // the next row's knobs, uniform and history offsets into L1
-            const Vars *v = c.v;
-            if (lane == NCHUNK + 1) prefetch_l1(v->p_knobs + (int64_t)nr * v->p_knob_stride);
-            if (lane == NCHUNK + 2 && v->p_uniform) prefetch_l1(v->p_uniform + nr);
-            if (lane == NCHUNK + 3 && v->p_hist_off) prefetch_l1(v->p_hist_off + nr);
-            // warm L2 with the row claimed about one round later
-            const int pre = next_row + (int)gridDim.x;
-            if (lane == NCHUNK && pre < c.B)
-                prefetch_row(c.logits + (int64_t)(c.row_map ? (int)c.row_map[pre] : pre) * c.ld,
-                             c.V);
+            if (warp == 0) {
+                if (lane < NCHUNK)
+                    issue_chunk(c.logits + (int64_t)nr * c.ld, c.V, c.mbar, c.row, lane);
+            } else {
+                // the next row's knobs, uniform and history offsets into L1
+                const Vars *v = c.v;
+                if (lane == 1) prefetch_l1(v->p_knobs + (int64_t)nr * v->p_knob_stride);
+                if (lane == 2 && v->p_uniform) prefetch_l1(v->p_uniform + nr);
+                if (lane == 3 && v->p_hist_off) prefetch_l1(v->p_hist_off + nr);
+                // warm L2 with the row claimed about one round later
+                const int pre = next_row + (int)gridDim.x;
+                if (lane == 0 && pre < c.B)
+                    prefetch_row(c.logits + (int64_t)(c.row_map ? (int)c.row_map[pre] : pre) * c.ld,
+                                 c.V);
+            }
         }
     }
 }
@@ -914,7 +918,7 @@ __device__ __noinline__ int guard_argmax(Ctx c) {
 
 // ---------------------------------------------------------------- top_k --
 template <bool SCALE>
-__device__ __forceinline__ void topk_path(Ctx &c) {
+__device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots, V = c.V, k = v->k;
@@ -1009,32 +1013,68 @@ __device__ __forceinline__ void topk_path(Ctx &c) {
         if (threadIdx.x == 0) v->kcnt = n2;
         __syncthreads();
     } else if (v->min_p > 0.0f) {
-        uint32_t *mk = reinterpret_cast<uint32_t *>(kc);  // MASKW words per thread
-        uint32_t w = 0;
-        int i = 0;
-        for (int s = threadIdx.x; s < nslots; s += NT, ++i) {
+        // Each thread marks its candidates, a bit per element, in registers.
+        // A thread whose own maximum in the load pass (tmax: the same scaled
+        // values of the same interior slots) lies below thr has none there
+        // and skips its slots; the ragged head / tail slots were consumed by
+        // other threads in the load pass, so their threads here always scan.
+        bool edge = (int)threadIdx.x < v->s_int0;
+        for (int s = v->s_int1; s < nslots; ++s) edge |= (s % NT) == (int)threadIdx.x;
+        const bool need = edge || !(tmax < thr);
+        // candidate bits of slot s: bit q for element q of the slot
+        auto bits4 = [&](int s) -> uint32_t {
             const float4 x = r4[s];
-            float t[4] = {x.x, x.y, x.z, x.w};
+            const float t[4] = {x.x, x.y, x.z, x.w};
             uint32_t b4 = 0;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
                 b4 |= (l >= thr ? 1u : 0u) << q;
             }
-            w |= b4 << (4 * (i & 7));
-            if ((i & 7) == 7) { mk[(i >> 3) * NT + threadIdx.x] = w; w = 0; }
+            return b4;
+        };
+        uint32_t wv[MASKW] = {0u, 0u, 0u, 0u};
+        const uint32_t scanners = __ballot_sync(FULL, need);
+        if (__popc(scanners) <= 8) {
+            // few threads of this warp have candidates: the whole warp scans
+            // each one's slots (lane i takes its slot i), and groups of 8
+            // lanes assemble its mask words (word q = slots 8q..8q+7)
+            for (uint32_t m = scanners; m; m &= m - 1) {
+                const int ln = __ffs(m) - 1;
+                const int s = (int)(threadIdx.x & ~31u) + ln + lane * NT;
+                uint32_t w = (s < nslots) ? bits4(s) << (4 * (lane & 7)) : 0u;
+                w |= __shfl_xor_sync(FULL, w, 1);
+                w |= __shfl_xor_sync(FULL, w, 2);
+                w |= __shfl_xor_sync(FULL, w, 4);
+#pragma unroll
+                for (int q = 0; q < MASKW; ++q) {
+                    const uint32_t wq = __shfl_sync(FULL, w, 8 * q);
+                    if (lane == ln) wv[q] = wq;
+                }
+            }
+        } else if (need) {
+            uint32_t w = 0;
+            int i = 0;
+            for (int s = threadIdx.x; s < nslots; s += NT, ++i) {
+                w |= bits4(s) << (4 * (i & 7));
+                if ((i & 7) == 7) {
+#pragma unroll
+                    for (int q = 0; q < MASKW; ++q)
+                        if (q == (i >> 3)) wv[q] = w;
+                    w = 0;
+                }
+            }
+            if (i & 7) {
+#pragma unroll
+                for (int q = 0; q < MASKW; ++q)
+                    if (q == (i >> 3)) wv[q] = w;
+            }
         }
-        if (i & 7) mk[(i >> 3) * NT + threadIdx.x] = w;
-        const int nw = (i + 7) >> 3;
-        uint32_t wv[MASKW];
         int nb = 0;
 #pragma unroll
-        for (int q = 0; q < MASKW; ++q) {
-            wv[q] = (q < nw) ? mk[q * NT + threadIdx.x] : 0u;
-            nb += __popc(wv[q]);
-        }
+        for (int q = 0; q < MASKW; ++q) nb += __popc(wv[q]);
         int tot;
-        int j = block_xscan_i(nb, tot, c.red);  // (its barriers end the mask reads)
+        int j = block_xscan_i(nb, tot, c.red);
         if (tot <= KCAP) {
             listed = true;
             for (int q = 0; q < 8 * HB; q += NT)
@@ -2992,8 +3032,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             }
             __syncthreads();
             if (v->k > 0) {
-                if (scale) topk_path<true>(c);
-                else topk_path<false>(c);
+                if (scale) topk_path<true>(c, lmx);
+                else topk_path<false>(c, lmx);
             } else {
                 if (scale) full_path<true>(c);
                 else full_path<false>(c);
@@ -3179,7 +3219,7 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
                 }
             }
             __syncthreads();
-            topk_path<false>(c);
+            topk_path<false>(c, PINF);  // (the lists: no candidate scan)
         } else if (tid == 0) {
             v->fb = 1;
         }
