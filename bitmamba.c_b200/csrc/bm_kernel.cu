@@ -92,6 +92,7 @@ struct __align__(16) Vars {
     int kcut, kcnt, n_cand, own;
     int clean, ln0, ln2, ln3;
     int sel_found, sel_j, res_id, n_final;
+    int wt;         // the one-warp top_k tail decided the row
     int bc, bk, bd0, bc_hi, bd_hi, next_row, lastb;
     int amax;       // index of the maximum (lowest among equal maxima)
     uint32_t h0b;   // fixed-point mass sum of bucket 0
@@ -549,6 +550,151 @@ __device__ __forceinline__ void sort_reg(unsigned long long *a, int n) {
     __syncthreads();  // the last exchange's reads are done
     if (t < n) a[t] = k;
     __syncthreads();
+}
+
+__device__ __forceinline__ unsigned long long shfl_xor64(unsigned long long v, int m) {
+    const unsigned lo = __shfl_xor_sync(FULL, (unsigned)v, m);
+    const unsigned hi = __shfl_xor_sync(FULL, (unsigned)(v >> 32), m);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+// The end of the top_k path for up to 64 candidates when the survivors'
+// order is their value order, on one warp with everything in registers (two
+// entries per lane: entry x = 2 * lane + r):
+//   - the candidates (kc: (id << 32) | bits(l)) sorted by value descending,
+//     ties by id (a bitonic network); the k survivors are the first
+//     min(n, k).  The reference's heap (src/model.c:239-254) holds exactly
+//     these k largest when no two of the k + 1 largest values are equal,
+//     and its stable sort by probability (src/model.c:275-276) then lists
+//     them in value order when no two probabilities are equal;
+//   - the survivor softmax (src/model.c:257-269): expf(l - max), fp64 sum,
+//     p = e * (1 / (float) sum);
+//   - filter_and_sample (src/model.c:72-118): the nucleus cut (cumulative
+//     fp64 sum >= top_p), r = u * (float) cut sum, the first r < cumulative.
+// The fp64 sums are exact in any order when every term is a multiple of
+// ulp(smallest term) below 2^53 of them (e >= 2^-22, p >= 2^-29); returns
+// false (nothing decided) when a value or probability tie, a +inf value or
+// an inexact sum makes the order matter: the block path then decides.
+__device__ __forceinline__ bool warp_tail(const unsigned long long *kc, int n, int k, float top_p,
+                                          float u, int lane, int &res_id, float &res_p,
+                                          int &res_nf) {
+    unsigned long long key[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int x = 2 * lane + r;
+        key[r] = ~0ull;
+        if (x < n) {
+            const unsigned long long e = kc[x];
+            const unsigned b = (unsigned)(e & 0xffffffffu);
+            const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+            key[r] = ((unsigned long long)(~ord) << 32) | (unsigned)(e >> 32);
+        }
+    }
+    // ascending bitonic sort of the 64 keys (padding ~0 sorts last)
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            unsigned long long o[2];
+            if (j == 1) {
+                o[0] = key[1];
+                o[1] = key[0];
+            } else {
+                o[0] = shfl_xor64(key[0], j >> 1);
+                o[1] = shfl_xor64(key[1], j >> 1);
+            }
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int x = 2 * lane + r;
+                const bool up = (x & size) == 0, lower = (x & j) == 0;
+                key[r] = (lower == up) ? (o[r] < key[r] ? o[r] : key[r])
+                                       : (o[r] > key[r] ? o[r] : key[r]);
+            }
+        }
+    }
+    const int ns = min(n, k), m = min(n, k + 1);
+    // equal values among the first k + 1, or a +inf maximum
+    const unsigned hi0 = (unsigned)(key[0] >> 32), hi1 = (unsigned)(key[1] >> 32);
+    const unsigned nxt = __shfl_down_sync(FULL, hi0, 1);
+    bool tie = (2 * lane + 1 < m && hi0 == hi1) || (2 * lane + 2 < m && hi1 == nxt);
+    if (lane == 0) tie |= (~hi0) == 0xff800000u;
+    if (__any_sync(FULL, tie)) return false;
+    float l[2], e[2], p[2];
+    int id[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const unsigned ord = ~(unsigned)(key[r] >> 32);
+        l[r] = __uint_as_float((ord & 0x80000000u) ? (ord ^ 0x80000000u) : ~ord);
+        id[r] = (int)(unsigned)(key[r] & 0xffffffffu);
+    }
+    const float lm = __shfl_sync(FULL, l[0], 0);  // the largest survivor
+    double s = 0.0;
+    float emin = PINF;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const bool sv = 2 * lane + r < ns;
+        e[r] = sv ? expf(__fsub_rn(l[r], lm)) : 0.0f;
+        s += (double)e[r];
+        if (sv && e[r] > 0.0f) emin = fminf(emin, e[r]);
+    }
+    emin = warp_min(emin);
+    if (!(emin >= 0x1p-22f)) return false;
+    const double S = warp_sum(s);
+    const float inv = __fdiv_rn(1.0f, __double2float_rn(S));
+    float pmin = PINF;
+    double ls = 0.0;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const bool sv = 2 * lane + r < ns;
+        p[r] = sv ? __fmul_rn(e[r], inv) : 0.0f;
+        ls += (double)p[r];
+        if (sv && p[r] > 0.0f) pmin = fminf(pmin, p[r]);
+    }
+    // equal probabilities: the stable sort keeps heap order among them
+    const float pn = __shfl_down_sync(FULL, p[0], 1);
+    const bool ptie = (2 * lane + 1 < ns && p[0] == p[1]) || (2 * lane + 2 < ns && p[1] == pn);
+    if (__any_sync(FULL, ptie)) return false;
+    pmin = warp_min(pmin);
+    if (!(pmin >= 0x1p-29f)) return false;
+    const double inc = warp_iscan(ls, lane);
+    const double pre = inc - ls;
+    // nucleus cut: the first entry whose cumulative sum reaches top_p
+    int hit = INT_MAX;
+    double hcs = 0.0, cs = pre;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (2 * lane + r < ns && hit == INT_MAX) {
+            cs += (double)p[r];
+            if (cs >= (double)top_p) { hit = 2 * lane + r; hcs = cs; }
+        }
+    }
+    int nf = ns;
+    double cs_cut = __shfl_sync(FULL, inc, 31);
+    const int best = warp_imin(hit);
+    if (best != INT_MAX) {
+        cs_cut = __shfl_sync(FULL, hcs, best >> 1);
+        nf = best + 1;
+    }
+    // the draw: the first entry of the nucleus whose cumulative sum exceeds r
+    const float rr = __fmul_rn(u, __double2float_rn(cs_cut));
+    int hit2 = INT_MAX;
+    cs = pre;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (2 * lane + r < nf && hit2 == INT_MAX) {
+            cs += (double)p[r];
+            if ((double)rr < cs) hit2 = 2 * lane + r;
+        }
+    }
+    int pos = warp_imin(hit2);
+    if (pos == INT_MAX) pos = nf - 1;
+    const int sl = pos >> 1;
+    const int i0 = __shfl_sync(FULL, id[0], sl), i1 = __shfl_sync(FULL, id[1], sl);
+    const float p0 = __shfl_sync(FULL, p[0], sl), p1 = __shfl_sync(FULL, p[1], sl);
+    res_id = (pos & 1) ? i1 : i0;
+    res_p = (pos & 1) ? p1 : p0;
+    res_nf = nf;
+    return true;
 }
 
 // Min-heap sift-down on parallel arrays, exactly src/model.c:50-66
@@ -1256,6 +1402,25 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
         const int id = guard_argmax(c);
         write_result(c, id, 1.0f, 2, 0, 0, 0);
         return;
+    }
+    if (n <= 64 && v->top_p < 1.0f) {
+        // short lists in value order: one warp, no block barrier
+        if (warp == 0) {
+            int rid = 0, rnf = 0;
+            float rp = 0.0f;
+            const bool ok = warp_tail(kc, n, k, v->top_p, v->u, lane, rid, rp, rnf);
+            if (lane == 0) {
+                v->wt = ok ? 1 : 0;
+                v->res_id = rid;
+                v->res_p = rp;
+                v->n_final = rnf;
+            }
+        }
+        __syncthreads();
+        if (v->wt) {
+            write_result(c, v->res_id, v->res_p, 3, n, v->n_final, 1);
+            return;
+        }
     }
     float *hv = reinterpret_cast<float *>(c.scr);         // 256 (reuses the histogram)
     int *hi = reinterpret_cast<int *>(c.scr + 1024);      // 256
