@@ -73,6 +73,9 @@ __device__ __forceinline__ bool protected_id(int id) {
 
 struct __align__(16) Vars {
     double S, cs, aux0, aux1;
+    int64_t nh[2];    // the next row's history offsets, knobs and uniform,
+    bm_knobs_t nk;    // copied in asynchronously at the release
+    float nu;
     double mc, ec, mk, ek, md;
     double adj[3];    // per target: mass of the band elements above its buckets
     double lbm[3];    // per target: mass of the listed elements in front of its range
@@ -152,8 +155,8 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-__device__ __forceinline__ void prefetch_l1(const void *p) {
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+__device__ __forceinline__ void prefetch_l2_line(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
@@ -814,11 +817,20 @@ __device__ __forceinline__ void release_row(Ctx &c) {
                 if (lane < NCHUNK)
                     issue_chunk(c.logits + (int64_t)nr * c.ld, c.V, c.mbar, c.row, lane);
             } else {
-                // the next row's knobs, uniform and history offsets into L1
-                const Vars *v = c.v;
-                if (lane == 1) prefetch_l1(v->p_knobs + (int64_t)nr * v->p_knob_stride);
-                if (lane == 2 && v->p_uniform) prefetch_l1(v->p_uniform + nr);
-                if (lane == 3 && v->p_hist_off) prefetch_l1(v->p_hist_off + nr);
+                // the next row's knobs, uniform and history offsets into the
+                // staging fields (4-byte asynchronous copies; waited for at
+                // the end of this row)
+                Vars *v = c.v;
+                if (lane >= 8 && lane < 16)
+                    cp_async4(reinterpret_cast<uint32_t *>(&v->nk) + (lane - 8),
+                              reinterpret_cast<const uint32_t *>(v->p_knobs +
+                                                                 (int64_t)nr * v->p_knob_stride) +
+                                  (lane - 8));
+                if (lane == 16 && v->p_uniform) cp_async4(&v->nu, v->p_uniform + nr);
+                if (lane >= 17 && lane < 21 && v->p_hist_off)
+                    cp_async4(reinterpret_cast<uint32_t *>(v->nh) + (lane - 17),
+                              reinterpret_cast<const uint32_t *>(v->p_hist_off + nr) + (lane - 17));
+                if (lane >= 8 && lane < 21) cp_async_commit();
                 // warm L2 with the row claimed about one round later
                 const int pre = next_row + (int)gridDim.x;
                 if (lane == 0 && pre < c.B)
@@ -3106,7 +3118,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             v->released = 0;
             v->fail2 = 0;
             v->amax = INT_MAX;
-            const bm_knobs_t kn = P.knobs[(int64_t)row * P.knob_stride];
+            // (rows after a CTA's first: the values staged at the release)
+            const bool st = it > 0;
+            const bm_knobs_t kn = st ? v->nk : P.knobs[(int64_t)row * P.knob_stride];
             v->temp = kn.temp;
             v->penalty = kn.penalty;
             v->min_p = kn.min_p;
@@ -3114,10 +3128,13 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             v->top_k = kn.top_k;
             v->inv_temp = kn.inv_temp;
             v->log_min_p = kn.log_min_p;
-            v->u = P.uniform ? P.uniform[row] : 0.0f;
+            v->u = P.uniform ? (st ? v->nu : P.uniform[row]) : 0.0f;
             v->greedy = (kn.temp < 0.05f);  // src/model.c:144
             int h0 = 0, h1 = 0;
-            if (P.hist && P.hist_off) { h0 = (int)P.hist_off[row]; h1 = (int)P.hist_off[row + 1]; }
+            if (P.hist && P.hist_off) {
+                h0 = (int)(st ? v->nh[0] : P.hist_off[row]);
+                h1 = (int)(st ? v->nh[1] : P.hist_off[row + 1]);
+            }
             v->pen = (h1 > h0) && (kn.penalty > 0.0f) && (kn.penalty != 1.0f);
             v->h0 = h0;
             v->h1 = h1;
@@ -3206,6 +3223,18 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         }
         __syncthreads();
         if (!v->released) release_row(c);
+        if ((tid >> 5) == 1) {
+            // the next row's staged values have landed; its history ids into
+            // L2 (up to 256 lines), so the load pass finds them there
+            cp_async_wait_all();
+            __syncwarp();
+            const int nxt = v->next_row;
+            if (P.hist && P.hist_off && nxt < B) {
+                const int64_t a = v->nh[0], b = v->nh[1];
+                const int64_t lines = min((b - a + 31) / 32, (int64_t)256);
+                for (int64_t q = tid & 31; q < lines; q += 32) prefetch_l2_line(P.hist + a + 32 * q);
+            }
+        }
         __syncthreads();
         lrow = v->next_row;
     }
