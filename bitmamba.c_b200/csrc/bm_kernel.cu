@@ -1116,6 +1116,7 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
     // marks them (a bit per element, no branch), a gather lists them, and the
     // histogram, cut and extraction work on that list.
     bool listed = false;
+    bool early = false;  // the row buffer was released right after the listing
     if (c.summary) {
         // The merge kernel listed every tile-list entry with l >= thr.  Each
         // tile's list holds its KS largest values, so it holds every value of
@@ -1249,7 +1250,11 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
                     kc[j++] = ((unsigned long long)(unsigned)(r - sh) << 32) | __float_as_uint(l);
                 }
             }
-            __syncthreads();
+            // the row buffer is no longer read (its barrier orders the list
+            // writes above before the reads below): the next row's copy
+            // starts here, beside the cut and the extraction
+            release_row(c);
+            early = true;
             // histogram of the listed candidates (src/model.c:185-195); the last
             // bucket never decides the cut, so it is not counted
             for (int q = threadIdx.x; q < tot; q += NT) {
@@ -1409,7 +1414,7 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
     }
     // the buffer is no longer needed: the rest works on the candidate list
     // (or re-reads global memory on the rare overflow / guard paths)
-    if (!c.summary) release_row(c);
+    if (!c.summary && !early) release_row(c);
     if (n == 0) {  // argmax guard (src/model.c:227-237)
         const int id = guard_argmax(c);
         write_result(c, id, 1.0f, 2, 0, 0, 0);
