@@ -3367,54 +3367,74 @@ __global__ void __launch_bounds__(NT, MERGE_CTAS_PER_SM) summary_kernel(const Su
                 v->thr = thr;
                 v->sumvk = -nvk;
             }
-            // the listed candidates (l >= thr, src/model.c:185) by the
-            // reference's 128 buckets: the first bucket where their count
-            // reaches top_k lies at or past the row's own cut (the lists hold
-            // a subset of the row), so every candidate the cut or the
-            // extraction can need lies in the buckets up to one past it
+            // the listed candidates (l >= thr, src/model.c:185).  More entries
+            // than the candidate list holds: only those in the reference's
+            // 128 buckets up to one past the first bucket where their count
+            // reaches top_k (it lies at or past the row's own cut: the lists
+            // hold a subset of the row, so every candidate the cut or the
+            // extraction can need lies there)
             uint32_t *hb = reinterpret_cast<uint32_t *>(c.scr);
             const float bscale = __fdiv_rn(127.0f, 20.0f);  // src/model.c:184
-            for (int q = tid; q < HB; q += NT) hb[q] = 0u;
+            const bool all_fit = ne <= KCAP;
+            if (!all_fit)
+                for (int q = tid; q < HB; q += NT) hb[q] = 0u;
             __syncthreads();
             const float thr = v->thr, mxr = v->mx;
             auto bucket_of = [&](float l) {
                 const int b = x86_cvtt(__fmul_rn(__fsub_rn(mxr, l), bscale));
                 return min(max(b, 0), HB - 1);
             };
-            for (int i = tid; i < ne; i += NT) {
-                const unsigned long long e = se[i];
-                if ((unsigned)e == NONE) continue;
-                const float x = __uint_as_float((unsigned)(e >> 32));
-                if (x >= thr) {
-                    const int b = bucket_of(x);
-                    if (b < HB - 1) atomicAdd(&hb[b], 1u);
+            int lim = HB - 1;
+            if (!all_fit) {
+                for (int i = tid; i < ne; i += NT) {
+                    const unsigned long long e = se[i];
+                    if ((unsigned)e == NONE) continue;
+                    const float x = __uint_as_float((unsigned)(e >> 32));
+                    if (x >= thr) {
+                        const int b = bucket_of(x);
+                        if (b < HB - 1) atomicAdd(&hb[b], 1u);
+                    }
                 }
-            }
-            __syncthreads();
-            if (tid < 32) {
-                uint32_t cq[4], ls = 0;
+                __syncthreads();
+                if (tid < 32) {
+                    uint32_t cq[4], ls = 0;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) { cq[q] = hb[4 * tid + q]; ls += cq[q]; }
-                const uint32_t inc = warp_iscan(ls, tid);
-                uint32_t run = inc - ls;
-                int hit = INT_MAX;
+                    for (int q = 0; q < 4; ++q) { cq[q] = hb[4 * tid + q]; ls += cq[q]; }
+                    const uint32_t inc = warp_iscan(ls, tid);
+                    uint32_t run = inc - ls;
+                    int hit = INT_MAX;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    run += cq[q];
-                    if (hit == INT_MAX && run >= (uint32_t)v->k) hit = 4 * tid + q;
+                    for (int q = 0; q < 4; ++q) {
+                        run += cq[q];
+                        if (hit == INT_MAX && run >= (uint32_t)v->k) hit = 4 * tid + q;
+                    }
+                    hit = warp_imin(hit);
+                    if (tid == 0) v->kcut = (hit == INT_MAX) ? HB - 1 : hit;
                 }
-                hit = warp_imin(hit);
-                if (tid == 0) v->kcut = (hit == INT_MAX) ? HB - 1 : hit;
+                __syncthreads();
+                lim = min(v->kcut + 1, HB - 1);
             }
-            __syncthreads();
-            const int lim = min(v->kcut + 1, HB - 1);
-            for (int i = tid; i < ne; i += NT) {
-                const unsigned long long e = se[i];
-                if ((unsigned)e == NONE) continue;
-                const float x = __uint_as_float((unsigned)(e >> 32));
-                if (x >= thr && bucket_of(x) <= lim) {
-                    const int pos = atomicAdd(&v->kcnt, 1);
-                    if (pos < KCAP) kc[pos] = ((unsigned long long)(unsigned)e << 32) | (e >> 32);
+            // the kept entries, one shared atomic a warp
+            const int lane = tid & 31;
+            for (int base = 0; base < ne; base += NT) {
+                const int i = base + tid;
+                bool keep = false;
+                unsigned long long ent = 0ull;
+                if (i < ne) {
+                    const unsigned long long e = se[i];
+                    if ((unsigned)e != NONE) {
+                        const float x = __uint_as_float((unsigned)(e >> 32));
+                        keep = x >= thr && bucket_of(x) <= lim;
+                        ent = ((unsigned long long)(unsigned)e << 32) | (e >> 32);
+                    }
+                }
+                const unsigned m = __ballot_sync(FULL, keep);
+                int pos0 = 0;
+                if (lane == 0 && m) pos0 = atomicAdd(&v->kcnt, __popc(m));
+                pos0 = __shfl_sync(FULL, pos0, 0);
+                if (keep) {
+                    const int pos = pos0 + __popc(m & ((1u << lane) - 1u));
+                    if (pos < KCAP) kc[pos] = ent;
                 }
             }
             __syncthreads();
