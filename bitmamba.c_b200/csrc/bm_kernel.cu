@@ -578,15 +578,15 @@ __device__ __forceinline__ unsigned long long shfl_xor64(unsigned long long v, i
 // ulp(smallest term) below 2^53 of them (e >= 2^-22, p >= 2^-29); returns
 // false (nothing decided) when a value or probability tie, a +inf value or
 // an inexact sum makes the order matter: the block path then decides.
-__device__ __forceinline__ bool warp_tail(const unsigned long long *kc, int n, int k, float top_p,
-                                          float u, int lane, int &res_id, float &res_p,
-                                          int &res_nf) {
+__device__ __forceinline__ bool warp_tail(const unsigned long long *kc, int cnt, int k, float top_p,
+                                          float u, bool cut, float mx, float thr, int lane,
+                                          int &res_id, float &res_p, int &res_nf, int &res_n) {
     unsigned long long key[2];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int x = 2 * lane + r;
         key[r] = ~0ull;
-        if (x < n) {
+        if (x < cnt) {
             const unsigned long long e = kc[x];
             const unsigned b = (unsigned)(e & 0xffffffffu);
             const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -615,13 +615,6 @@ __device__ __forceinline__ bool warp_tail(const unsigned long long *kc, int n, i
             }
         }
     }
-    const int ns = min(n, k), m = min(n, k + 1);
-    // equal values among the first k + 1, or a +inf maximum
-    const unsigned hi0 = (unsigned)(key[0] >> 32), hi1 = (unsigned)(key[1] >> 32);
-    const unsigned nxt = __shfl_down_sync(FULL, hi0, 1);
-    bool tie = (2 * lane + 1 < m && hi0 == hi1) || (2 * lane + 2 < m && hi1 == nxt);
-    if (lane == 0) tie |= (~hi0) == 0xff800000u;
-    if (__any_sync(FULL, tie)) return false;
     float l[2], e[2], p[2];
     int id[2];
 #pragma unroll
@@ -630,6 +623,36 @@ __device__ __forceinline__ bool warp_tail(const unsigned long long *kc, int n, i
         l[r] = __uint_as_float((ord & 0x80000000u) ? (ord ^ 0x80000000u) : ~ord);
         id[r] = (int)(unsigned)(key[r] & 0xffffffffu);
     }
+    int n = cnt;
+    if (cut) {
+        // the candidates' cut and extraction (src/model.c:181-224) on the
+        // sorted list: a bucket grows as the value falls, so the counted
+        // candidates (buckets below the last) are a prefix, the cut bucket
+        // is that of the k-th of them, and the extraction set (l >= ethr) is
+        // a prefix too
+        const float bscale = __fdiv_rn(127.0f, 20.0f);  // src/model.c:184
+        int b[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            b[r] = min(max(x86_cvtt(__fmul_rn(__fsub_rn(mx, l[r]), bscale)), 0), HB - 1);
+        const bool c0 = 2 * lane < cnt && b[0] < HB - 1, c1 = 2 * lane + 1 < cnt && b[1] < HB - 1;
+        const int counted = __popc(__ballot_sync(FULL, c0)) + __popc(__ballot_sync(FULL, c1));
+        const int bk0 = __shfl_sync(FULL, b[0], (k - 1) >> 1), bk1 = __shfl_sync(FULL, b[1], (k - 1) >> 1);
+        const int kcut = (k - 1 < counted) ? (((k - 1) & 1) ? bk1 : bk0) : HB - 1;
+        const float bthr = __fsub_rn(mx, __fdiv_rn((float)(kcut + 1), bscale));  // src/model.c:210-211
+        const float ethr = bthr > thr ? bthr : thr;                                // src/model.c:213-214
+        const bool x0 = 2 * lane < cnt && l[0] >= ethr, x1 = 2 * lane + 1 < cnt && l[1] >= ethr;
+        n = __popc(__ballot_sync(FULL, x0)) + __popc(__ballot_sync(FULL, x1));
+    }
+    res_n = n;
+    if (n == 0) return false;
+    const int ns = min(n, k), m = min(n, k + 1);
+    // equal values among the first k + 1, or a +inf maximum
+    const unsigned hi0 = (unsigned)(key[0] >> 32), hi1 = (unsigned)(key[1] >> 32);
+    const unsigned nxt = __shfl_down_sync(FULL, hi0, 1);
+    bool tie = (2 * lane + 1 < m && hi0 == hi1) || (2 * lane + 2 < m && hi1 == nxt);
+    if (lane == 0) tie |= (~hi0) == 0xff800000u;
+    if (__any_sync(FULL, tie)) return false;
     const float lm = __shfl_sync(FULL, l[0], 0);  // the largest survivor
     double s = 0.0;
     float emin = PINF;
@@ -1255,6 +1278,28 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
             // starts here, beside the cut and the extraction
             release_row(c);
             early = true;
+            if (tot <= 64 && v->top_p < 1.0f) {
+                // few candidates: cut, extraction and the end of the row on
+                // one warp (the block path below when the warp cannot decide)
+                if (warp == 0) {
+                    int rid = 0, rnf = 0, rn = 0;
+                    float rp = 0.0f;
+                    const bool ok = warp_tail(kc, tot, k, v->top_p, v->u, true, mx, thr, lane, rid,
+                                              rp, rnf, rn);
+                    if (lane == 0) {
+                        v->wt = ok ? 1 : 0;
+                        v->res_id = rid;
+                        v->res_p = rp;
+                        v->n_final = rnf;
+                        v->kcnt = rn;
+                    }
+                }
+                __syncthreads();
+                if (v->wt) {
+                    write_result(c, v->res_id, v->res_p, 3, v->kcnt, v->n_final, 1);
+                    return;
+                }
+            }
             // histogram of the listed candidates (src/model.c:185-195); the last
             // bucket never decides the cut, so it is not counted
             for (int q = threadIdx.x; q < tot; q += NT) {
@@ -1425,7 +1470,9 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
         if (warp == 0) {
             int rid = 0, rnf = 0;
             float rp = 0.0f;
-            const bool ok = warp_tail(kc, n, k, v->top_p, v->u, lane, rid, rp, rnf);
+            int rn = 0;
+            const bool ok = warp_tail(kc, n, k, v->top_p, v->u, false, 0.0f, 0.0f, lane, rid, rp,
+                                      rnf, rn);
             if (lane == 0) {
                 v->wt = ok ? 1 : 0;
                 v->res_id = rid;
