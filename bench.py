@@ -37,10 +37,10 @@ RNG_SEED = 42
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per row of the c3 workload, from one ncu capture
 # of sample_kernel on B = 1024 rows (dram__bytes_read.sum 206.01 MB +
-# dram__bytes_write.sum 5.13 MB, profiles/sample_kernel_c3.md); traffic grows
+# dram__bytes_write.sum 4.32 MB, profiles/sample_kernel_c3.md); traffic grows
 # with the rows processed (each row is read once), so a launch of B rows moves
 # about B times this.
-DRAM_BYTES_PER_ROW_C3 = (206.013184e6 + 5.125632e6) / 1024
+DRAM_BYTES_PER_ROW_C3 = (206.067968e6 + 4.322304e6) / 1024
 
 
 def workload_config(B, V):
