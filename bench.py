@@ -36,7 +36,7 @@ KNOBS = dict(temp=1.0, penalty=1.0, min_p=0.0, top_p=0.95, top_k=0)
 RNG_SEED = 42
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per row of the c3 workload, from one ncu capture
-# of sample_kernel on B = 1024 rows (dram__bytes_read.sum 206.01 MB +
+# of sample_kernel on B = 1024 rows (dram__bytes_read.sum 206.07 MB +
 # dram__bytes_write.sum 4.32 MB, profiles/sample_kernel_c3.md); traffic grows
 # with the rows processed (each row is read once), so a launch of B rows moves
 # about B times this.
