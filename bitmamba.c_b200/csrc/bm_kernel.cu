@@ -3213,9 +3213,11 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             if (scale) load_pass<false, false, true>(c, P.hist, mx, xmin, chk, gv, gi);
             else load_pass<false, false, false>(c, P.hist, mx, xmin, chk, gv, gi);
         }
-        // a plain barrier, then the flag from shared memory (measured faster
-        // here than a barrier reduction of the flag)
-        __syncthreads();
+        // the block reductions (their barriers also make a failed wait's flag
+        // visible to every thread)
+        const float lmx = mx;
+        if (greedy) block_argmax(gv, gi, c.red);
+        else block_maxmin_chk(mx, xmin, chk, c.red);
         if (v->fail) {
             // a bounded wait expired: wait (bounded) for this row's copies,
             // then stop; the host sees the error flag
@@ -3231,12 +3233,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             break;
         }
         if (greedy) {
-            block_argmax(gv, gi, c.red);
             release_row(c);
             write_result(c, gi == INT_MAX ? 0 : gi, 1.0f, 1, 0, 0, 0);
         } else {
-            const float lmx = mx;
-            block_maxmin_chk(mx, xmin, chk, c.red);
             if (lmx == mx && gi != INT_MAX) {
                 // this thread saw the maximum in slot gi: its index
                 const float4 x = reinterpret_cast<const float4 *>(c.row)[gi];
@@ -3250,21 +3249,24 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
                 }
                 if (idx != INT_MAX) atomicMin(&v->amax, idx);
             }
-            if (tid == 0) {
-                v->mx = mx;
-                v->xmin = xmin;
+            {
+                // every thread derives the row's values and writes them (the
+                // same values) before it reads them: no barrier needed here
                 // src/model.c:169-173 (logf from the host)
                 float thr = -1e30f;
                 if (v->min_p >= 1.0f) thr = mx;
                 else if (v->min_p > 0.0f) thr = __fadd_rn(mx, v->log_min_p);
-                v->thr = thr;
                 // every logit finite and a candidate: the streaming passes
                 // need no candidate test
-                v->clean = (chk == 0.0f) && (xmin >= thr) && (fabsf(mx) < 1e30f) &&
-                           (v->inv_temp >= 1e-6f);
-                v->k = (v->top_k > 0 && v->top_k <= 256) ? v->top_k : 0;  // src/model.c:175
+                const int clean = (chk == 0.0f) && (xmin >= thr) && (fabsf(mx) < 1e30f) &&
+                                  (v->inv_temp >= 1e-6f);
+                const int kk = (v->top_k > 0 && v->top_k <= 256) ? v->top_k : 0;  // src/model.c:175
+                v->mx = mx;
+                v->xmin = xmin;
+                v->thr = thr;
+                v->clean = clean;
+                v->k = kk;
             }
-            __syncthreads();
             if (v->k > 0) {
                 if (scale) topk_path<true>(c, lmx);
                 else topk_path<false>(c, lmx);
