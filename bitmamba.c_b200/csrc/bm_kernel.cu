@@ -76,6 +76,7 @@ struct __align__(16) Vars {
     int64_t nh[2];    // the next row's history offsets, knobs and uniform,
     bm_knobs_t nk;    // copied in asynchronously at the release
     float nu;
+    int nclaim;       // the row claimed to follow the next one
     double mc, ec, mk, ek, md;
     double adj[3];    // per target: mass of the band elements above its buckets
     double lbm[3];    // per target: mass of the listed elements in front of its range
@@ -769,6 +770,7 @@ struct Ctx {
     bm_row_stats_t *stats;
     int rowid;
     int claim;  // thread 0: the row claimed to follow this one
+    int succ;   // thread 32 + 1: the row claimed at the release to follow that one
     int mark;   // failed rows get id -1 (the allocation-free entry point)
     int summary;  // the merge kernel: candidates come from per-tile lists
     const int32_t *row_map;  // launch row -> row of the per-row arrays (or NULL)
@@ -854,6 +856,8 @@ __device__ __forceinline__ void release_row(Ctx &c) {
                     cp_async4(reinterpret_cast<uint32_t *>(v->nh) + (lane - 17),
                               reinterpret_cast<const uint32_t *>(v->p_hist_off + nr) + (lane - 17));
                 if (lane >= 8 && lane < 21) cp_async_commit();
+                // the row to follow the next one (published at this row's end)
+                if (lane == 1) c.succ = (int)gridDim.x + atomicAdd(c.sched, 1);
                 // warm L2 with the row claimed about one round later
                 const int pre = next_row + (int)gridDim.x;
                 if (lane == 0 && pre < c.B)
@@ -3154,10 +3158,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
         if (tid == 0) {
             // dynamic schedule: the first gridDim.x rows go one per CTA, every
             // later row to the CTA that asks first (rows of unequal cost would
-            // otherwise leave SMs idle at the end of the launch); claimed now
-            // (the result is first read when this row's buffer is released),
-            // its copy is issued at the release
-            c.claim = (int)gridDim.x + atomicAdd(&P.sched[0], 1);
+            // otherwise leave SMs idle at the end of the launch).  The row to
+            // follow this one was claimed at the last release (the first row:
+            // claimed now); its copy is issued at this row's release
+            c.claim = (it == 0) ? (int)gridDim.x + atomicAdd(&P.sched[0], 1) : v->nclaim;
             const int sh = (int)(((uintptr_t)c.g & 15u) >> 2);
             int i0 = sh ? 4 - sh : 0;
             if (i0 > V) i0 = V;
@@ -3281,6 +3285,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
             // the next row's staged values have landed; its history ids into
             // L2 (up to 256 lines), so the load pass finds them there
             cp_async_wait_all();
+            if (tid == 33) v->nclaim = c.succ;
             __syncwarp();
             const int nxt = v->next_row;
             if (P.hist && P.hist_off && nxt < B) {
