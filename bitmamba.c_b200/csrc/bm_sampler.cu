@@ -623,23 +623,24 @@ constexpr size_t STAGE_MAX = size_t(16) << 20;
 constexpr size_t r16h(size_t x) { return (x + 15) & ~size_t(15); }
 
 // Byte offsets of the staging region's sections (16-byte aligned):
-// [words 16 B | ids | probabilities | stats | logits | knobs | uniforms |
-//  history ids | history offsets]; `o_in` is where the inputs start.
+// [logits | knobs | uniforms | history ids | history offsets | words 16 B |
+//  ids | probabilities | stats].  The upload is [0, o_w + 16): the inputs and
+// the zeroed words; the read-back is [o_w, total): the words and the outputs.
 struct StageLayout {
-    size_t o_id, o_prob, o_st, o_in, o_log, o_kn, o_u, o_h, o_off, total;
+    size_t o_log, o_kn, o_u, o_h, o_off, o_w, o_id, o_prob, o_st, total;
 };
 StageLayout stage_layout(size_t rows, int64_t ld, size_t nk, int64_t h1, bool hist) {
     StageLayout L;
-    L.o_id = 16;
-    L.o_prob = L.o_id + r16h(rows * sizeof(int32_t));
-    L.o_st = L.o_prob + r16h(rows * sizeof(float));
-    L.o_in = L.o_st + r16h(rows * sizeof(bm_row_stats_t));
-    L.o_log = L.o_in;
+    L.o_log = 0;
     L.o_kn = L.o_log + r16h(rows * (size_t)ld * sizeof(float));
     L.o_u = L.o_kn + r16h(nk * sizeof(bm_knobs_t));
     L.o_h = L.o_u + r16h(rows * sizeof(float));
     L.o_off = L.o_h + (hist ? r16h((size_t)h1 * sizeof(int32_t)) : 0);
-    L.total = L.o_off + (hist ? r16h((rows + 1) * sizeof(int64_t)) : 0);
+    L.o_w = L.o_off + (hist ? r16h((rows + 1) * sizeof(int64_t)) : 0);
+    L.o_id = L.o_w + 16;
+    L.o_prob = L.o_id + r16h(rows * sizeof(int32_t));
+    L.o_st = L.o_prob + r16h(rows * sizeof(float));
+    L.total = L.o_st + r16h(rows * sizeof(bm_row_stats_t));
     return L;
 }
 
@@ -649,7 +650,7 @@ int sample_host_small(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t 
                       int32_t *h_out_id, float *h_out_prob, bm_row_stats_t *h_stats,
                       size_t nk, int64_t h1, const StageLayout &L) {
     const size_t rows = (size_t)B;
-    const size_t o_id = L.o_id, o_prob = L.o_prob, o_st = L.o_st, o_in = L.o_in;
+    const size_t o_id = L.o_id, o_prob = L.o_prob, o_st = L.o_st, o_w = L.o_w;
     const size_t o_log = L.o_log, o_kn = L.o_kn, o_u = L.o_u, o_h = L.o_h, o_off = L.o_off;
     const size_t total = L.total;
     cudaStream_t s = c->stream;
@@ -669,7 +670,7 @@ int sample_host_small(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t 
     }
     // (every call leaves the stream idle, so no copy still reads the region)
     unsigned char *h = c->h_stage, *d = c->d_stage;
-    memset(h, 0, 16);  // error word and the two row-schedule counters
+    memset(h + o_w, 0, 16);  // error word and the two row-schedule counters
     memcpy(h + o_log, h_logits, rows * (size_t)ld * sizeof(float));
     memcpy(h + o_kn, h_knobs, nk * sizeof(bm_knobs_t));
     memcpy(h + o_u, h_uniform, rows * sizeof(float));
@@ -677,7 +678,7 @@ int sample_host_small(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t 
         if (h1 > 0) memcpy(h + o_h, h_hist, (size_t)h1 * sizeof(int32_t));
         memcpy(h + o_off, h_hist_off, (rows + 1) * sizeof(int64_t));
     }
-    CK(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(d, h, o_w + 16, cudaMemcpyHostToDevice, s));
     bmk::Params p;
     p.logits = reinterpret_cast<const float *>(d + o_log);
     p.ld = ld;
@@ -691,17 +692,17 @@ int sample_host_small(bm_ctx_t *c, const float *h_logits, int B, int V, int64_t 
     p.out_id = reinterpret_cast<int32_t *>(d + o_id);
     p.out_prob = h_out_prob ? reinterpret_cast<float *>(d + o_prob) : nullptr;
     p.stats = h_stats ? reinterpret_cast<bm_row_stats_t *>(d + o_st) : nullptr;
-    p.err = reinterpret_cast<int *>(d);
-    p.sched = reinterpret_cast<int *>(d) + 1;
+    p.err = reinterpret_cast<int *>(d + o_w);
+    p.sched = reinterpret_cast<int *>(d + o_w) + 1;
     const int grid = B < c->sms ? B : c->sms;
     cudaError_t e = bmk::launch(p, grid, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(h, d, o_in, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h + o_w, d + o_w, total - o_w, cudaMemcpyDeviceToHost, s);
     // synchronise on the failure path too: the upload may still read the region
     const cudaError_t es = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "small host-buffer call");
     if (es != cudaSuccess) return cuda_fail(es, "cudaStreamSynchronize");
     int err = 0;
-    memcpy(&err, h, sizeof(int));
+    memcpy(&err, h + o_w, sizeof(int));
     if (err)
         return fail(BM_ERR_DEVICE, "device error flag 0x%x (bounded wait expired or select "
                                    "did not converge)", err);
