@@ -1101,6 +1101,95 @@ __device__ __noinline__ int guard_argmax(Ctx c) {
     return bi;
 }
 
+// The candidates (l >= thr) of a row with a real min_p threshold, listed in
+// kc as (id << 32) | bits(l) when they are at most KCAP; returns their count.
+// Each thread marks its candidates, a bit per element, in registers.  A
+// thread whose own maximum in the load pass (tmax: the same scaled values of
+// the same interior slots) lies below thr has none there and skips its
+// slots; the ragged head / tail slots were consumed by other threads in the
+// load pass, so their threads here always scan.  The count's block scan
+// ends the mask reads; the caller's next barrier orders the list writes.
+template <bool SCALE>
+__device__ __forceinline__ int list_candidates(Ctx &c, float tmax, unsigned long long *kc) {
+    const int lane = threadIdx.x & 31;
+    Vars *v = c.v;
+    const int sh = v->sh, nslots = v->nslots;
+    const float thr = v->thr, inv_temp = v->inv_temp;
+    const float4 *r4 = reinterpret_cast<const float4 *>(c.row);
+    bool edge = (int)threadIdx.x < v->s_int0;
+    for (int s = v->s_int1; s < nslots; ++s) edge |= (s % NT) == (int)threadIdx.x;
+    const bool need = edge || !(tmax < thr);
+    // candidate bits of slot s: bit q for element q of the slot
+    auto bits4 = [&](int s) -> uint32_t {
+        const float4 x = r4[s];
+        const float t[4] = {x.x, x.y, x.z, x.w};
+        uint32_t b4 = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
+            b4 |= (l >= thr ? 1u : 0u) << q;
+        }
+        return b4;
+    };
+    uint32_t wv[MASKW] = {0u, 0u, 0u, 0u};
+    const uint32_t scanners = __ballot_sync(FULL, need);
+    if (__popc(scanners) <= 8) {
+        // few threads of this warp have candidates: the whole warp scans
+        // each one's slots (lane i takes its slot i), and groups of 8
+        // lanes assemble its mask words (word q = slots 8q..8q+7)
+        for (uint32_t m = scanners; m; m &= m - 1) {
+            const int ln = __ffs(m) - 1;
+            const int s = (int)(threadIdx.x & ~31u) + ln + lane * NT;
+            uint32_t w = (s < nslots) ? bits4(s) << (4 * (lane & 7)) : 0u;
+            w |= __shfl_xor_sync(FULL, w, 1);
+            w |= __shfl_xor_sync(FULL, w, 2);
+            w |= __shfl_xor_sync(FULL, w, 4);
+#pragma unroll
+            for (int q = 0; q < MASKW; ++q) {
+                const uint32_t wq = __shfl_sync(FULL, w, 8 * q);
+                if (lane == ln) wv[q] = wq;
+            }
+        }
+    } else if (need) {
+        uint32_t w = 0;
+        int i = 0;
+        for (int s = threadIdx.x; s < nslots; s += NT, ++i) {
+            w |= bits4(s) << (4 * (i & 7));
+            if ((i & 7) == 7) {
+#pragma unroll
+                for (int q = 0; q < MASKW; ++q)
+                    if (q == (i >> 3)) wv[q] = w;
+                w = 0;
+            }
+        }
+        if (i & 7) {
+#pragma unroll
+            for (int q = 0; q < MASKW; ++q)
+                if (q == (i >> 3)) wv[q] = w;
+        }
+    }
+    int nb = 0;
+#pragma unroll
+    for (int q = 0; q < MASKW; ++q) nb += __popc(wv[q]);
+    int tot;
+    int j = block_xscan_i(nb, tot, c.red);
+    if (tot <= KCAP) {
+#pragma unroll
+        for (int q = 0; q < MASKW; ++q) {
+            uint32_t m = wv[q];
+            while (m) {
+                const int bp = __ffs(m) - 1;
+                m &= m - 1;
+                const int s = threadIdx.x + (8 * q + (bp >> 2)) * NT;
+                const int r = min(4 * s + (bp & 3), 4 * nslots - 1);
+                const float l = SCALE ? __fmul_rn(c.row[r], inv_temp) : c.row[r];
+                kc[j++] = ((unsigned long long)(unsigned)(r - sh) << 32) | __float_as_uint(l);
+            }
+        }
+    }
+    return tot;
+}
+
 // ---------------------------------------------------------------- top_k --
 template <bool SCALE>
 __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
@@ -1199,84 +1288,11 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
         if (threadIdx.x == 0) v->kcnt = n2;
         __syncthreads();
     } else if (v->min_p > 0.0f) {
-        // Each thread marks its candidates, a bit per element, in registers.
-        // A thread whose own maximum in the load pass (tmax: the same scaled
-        // values of the same interior slots) lies below thr has none there
-        // and skips its slots; the ragged head / tail slots were consumed by
-        // other threads in the load pass, so their threads here always scan.
-        bool edge = (int)threadIdx.x < v->s_int0;
-        for (int s = v->s_int1; s < nslots; ++s) edge |= (s % NT) == (int)threadIdx.x;
-        const bool need = edge || !(tmax < thr);
-        // candidate bits of slot s: bit q for element q of the slot
-        auto bits4 = [&](int s) -> uint32_t {
-            const float4 x = r4[s];
-            const float t[4] = {x.x, x.y, x.z, x.w};
-            uint32_t b4 = 0;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float l = SCALE ? __fmul_rn(t[q], inv_temp) : t[q];
-                b4 |= (l >= thr ? 1u : 0u) << q;
-            }
-            return b4;
-        };
-        uint32_t wv[MASKW] = {0u, 0u, 0u, 0u};
-        const uint32_t scanners = __ballot_sync(FULL, need);
-        if (__popc(scanners) <= 8) {
-            // few threads of this warp have candidates: the whole warp scans
-            // each one's slots (lane i takes its slot i), and groups of 8
-            // lanes assemble its mask words (word q = slots 8q..8q+7)
-            for (uint32_t m = scanners; m; m &= m - 1) {
-                const int ln = __ffs(m) - 1;
-                const int s = (int)(threadIdx.x & ~31u) + ln + lane * NT;
-                uint32_t w = (s < nslots) ? bits4(s) << (4 * (lane & 7)) : 0u;
-                w |= __shfl_xor_sync(FULL, w, 1);
-                w |= __shfl_xor_sync(FULL, w, 2);
-                w |= __shfl_xor_sync(FULL, w, 4);
-#pragma unroll
-                for (int q = 0; q < MASKW; ++q) {
-                    const uint32_t wq = __shfl_sync(FULL, w, 8 * q);
-                    if (lane == ln) wv[q] = wq;
-                }
-            }
-        } else if (need) {
-            uint32_t w = 0;
-            int i = 0;
-            for (int s = threadIdx.x; s < nslots; s += NT, ++i) {
-                w |= bits4(s) << (4 * (i & 7));
-                if ((i & 7) == 7) {
-#pragma unroll
-                    for (int q = 0; q < MASKW; ++q)
-                        if (q == (i >> 3)) wv[q] = w;
-                    w = 0;
-                }
-            }
-            if (i & 7) {
-#pragma unroll
-                for (int q = 0; q < MASKW; ++q)
-                    if (q == (i >> 3)) wv[q] = w;
-            }
-        }
-        int nb = 0;
-#pragma unroll
-        for (int q = 0; q < MASKW; ++q) nb += __popc(wv[q]);
-        int tot;
-        int j = block_xscan_i(nb, tot, c.red);
+        const int tot = list_candidates<SCALE>(c, tmax, kc);
         if (tot <= KCAP) {
             listed = true;
             for (int q = 0; q < 8 * HB; q += NT)
                 if (q + (int)threadIdx.x < 8 * HB) kh[q + threadIdx.x] = 0;
-#pragma unroll
-            for (int q = 0; q < MASKW; ++q) {
-                uint32_t m = wv[q];
-                while (m) {
-                    const int bp = __ffs(m) - 1;
-                    m &= m - 1;
-                    const int s = threadIdx.x + (8 * q + (bp >> 2)) * NT;
-                    const int r = min(4 * s + (bp & 3), 4 * nslots - 1);
-                    const float l = SCALE ? __fmul_rn(c.row[r], inv_temp) : c.row[r];
-                    kc[j++] = ((unsigned long long)(unsigned)(r - sh) << 32) | __float_as_uint(l);
-                }
-            }
             // the row buffer is no longer read (its barrier orders the list
             // writes above before the reads below): the next row's copy
             // starts here, beside the cut and the extraction
@@ -2474,8 +2490,36 @@ __device__ __forceinline__ void pwin_of(int b0, int b1, float w, float inv_sum, 
     plo = __fmul_rn(exp_one(-((float)b1 + 0.5f) * w), inv_sum);
 }
 
+// A full-path row's candidates when they are at most 64 (listed into the
+// scratch area), finished on one warp; returns their count when the warp
+// decided the row (v->res_id, v->res_p, v->n_final), else 0.  Out of line:
+// the rows of the bucket path run none of it.
 template <bool SCALE>
-__device__ __forceinline__ void full_path(Ctx &c) {
+__device__ __noinline__ int few_candidates(Ctx c, float tmax) {
+    c.attach();
+    Vars *v = c.v;
+    unsigned long long *kl = reinterpret_cast<unsigned long long *>(c.scr + 4096);
+    const int tot = list_candidates<SCALE>(c, tmax, kl);
+    __syncthreads();  // the list writes (the buckets of the caller reuse the area)
+    if (tot > 64) return 0;
+    if (threadIdx.x < 32) {
+        int rid = 0, rnf = 0, rn = 0;
+        float rp = 0.0f;
+        const bool ok = warp_tail(kl, tot, tot, v->top_p, v->u, false, v->mx, v->thr,
+                                  (int)threadIdx.x, rid, rp, rnf, rn);
+        if (threadIdx.x == 0) {
+            v->wt = ok ? 1 : 0;
+            v->res_id = rid;
+            v->res_p = rp;
+            v->n_final = rnf;
+        }
+    }
+    __syncthreads();
+    return v->wt ? tot : 0;
+}
+
+template <bool SCALE>
+__device__ __forceinline__ void full_path(Ctx &c, float tmax) {
     Vars *v = c.v;
     const int sh = v->sh, nslots = v->nslots;
     const float mx = v->mx, thr = v->thr;
@@ -2497,6 +2541,21 @@ __device__ __forceinline__ void full_path(Ctx &c) {
         const bool lazy = (top_p >= 1.0f) && (top_k <= 0 || top_k >= cnt);
         write_result(c, last, __int_as_float(0x7fc00000), lazy ? 5 : 7, cnt, cnt, 1);
         return;
+    }
+    // A real min_p threshold usually leaves few candidates: they are listed
+    // as on the top_k path and, up to 64 of them, finish the row on one warp.
+    // The reference's softmax over them and its stable sort by probability
+    // (src/model.c:306-313, 359-360) list them in value order when no two
+    // values or probabilities are equal; otherwise the warp leaves the row
+    // undecided and the bucket path below takes it (the row is still
+    // resident).  Rows where more than 64 threads hold a candidate skip it.
+    if (!v->clean && v->min_p > 0.0f && top_p < 1.0f && __syncthreads_count(!(tmax < thr)) <= 64) {
+        const int tot = few_candidates<SCALE>(c, tmax);
+        if (tot > 0) {
+            release_row(c);
+            write_result(c, v->res_id, v->res_p, 7, tot, v->n_final, 1);  // src/model.c:359-360
+            return;
+        }
     }
     // bucket geometry over d = max - l
     float dmax = __fsub_rn(mx, v->xmin);
@@ -3275,8 +3334,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params P) {
                 if (scale) topk_path<true>(c, lmx);
                 else topk_path<false>(c, lmx);
             } else {
-                if (scale) full_path<true>(c);
-                else full_path<false>(c);
+                if (scale) full_path<true>(c, lmx);
+                else full_path<false>(c, lmx);
             }
         }
         __syncthreads();

@@ -97,6 +97,27 @@ def test_min_p_scaled_rows(gpu_ctx, sampler_lib, oracle_lib):
     _run(gpu_ctx, sampler_lib, oracle_lib, b, u, "min_p")
 
 
+def test_few_min_p_candidates(gpu_ctx, sampler_lib, oracle_lib):
+    """top_k 0 with a real min_p: about 10 to 200 candidates a row, so the
+    rows of up to 64 finish on one warp and the others take the bucket path;
+    rows with a tied maximum or quantised values leave the warp undecided."""
+    B = 64
+    z = (2.0 * synth.normal(10, 1, B * V)).reshape(B, V).astype(np.float32)
+    r = np.arange(B)
+    temp = np.where(r % 3 == 0, 0.5, np.where(r % 3 == 1, 0.7, 1.0)).astype(np.float32)
+    min_p = np.where(r % 2 == 0, 0.05, 0.2).astype(np.float32)
+    top_p = np.where(r % 5 == 0, 0.5, 0.9).astype(np.float32)
+    for i in range(B):
+        if i % 4 == 1:    # the maximum twice
+            z[i, 1234] = z[i].max()
+        elif i % 4 == 2:  # quantised values: ties among the candidates
+            z[i] = np.round(4.0 * z[i]) / 4.0
+    b = synth.Batch(z, np.zeros(0, np.int32), np.zeros(B + 1, np.int64), temp,
+                    np.ones(B, np.float32), min_p, top_p, np.zeros(B, np.int32))
+    u = synth.uniform(10, 2, B).astype(np.float32)
+    _run(gpu_ctx, sampler_lib, oracle_lib, b, u, "few min_p candidates")
+
+
 @pytest.mark.parametrize("name,rows", [("c3", 1024), ("c4", 1024)])
 def test_large_batches(gpu_ctx, sampler_lib, oracle_lib, name, rows):
     b = synth.MAKERS[name](303, rows)
