@@ -594,9 +594,14 @@ __device__ __forceinline__ bool warp_tail(const unsigned long long *kc, int cnt,
             key[r] = ((unsigned long long)(~ord) << 32) | (unsigned)(e >> 32);
         }
     }
-    // ascending bitonic sort of the 64 keys (padding ~0 sorts last)
+    // ascending bitonic sort of the 64 keys (padding ~0 sorts last).  Only
+    // the first `lim` (a power of two >= cnt) hold keys: the network's
+    // stages up to that size sort them, and the padding behind them is
+    // already in order.
+    const int lim = (cnt <= 2) ? 2 : 1 << (32 - __clz(cnt - 1));
 #pragma unroll
     for (int size = 2; size <= 64; size <<= 1) {
+        if (size > lim) break;
 #pragma unroll
         for (int j = size >> 1; j > 0; j >>= 1) {
             unsigned long long o[2];
@@ -823,9 +828,11 @@ __device__ __forceinline__ void prefetch_row(const float *g, int V) {
 }
 
 // The row buffer is no longer read for this row: let the next row's copy in.
-// Warp 0 issues the copies (one lane per chunk); warp 1 the prefetches, so
-// the two sets of instructions do not run one after the other.
-__device__ __forceinline__ void release_row(Ctx &c) {
+// Warp `cw` issues the copies (one lane per chunk); warp 1 the prefetches,
+// so the two sets of instructions do not run one after the other.  The top_k
+// path passes cw = 2: its warp 0 finishes short lists right after the
+// release.
+__device__ __forceinline__ void release_row(Ctx &c, int cw = 0) {
     if (threadIdx.x == 0) {
         // the row claimed when this one started (thread 0 holds it)
         c.v->released = 1;
@@ -834,11 +841,11 @@ __device__ __forceinline__ void release_row(Ctx &c) {
     fence_proxy_async();
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < 2) {
+    if (warp == 1 || warp == cw) {
         const int next_row = c.v->next_row;
         if (next_row < c.B) {
             const int nr = c.row_map ? (int)c.row_map[next_row] : next_row;
-            if (warp == 0) {
+            if (warp == cw) {
                 if (lane < NCHUNK)
                     issue_chunk(c.logits + (int64_t)nr * c.ld, c.V, c.mbar, c.row, lane);
             } else {
@@ -1296,7 +1303,7 @@ __device__ __forceinline__ void topk_path(Ctx &c, float tmax) {
             // the row buffer is no longer read (its barrier orders the list
             // writes above before the reads below): the next row's copy
             // starts here, beside the cut and the extraction
-            release_row(c);
+            release_row(c, 2);
             early = true;
             if (tot <= 64 && v->top_p < 1.0f) {
                 // few candidates: cut, extraction and the end of the row on
