@@ -12,26 +12,33 @@
 //             bitset; src/model.c:1277-1304); the pass then reduces max / min
 //             of the scaled logits
 //             (src/model.c:156-163) or the greedy argmax (src/model.c:144-154).
-//   top_k     1 <= top_k <= 256: the reference's 128-bucket histogram cut
-//             (src/model.c:181-214) with the candidates above the min_p
-//             threshold collected in the same pass, exact emulation of its
+//   top_k     1 <= top_k <= 256: with a real min_p threshold the candidates
+//             are listed first (threads whose own maximum lies below it skip
+//             their slots); up to 64 in value order finish on one warp: a
+//             bitonic sort of the occupied part of the list, the reference's
+//             128-bucket cut and extraction (src/model.c:181-224) as prefixes
+//             of it, survivor softmax, nucleus cut and draw.  Otherwise the
+//             128-bucket histogram cut, exact emulation of the reference's
 //             min-heap (the heap layout decides the CDF walk order), survivor
 //             softmax, stable descending sort, nucleus cut and draw.
-//   full      other top_k: a bucket-count histogram over d = max - l (one
-//             shared atomic per candidate), then either the id-order walk
-//             (src/model.c:319-320) or, for the sorted order, windows of one
-//             or two buckets around the estimated nucleus cut, top_k position
-//             and draw; one exact pass computes exp(l - max), its fp64 sum,
-//             the exact mass above each window and lists the window elements;
-//             the list is sorted in (probability desc, id asc) order -- the
-//             order the reference's stable qsort produces -- and every target
-//             is resolved block-parallel over it.  Rows where the reference's
-//             top-256 heap path applies and ties make its layout visible are
-//             replayed exactly (src/model.c:327-356); a target that falls
-//             outside its window takes exact passes over global memory.
-//   schedule  the first gridDim.x rows go one per CTA, every later row to the
-//             CTA that frees its row buffer first (atomic counter, rewound by
-//             the last CTA to finish).
+//   full      other top_k: rows with a real min_p threshold and at most 64
+//             candidates take the same one-warp end without the cut.  Else a
+//             bucket-mass histogram over d = max - l (one shared atomic per
+//             candidate adds its fixed-point e-mass), then either the id-order
+//             walk (src/model.c:319-320) or, for the sorted order, windows of
+//             buckets around the nucleus cut, the top_k position and the
+//             draw: a membership pass flags the window elements, a gather
+//             lists them with exact probabilities, and order statistics over
+//             the list in (probability desc, id asc) order -- the order the
+//             reference's stable sort produces -- resolve every target
+//             block-parallel.  Rows where the reference's top-256 heap path
+//             applies and ties make its layout visible are replayed exactly
+//             (src/model.c:327-356); a target that falls outside its window
+//             takes exact passes over global memory.
+//   schedule  the first gridDim.x rows go one per CTA; at each release a CTA
+//             claims the row after the one whose copy it issues there (atomic
+//             counter, rewound by the last CTA to finish), so rows of unequal
+//             cost keep every SM busy to the end of the launch.
 //
 // Arithmetic that decides ids uses the reference's fp32 operations (no
 // contraction: explicit __fmul_rn/__fadd_rn/__fdiv_rn; the library is built
@@ -834,7 +841,7 @@ __device__ __forceinline__ void prefetch_row(const float *g, int V) {
 // release.
 __device__ __forceinline__ void release_row(Ctx &c, int cw = 0) {
     if (threadIdx.x == 0) {
-        // the row claimed when this one started (thread 0 holds it)
+        // the row claimed to follow this one (thread 0 holds it)
         c.v->released = 1;
         c.v->next_row = c.claim;
     }
